@@ -1,0 +1,161 @@
+/*
+ * b200q -- B200-native (sm_100a) int8 / quantized-int32 NHWC convolution and
+ * batched GEMM behind a plain C ABI.
+ *
+ * Every entry point takes device pointers, plain sizes and a CUDA stream passed
+ * as `void*` (a cudaStream_t; NULL = legacy default stream), returns an int
+ * status (B200Q_OK on success) and never throws.  The message of the last
+ * failure on the calling thread is returned by b200q_last_error().
+ * Launches are asynchronous on `stream` unless stated otherwise.
+ *
+ * Drop-in mapping (reference = NikitaYak02/my_own_cnn):
+ *   b200q_fprop_nhwc_qi32        replaces conv_quant_detail::launch_fprop_nhwc_qi32_{u8,s5}
+ *                                (src/conv_types.h:232-241, src/cuda_kernels.cu:1336-1392,1465-1481)
+ *   b200q_block_fprop_nhwc_qi32  replaces conv_quant_detail::launch_block_fprop_nhwc_qi32_{u8,s5}
+ *                                (src/conv_types.h:242-251, src/cuda_kernels.cu:1394-1461,1483-1497)
+ *   b200q_bmm_matmul_i32         replaces bmm_matmul_i32 (bmm.h:69-74, bmm.cu:298-322)
+ * New entry points (int8 storage, fused requantization; no reference counterpart):
+ *   b200q_conv2d_s8, b200q_bmm_s8.
+ * The C++ shim my_own_cnn_b200/shim/reference_shim.cpp defines the reference's
+ * own symbols on top of these, so reference callers link unchanged.
+ */
+#ifndef B200Q_H_
+#define B200Q_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ---- */
+enum b200q_status {
+  B200Q_OK = 0,
+  B200Q_ERR_INVALID_ARG = 1,  /* bad shape / pointer / parameter (the reference throws here) */
+  B200Q_ERR_UNSUPPORTED = 2,  /* valid request this build cannot run */
+  B200Q_ERR_CUDA = 3,         /* a CUDA runtime / driver call failed */
+  B200Q_ERR_TIMEOUT = 4       /* a device-side wait ran out; the kernel returned early */
+};
+
+/* ---- quantized input types: same values as nnalgebra::DataType (src/nnalgebra_quantization.h:19-24) ---- */
+enum b200q_qtype { B200Q_LINQUANT_U8 = 1, B200Q_LINQUANT_S5 = 2 };
+
+/* Same layout as Conv2DParams (src/conv_types.h:21-29). */
+typedef struct b200q_conv_params {
+  int pad_h, pad_w, stride_h, stride_w, dilation_h, dilation_w, groups;
+} b200q_conv_params;
+
+/* Same layouts as QuantizationParameters<LinQuantU8/LinQuantS5>
+ * (src/nnalgebra_quantization.h:29-41).  Only zero_point is read. */
+typedef struct b200q_qparams_u8 {
+  uint8_t zero_point;
+  float scale;
+  uint8_t symmetric; /* C++ bool */
+} b200q_qparams_u8;
+typedef struct b200q_qparams_s5 {
+  int8_t zero_point;
+  uint8_t n_bins;
+  float scale;
+} b200q_qparams_s5;
+
+/* ---- output epilogue of the int8 entry points ----
+ * out_kind B200Q_OUT_S32 : y[m][k] = acc + bias[k]                       (int32, wrapping; bias may be NULL)
+ * out_kind B200Q_OUT_S8  : t = acc + bias[k] (int32 wrap); p = (float)t * scale[k] (fp32, RNE);
+ *                          q = rint(clamp(p, clamp_lo - zp_out, clamp_hi - zp_out)) + zp_out  (half to even);
+ *                          stored as int8.  ReLU = clamp_lo = zp_out; ReLU6 = clamp_hi = q6.
+ * out_kind B200Q_OUT_F32 : y = (float)(acc + bias[k]) * scale[k]        (fp32, RNE)
+ * For bmm, "k" is the output column n (per-column bias / scale). */
+enum b200q_out_kind { B200Q_OUT_S32 = 0, B200Q_OUT_S8 = 1, B200Q_OUT_F32 = 2 };
+typedef struct b200q_epilogue {
+  int out_kind;
+  int zp_out;
+  int clamp_lo;
+  int clamp_hi;
+} b200q_epilogue;
+
+/* ---- drop-in entry points ---- */
+
+/* Quantized NHWC conv forward, int32 accumulators.
+ * d_x: [n,h,w,c] float codes, d_w: [k,r,s,c/groups] float codes (cast with truncation
+ * like static_cast<int32_t>), d_y: [n,ho,wo,k] int32, every element written.
+ * d_in_qp: device array of n qparams (per image), d_f_qp: device pointer to one qparams,
+ * of the struct type selected by qtype.
+ * y = sum over valid taps of (x - zp_in[img]) * (w - zp_f), int32 wrapping.
+ * Replaces conv_quant_detail::launch_fprop_nhwc_qi32_{u8,s5} (src/conv_types.h:232-241). */
+int b200q_fprop_nhwc_qi32(int qtype, const float* d_x, const float* d_w, int32_t* d_y, int n, int h,
+                          int w, int c, int r, int s, int k, const b200q_conv_params* p,
+                          const void* d_in_qp, const void* d_f_qp, void* stream);
+
+/* Blocked variant: the filter slice is chosen by the output block
+ * (by = ho / (ho_total / block_by), bx = wo / (wo_total / block_bx));
+ * d_w: [k, block_by, block_bx, r, s, c/groups].
+ * Replaces conv_quant_detail::launch_block_fprop_nhwc_qi32_{u8,s5} (src/conv_types.h:242-251). */
+int b200q_block_fprop_nhwc_qi32(int qtype, const float* d_x, const float* d_w, int32_t* d_y, int n,
+                                int h, int w, int c, int r, int s, int k,
+                                const b200q_conv_params* p, int block_by, int block_bx,
+                                const void* d_in_qp, const void* d_f_qp, void* stream);
+
+/* Row-major int32 batched GEMM, C_b = op(A_b) @ op(B_b), int32 wrap-around.
+ * Layouts as bmm.h:9-29.  Replaces bmm_matmul_i32 (bmm.h:69-74). */
+int b200q_bmm_matmul_i32(const int32_t* A, const int32_t* B, int32_t* C, int batch, int M, int N,
+                         int K, int trans_a, int trans_b, void* stream);
+
+/* ---- new int8 entry points ---- */
+
+/* int8 NHWC conv: d_x [n,h,w,c] int8, d_w [k,r,s,c/groups] int8, zero points 0,
+ * int32 accumulation, fused epilogue (see b200q_epilogue).  d_y element type per out_kind.
+ * d_bias: [k] int32 or NULL; d_scale: [k] fp32 (required for S8 / F32 outputs). */
+int b200q_conv2d_s8(const int8_t* d_x, const int8_t* d_w, const int32_t* d_bias,
+                    const float* d_scale, void* d_y, int n, int h, int w, int c, int r, int s,
+                    int k, const b200q_conv_params* p, const b200q_epilogue* epi, void* stream);
+
+/* int8 batched GEMM, layouts as bmm.h:9-29, int32 accumulation, per-column epilogue.
+ * d_bias: [N] int32 or NULL; d_col_scale: [N] fp32 (required for S8 / F32 outputs). */
+int b200q_bmm_s8(const int8_t* A, const int8_t* B, const int32_t* d_bias, const float* d_col_scale,
+                 void* C, int batch, int M, int N, int K, int trans_a, int trans_b,
+                 const b200q_epilogue* epi, void* stream);
+
+/* ---- host utilities ---- */
+
+/* Output shape with the checks of infer_conv_shape (src/conv_types.h:125-146). */
+int b200q_conv_out_shape(int h, int w, int c, int r, int s, int k, const b200q_conv_params* p,
+                         int* ho, int* wo);
+
+/* Message of the last failed call on this thread ("" if none). */
+const char* b200q_last_error(void);
+
+/* Synchronizes the device, then reads and clears the device-side error word that
+ * kernels set when a bounded wait runs out.  Returns B200Q_OK or B200Q_ERR_TIMEOUT. */
+int b200q_device_error(void);
+
+/* Which kernel family the last conv / bmm call on this thread dispatched to:
+ * 1 tcgen05 im2col conv, 2 tcgen05 tiled GEMM, 3 CUDA-core generic, 4 CUDA-core depthwise,
+ * 5 CUDA-core quantized-int32 (drop-in), 6 CUDA-core int32 bmm. */
+int b200q_last_path(void);
+
+/* 0 = automatic dispatch (default); 1 = force the CUDA-core kernels (cross-checks). */
+void b200q_set_path_policy(int policy);
+
+/* Number of tcgen05 kernel launches issued since load (for launch accounting). */
+long long b200q_tc_launch_count(void);
+
+/* ---- seeded synthetic data (counter-based splitmix64; the CPU oracle regenerates any slice) ---- */
+int b200q_fill_s8_uniform(int8_t* d_out, size_t count, uint64_t seed, uint64_t tensor_id, int lo,
+                          int hi, void* stream);
+int b200q_fill_i32_uniform(int32_t* d_out, size_t count, uint64_t seed, uint64_t tensor_id,
+                           int32_t lo, int32_t hi, void* stream);
+/* d_table: 65536 int8 codes in device memory (quantiles of the wanted distribution). */
+int b200q_fill_s8_table(int8_t* d_out, size_t count, uint64_t seed, uint64_t tensor_id,
+                        const int8_t* d_table, void* stream);
+
+/* Failure-path self test: one CTA waits on an mbarrier that nothing completes, with a
+ * limit of `cycles` SM clocks, then records a timeout and returns.  Synchronous.
+ * Returns B200Q_ERR_TIMEOUT when the bounded wait behaved (the expected result). */
+int b200q_selftest_wait_timeout(long long cycles);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B200Q_H_ */

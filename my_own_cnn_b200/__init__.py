@@ -1,0 +1,21 @@
+"""my_own_cnn_b200: B200-native (sm_100a) int8 NHWC convolution and batched GEMM.
+
+A from-scratch implementation of the quantized conv / bmm hot path of NikitaYak02/my_own_cnn
+behind the reference's own entry points.  The kernels live in ``libb200q.so`` (C ABI:
+include/b200q.h); this package is the Python host side over that ABI.
+"""
+from .quant import (DataType, QuantizationParametersU8, QuantizationParametersS5, get_zero_point,
+                    qparams_to_device)
+from .conv import (Conv2DParams, BlockConv2DParams, ConvShape, BlockConvShape, Epilogue, infer_conv_shape,
+                   infer_block_conv_shape, launch_fprop_nhwc_qi32, launch_block_fprop_nhwc_qi32, conv2d_s8,
+                   conv2d_s8_into, conv_out_shape)
+from .bmm import BMM_TRANSPOSE_NONE, BMM_TRANSPOSE_YES, bmm_matmul_i32, bmm_s8, bmm_s8_into
+from ._lib import B200QError, last_path, set_path_policy, tc_launch_count
+
+__all__ = [
+    "DataType", "QuantizationParametersU8", "QuantizationParametersS5", "get_zero_point", "qparams_to_device",
+    "Conv2DParams", "BlockConv2DParams", "ConvShape", "BlockConvShape", "Epilogue", "infer_conv_shape",
+    "infer_block_conv_shape", "launch_fprop_nhwc_qi32", "launch_block_fprop_nhwc_qi32", "conv2d_s8",
+    "conv2d_s8_into", "conv_out_shape", "BMM_TRANSPOSE_NONE", "BMM_TRANSPOSE_YES", "bmm_matmul_i32", "bmm_s8",
+    "bmm_s8_into", "B200QError", "last_path", "set_path_policy", "tc_launch_count",
+]

@@ -1,0 +1,534 @@
+// b200q: host side of the C ABI declared in include/b200q.h.
+//
+// Validation follows the reference's own checks (infer_conv_shape / infer_block_conv_shape,
+// src/conv_types.h:125-169) but returns status codes instead of throwing.  Dispatch:
+//   conv2d_s8 : tcgen05 implicit GEMM (im2col TMA, or plain tiled TMA for 1x1/s1/p0) when
+//               groups == 1, C % 32 == 0, K % 16 == 0 and the tensors are 16-byte aligned;
+//               depthwise CUDA-core kernel for groups == C == K, C % 16 == 0;
+//               CUDA-core direct kernel otherwise.
+//   bmm_s8    : tcgen05 tiled GEMM (K-major or MN-major operands) when the TMA stride rules hold,
+//               CUDA-core tiled GEMM otherwise.
+//   *_qi32 drop-ins and bmm_matmul_i32: exact CUDA-core kernels (float codes / arbitrary int32
+//               values do not fit the int8 tensor-core datapath).
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+
+#include "../../include/b200q.h"
+#include "common.cuh"
+#include "simt.cuh"
+#include "tc_gemm.cuh"
+
+namespace b200q {
+namespace {
+
+thread_local char g_errmsg[512] = "";
+thread_local int g_last_path = 0;
+std::atomic<int> g_policy{0};
+std::atomic<long long> g_tc_launches{0};
+
+__device__ int g_dev_err;
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_errmsg, sizeof(g_errmsg), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(B200Q_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+// --------------------------------------------------------------- per-device state
+struct DeviceState {
+  bool init = false;
+  int sms = 0;
+  int* err = nullptr;  // device address of g_dev_err
+};
+DeviceState g_dev[64];
+std::mutex g_dev_mu;
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+typedef CUresult (*EncodeIm2colFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const int*, const int*, cuuint32_t, cuuint32_t,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn g_encode_tiled = nullptr;
+EncodeIm2colFn g_encode_im2col = nullptr;
+
+long long wait_limit() {
+  static long long v = [] {
+    const char* s = getenv("B200Q_WAIT_LIMIT_CYCLES");
+    long long x = s ? atoll(s) : 0;
+    return x > 0 ? x : (1ll << 31);  // ~1 s of SM clocks
+  }();
+  return v;
+}
+
+int device_state(DeviceState** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= 64) return fail(B200Q_ERR_UNSUPPORTED, "device index %d out of range", dev);
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  DeviceState& st = g_dev[dev];
+  if (!st.init) {
+    e = cudaDeviceGetAttribute(&st.sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
+    e = cudaGetSymbolAddress(reinterpret_cast<void**>(&st.err), g_dev_err);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(g_dev_err)");
+    e = cudaFuncSetAttribute(tc_gemm_s8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(tc_gemm_s8_kernel)");
+    if (!g_encode_tiled) {
+      cudaDriverEntryPointQueryResult q;
+      void* fn = nullptr;
+      e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+      if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn)
+        return fail(B200Q_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+      g_encode_tiled = reinterpret_cast<EncodeTiledFn>(fn);
+      fn = nullptr;
+      e = cudaGetDriverEntryPoint("cuTensorMapEncodeIm2col", &fn, cudaEnableDefault, &q);
+      if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn)
+        return fail(B200Q_ERR_CUDA, "cuTensorMapEncodeIm2col unavailable");
+      g_encode_im2col = reinterpret_cast<EncodeIm2colFn>(fn);
+    }
+    st.init = true;
+  }
+  *out = &st;
+  return B200Q_OK;
+}
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+inline cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
+
+int grid_for(size_t total, int threads, int sms) {
+  size_t blocks = (total + threads - 1) / threads;
+  size_t cap = static_cast<size_t>(sms) * 16;
+  if (blocks > cap) blocks = cap;
+  if (blocks < 1) blocks = 1;
+  return static_cast<int>(blocks);
+}
+
+int check_launch(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, what);
+  return B200Q_OK;
+}
+
+int make_epilogue(const b200q_epilogue* epi, const int32_t* bias, const float* scale, Epilogue* out) {
+  if (!epi) return fail(B200Q_ERR_INVALID_ARG, "epilogue descriptor is null");
+  if (epi->out_kind < 0 || epi->out_kind > 2) return fail(B200Q_ERR_INVALID_ARG, "bad out_kind %d", epi->out_kind);
+  if (epi->out_kind != B200Q_OUT_S32 && !scale)
+    return fail(B200Q_ERR_INVALID_ARG, "int8 / fp32 outputs need per-channel scales");
+  if (epi->out_kind == B200Q_OUT_S8) {
+    if (epi->clamp_lo > epi->clamp_hi || epi->clamp_lo < -128 || epi->clamp_hi > 127)
+      return fail(B200Q_ERR_INVALID_ARG, "int8 clamp bounds [%d,%d] invalid", epi->clamp_lo, epi->clamp_hi);
+    if (epi->zp_out < -128 || epi->zp_out > 127) return fail(B200Q_ERR_INVALID_ARG, "zp_out out of int8 range");
+  }
+  out->out_kind = epi->out_kind;
+  out->zp = epi->zp_out;
+  out->lo = epi->clamp_lo;
+  out->hi = epi->clamp_hi;
+  out->bias = bias;
+  out->scale = scale;
+  return B200Q_OK;
+}
+
+size_t out_elem_size(int kind) { return kind == B200Q_OUT_S8 ? 1 : 4; }
+
+// ------------------------------------------------------------------ TMA maps
+int encode_tiled_3d(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2, uint32_t b0,
+                    uint32_t b1, int swizzle_bytes) {
+  cuuint64_t dims[3] = {d0, d1, d2};
+  cuuint64_t strides[2] = {d0, d0 * d1};  // bytes (uint8 elements)
+  cuuint32_t box[3] = {b0, b1, 1};
+  cuuint32_t es[3] = {1, 1, 1};
+  CUtensorMapSwizzle sw = swizzle_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                          : swizzle_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                                : CU_TENSOR_MAP_SWIZZLE_32B;
+  CUresult r = g_encode_tiled(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box,
+                              es, CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(B200Q_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d) dims %llu,%llu,%llu box %u,%u", (int)r,
+                (unsigned long long)d0, (unsigned long long)d1, (unsigned long long)d2, b0, b1);
+  return B200Q_OK;
+}
+
+int encode_im2col(CUtensorMap* map, const int8_t* x, const ConvGeom& g, int bk) {
+  cuuint64_t dims[4] = {(cuuint64_t)g.c, (cuuint64_t)g.w, (cuuint64_t)g.h, (cuuint64_t)g.n};
+  cuuint64_t strides[3] = {(cuuint64_t)g.c, (cuuint64_t)g.c * g.w, (cuuint64_t)g.c * g.w * g.h};
+  int lower[2] = {-g.pad_w, -g.pad_h};
+  int upper[2] = {g.pad_w - (g.s - 1) * g.dil_w, g.pad_h - (g.r - 1) * g.dil_h};
+  cuuint32_t es[4] = {1, (cuuint32_t)g.stride_w, (cuuint32_t)g.stride_h, 1};
+  CUtensorMapSwizzle sw = bk == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                          : bk == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                     : CU_TENSOR_MAP_SWIZZLE_32B;
+  CUresult r = g_encode_im2col(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<int8_t*>(x), dims, strides, lower,
+                               upper, (cuuint32_t)bk, (cuuint32_t)kTcBM, es, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(B200Q_ERR_CUDA, "cuTensorMapEncodeIm2col failed (%d)", (int)r);
+  return B200Q_OK;
+}
+
+// ------------------------------------------------------------- tcgen05 launch
+constexpr int kSmemLimit = 227 * 1024;
+constexpr int kSmemReserve = 1024 + 256;  // alignment slack + barriers / TMEM slot
+
+int pick_bn(int n, int mn_major_b) {
+  if (mn_major_b) return n <= 128 ? 128 : 256;
+  if (n <= 64) return 64;
+  if (n <= 128) return 128;
+  return 256;
+}
+
+int launch_tc(const DeviceState& st, const CUtensorMap& ma, const CUtensorMap& mb, TcArgs a, cudaStream_t stream) {
+  const int stage_bytes = kTcBM * a.BK + a.BN * a.BK;
+  int stages = (kSmemLimit - kSmemReserve) / stage_bytes;
+  if (stages > 8) stages = 8;
+  if (stages < 2) return fail(B200Q_ERR_UNSUPPORTED, "tile does not fit shared memory");
+  a.stages = stages;
+  a.m_tiles = (a.M + kTcBM - 1) / kTcBM;
+  a.n_tiles = (a.N + a.BN - 1) / a.BN;
+  const long long total = static_cast<long long>(a.batch) * a.m_tiles * a.n_tiles;
+  if (total > 0x7FFFFFFFll) return fail(B200Q_ERR_UNSUPPORTED, "too many tiles");
+  a.total_tiles = static_cast<int>(total);
+  a.tmem_cols = static_cast<uint32_t>(2 * a.BN);
+  a.idesc = (2u << 4)                                   // D = s32
+            | (1u << 7) | (1u << 10)                    // A, B signed int8
+            | (static_cast<uint32_t>(a.a_major) << 15)  // A major
+            | (static_cast<uint32_t>(a.b_major) << 16)  // B major
+            | (static_cast<uint32_t>(a.BN >> 3) << 17)  // N
+            | (static_cast<uint32_t>(kTcBM >> 4) << 24);  // M
+  a.wait_limit = wait_limit();
+  a.err = st.err;
+  const int grid = a.total_tiles < st.sms ? a.total_tiles : st.sms;
+  const size_t smem = static_cast<size_t>(stages) * stage_bytes + kSmemReserve;
+  tc_gemm_s8_kernel<<<grid, kTcThreads, smem, stream>>>(ma, mb, a);
+  g_tc_launches.fetch_add(1, std::memory_order_relaxed);
+  return check_launch("tc_gemm_s8_kernel launch");
+}
+
+int conv_geom(int n, int h, int w, int c, int r, int s, int k, const b200q_conv_params* p, int by, int bx,
+              ConvGeom* g) {
+  if (!p) return fail(B200Q_ERR_INVALID_ARG, "conv params pointer is null");
+  if (n <= 0 || h <= 0 || w <= 0 || c <= 0 || r <= 0 || s <= 0 || k <= 0)
+    return fail(B200Q_ERR_INVALID_ARG, "tensor dimensions must be > 0");
+  if (p->dilation_h <= 0 || p->dilation_w <= 0) return fail(B200Q_ERR_INVALID_ARG, "dilation must be > 0");
+  if (p->pad_h < 0 || p->pad_w < 0) return fail(B200Q_ERR_INVALID_ARG, "padding must be >= 0");
+  int ho = 0, wo = 0;
+  int rc = b200q_conv_out_shape(h, w, c, r, s, k, p, &ho, &wo);
+  if (rc) return rc;
+  if (by <= 0 || bx <= 0) return fail(B200Q_ERR_INVALID_ARG, "block_by and block_bx must be > 0");
+  if (ho % by || wo % bx) return fail(B200Q_ERR_INVALID_ARG, "blocked convolution requires Ho/Wo divisible by block grid");
+  g->n = n; g->h = h; g->w = w; g->c = c; g->r = r; g->s = s; g->k = k; g->ho = ho; g->wo = wo;
+  g->pad_h = p->pad_h; g->pad_w = p->pad_w; g->stride_h = p->stride_h; g->stride_w = p->stride_w;
+  g->dil_h = p->dilation_h; g->dil_w = p->dilation_w; g->groups = p->groups;
+  g->cg = c / p->groups; g->kg = k / p->groups;
+  g->by = by; g->bx = bx; g->bho = ho / by; g->bwo = wo / bx;
+  const long long total = static_cast<long long>(n) * ho * wo * k;
+  if (total > (1ll << 46)) return fail(B200Q_ERR_UNSUPPORTED, "output too large");
+  return B200Q_OK;
+}
+
+int qi32_common(int qtype, const float* x, const float* w, int32_t* y, const ConvGeom& g, const void* in_qp,
+                const void* f_qp, void* stream) {
+  if (qtype != B200Q_LINQUANT_U8 && qtype != B200Q_LINQUANT_S5)
+    return fail(B200Q_ERR_INVALID_ARG, "quantized conv supports only LinQuantU8 and LinQuantS5");
+  if (!in_qp || !f_qp) return fail(B200Q_ERR_INVALID_ARG, "quantized CUDA fprop requires non-null quantization parameters");
+  if (!x || !w || !y) return fail(B200Q_ERR_INVALID_ARG, "null tensor pointer");
+  DeviceState* st = nullptr;
+  int rc = device_state(&st);
+  if (rc) return rc;
+  const int stride = qtype == B200Q_LINQUANT_U8 ? (int)sizeof(b200q_qparams_u8) : (int)sizeof(b200q_qparams_s5);
+  const size_t total = static_cast<size_t>(g.n) * g.ho * g.wo * g.k;
+  qi32_conv_kernel<<<grid_for(total, 256, st->sms), 256, 0, as_stream(stream)>>>(
+      x, w, y, g, static_cast<const uint8_t*>(in_qp), static_cast<const uint8_t*>(f_qp), stride,
+      qtype == B200Q_LINQUANT_S5);
+  g_last_path = 5;
+  return check_launch("qi32_conv_kernel launch");
+}
+
+}  // namespace
+}  // namespace b200q
+
+using namespace b200q;
+
+extern "C" {
+
+const char* b200q_last_error(void) { return g_errmsg; }
+int b200q_last_path(void) { return g_last_path; }
+void b200q_set_path_policy(int policy) { g_policy.store(policy); }
+long long b200q_tc_launch_count(void) { return g_tc_launches.load(); }
+
+int b200q_conv_out_shape(int h, int w, int c, int r, int s, int k, const b200q_conv_params* p, int* ho, int* wo) {
+  if (!p || !ho || !wo) return fail(B200Q_ERR_INVALID_ARG, "null argument");
+  if (p->groups <= 0) return fail(B200Q_ERR_INVALID_ARG, "groups must be > 0");
+  if (c % p->groups != 0) return fail(B200Q_ERR_INVALID_ARG, "input channels must be divisible by groups");
+  if (k % p->groups != 0) return fail(B200Q_ERR_INVALID_ARG, "output channels must be divisible by groups");
+  const int hn = h + 2 * p->pad_h - p->dilation_h * (r - 1) - 1;
+  const int wn = w + 2 * p->pad_w - p->dilation_w * (s - 1) - 1;
+  if (hn < 0 || wn < 0) return fail(B200Q_ERR_INVALID_ARG, "invalid output size (negative numerator)");
+  if (p->stride_h <= 0 || p->stride_w <= 0) return fail(B200Q_ERR_INVALID_ARG, "stride must be > 0");
+  *ho = hn / p->stride_h + 1;
+  *wo = wn / p->stride_w + 1;
+  if (*ho <= 0 || *wo <= 0) return fail(B200Q_ERR_INVALID_ARG, "computed output size is <= 0");
+  return B200Q_OK;
+}
+
+int b200q_fprop_nhwc_qi32(int qtype, const float* d_x, const float* d_w, int32_t* d_y, int n, int h, int w, int c,
+                          int r, int s, int k, const b200q_conv_params* p, const void* d_in_qp, const void* d_f_qp,
+                          void* stream) {
+  ConvGeom g;
+  int rc = conv_geom(n, h, w, c, r, s, k, p, 1, 1, &g);
+  if (rc) return rc;
+  return qi32_common(qtype, d_x, d_w, d_y, g, d_in_qp, d_f_qp, stream);
+}
+
+int b200q_block_fprop_nhwc_qi32(int qtype, const float* d_x, const float* d_w, int32_t* d_y, int n, int h, int w,
+                                int c, int r, int s, int k, const b200q_conv_params* p, int block_by, int block_bx,
+                                const void* d_in_qp, const void* d_f_qp, void* stream) {
+  ConvGeom g;
+  int rc = conv_geom(n, h, w, c, r, s, k, p, block_by, block_bx, &g);
+  if (rc) return rc;
+  return qi32_common(qtype, d_x, d_w, d_y, g, d_in_qp, d_f_qp, stream);
+}
+
+int b200q_bmm_matmul_i32(const int32_t* A, const int32_t* B, int32_t* C, int batch, int M, int N, int K,
+                         int trans_a, int trans_b, void* stream) {
+  if (batch < 0 || M < 0 || N < 0 || K < 0) return fail(B200Q_ERR_INVALID_ARG, "negative bmm dimension");
+  if (batch == 0 || M == 0 || N == 0) return B200Q_OK;
+  if (!A || !B || !C) return fail(B200Q_ERR_INVALID_ARG, "null bmm pointer");
+  DeviceState* st = nullptr;
+  int rc = device_state(&st);
+  if (rc) return rc;
+  Epilogue e{kOutS32, 0, 0, 0, nullptr, nullptr};
+  for (int b0 = 0; b0 < batch; b0 += 65535) {
+    const int nb = batch - b0 < 65535 ? batch - b0 : 65535;
+    dim3 grid((N + 63) / 64, (M + 63) / 64, nb);
+    if (grid.y > 65535) return fail(B200Q_ERR_UNSUPPORTED, "M too large for the CUDA-core bmm");
+    bmm_simt_kernel<int32_t><<<grid, 256, 0, as_stream(stream)>>>(
+        A + static_cast<size_t>(b0) * M * K, B + static_cast<size_t>(b0) * K * N,
+        C + static_cast<size_t>(b0) * M * N, M, N, K, trans_a != 0, trans_b != 0, e);
+    rc = check_launch("bmm_simt_kernel<int32> launch");
+    if (rc) return rc;
+  }
+  g_last_path = 6;
+  return B200Q_OK;
+}
+
+int b200q_conv2d_s8(const int8_t* d_x, const int8_t* d_w, const int32_t* d_bias, const float* d_scale, void* d_y,
+                    int n, int h, int w, int c, int r, int s, int k, const b200q_conv_params* p,
+                    const b200q_epilogue* epi, void* stream) {
+  ConvGeom g;
+  int rc = conv_geom(n, h, w, c, r, s, k, p, 1, 1, &g);
+  if (rc) return rc;
+  if (!d_x || !d_w || !d_y) return fail(B200Q_ERR_INVALID_ARG, "null tensor pointer");
+  Epilogue e;
+  rc = make_epilogue(epi, d_bias, d_scale, &e);
+  if (rc) return rc;
+  DeviceState* st = nullptr;
+  rc = device_state(&st);
+  if (rc) return rc;
+  cudaStream_t cs = as_stream(stream);
+  const long long M = static_cast<long long>(n) * g.ho * g.wo;
+  const size_t x_bytes = static_cast<size_t>(n) * h * w * c;
+  const bool vec_ptrs = aligned16(d_x) && aligned16(d_w) && aligned16(d_y) && (!d_bias || aligned16(d_bias)) &&
+                        (!d_scale || aligned16(d_scale));
+  const bool is_1x1_plain = r == 1 && s == 1 && g.stride_h == 1 && g.stride_w == 1 && g.pad_h == 0 && g.pad_w == 0;
+  const bool corners_ok = g.pad_w <= 127 && g.pad_h <= 127 && g.pad_w - (s - 1) * g.dil_w >= -128 &&
+                          g.pad_h - (r - 1) * g.dil_h >= -128 && (s - 1) * g.dil_w <= 255 && (r - 1) * g.dil_h <= 255 &&
+                          g.stride_h <= 8 && g.stride_w <= 8;
+  // Small activations take the CUDA-core path: the im2col TMA mode is only used on tensors of
+  // at least 128 KiB (a driver limitation on small im2col maps).
+  const bool tc_ok = g_policy.load() == 0 && g.groups == 1 && c % 32 == 0 && k % 16 == 0 && vec_ptrs &&
+                     M < (1ll << 31) && (is_1x1_plain || (corners_ok && x_bytes >= (128u << 10)));
+  if (tc_ok) {
+    TcArgs a{};
+    a.BK = c % 128 == 0 ? 128 : (c % 64 == 0 ? 64 : 32);
+    a.BN = pick_bn(k, 0);
+    a.M = static_cast<int>(M);
+    a.N = k;
+    a.batch = 1;
+    a.a_major = 0;
+    a.b_major = 0;
+    a.b_batched = 0;
+    a.epi = e;
+    a.out = d_y;
+    a.ldc = k;
+    a.batch_stride = 0;
+    a.vec_ok = 1;
+    CUtensorMap ma, mb;
+    const int kdim = r * s * c;
+    rc = encode_tiled_3d(&mb, d_w, static_cast<uint64_t>(kdim), static_cast<uint64_t>(k), 1, a.BK, a.BN, a.BK);
+    if (rc) return rc;
+    if (is_1x1_plain) {
+      a.mode = 0;
+      a.num_kb = (c + a.BK - 1) / a.BK;
+      rc = encode_tiled_3d(&ma, d_x, static_cast<uint64_t>(c), static_cast<uint64_t>(M), 1, a.BK, kTcBM, a.BK);
+      if (rc) return rc;
+      g_last_path = 2;
+    } else {
+      a.mode = 1;
+      a.cchunks = c / a.BK;
+      a.num_kb = r * s * a.cchunks;
+      a.Ho = g.ho; a.Wo = g.wo; a.S = s;
+      a.stride_h = g.stride_h; a.stride_w = g.stride_w;
+      a.pad_h = g.pad_h; a.pad_w = g.pad_w;
+      a.dil_h = g.dil_h; a.dil_w = g.dil_w;
+      rc = encode_im2col(&ma, d_x, g, a.BK);
+      if (rc) return rc;
+      g_last_path = 1;
+    }
+    return launch_tc(*st, ma, mb, a, cs);
+  }
+  const size_t total = static_cast<size_t>(M) * k;
+  if (g.groups == c && k == c && c % 16 == 0 && r * s * c <= 48 * 1024 && aligned16(d_x) && aligned16(d_y)) {
+    const size_t items = static_cast<size_t>(M) * (c / 16);
+    dw_conv_s8_kernel<<<grid_for(items, 256, st->sms), 256, r * s * c, cs>>>(d_x, d_w, d_y, g, e);
+    g_last_path = 4;
+    return check_launch("dw_conv_s8_kernel launch");
+  }
+  const int dp4a = (g.cg % 4 == 0) && (c % 4 == 0) && (reinterpret_cast<uintptr_t>(d_x) % 4 == 0) &&
+                   (reinterpret_cast<uintptr_t>(d_w) % 4 == 0);
+  conv_s8_generic_kernel<<<grid_for(total, 256, st->sms), 256, 0, cs>>>(d_x, d_w, d_y, g, e, dp4a);
+  g_last_path = 3;
+  return check_launch("conv_s8_generic_kernel launch");
+}
+
+int b200q_bmm_s8(const int8_t* A, const int8_t* B, const int32_t* d_bias, const float* d_col_scale, void* C,
+                 int batch, int M, int N, int K, int trans_a, int trans_b, const b200q_epilogue* epi, void* stream) {
+  if (batch < 0 || M < 0 || N < 0 || K < 0) return fail(B200Q_ERR_INVALID_ARG, "negative bmm dimension");
+  if (batch == 0 || M == 0 || N == 0) return B200Q_OK;
+  if (!A || !B || !C) return fail(B200Q_ERR_INVALID_ARG, "null bmm pointer");
+  Epilogue e;
+  int rc = make_epilogue(epi, d_bias, d_col_scale, &e);
+  if (rc) return rc;
+  DeviceState* st = nullptr;
+  rc = device_state(&st);
+  if (rc) return rc;
+  cudaStream_t cs = as_stream(stream);
+  const bool ta = trans_a != 0, tb = trans_b != 0;
+  const bool vec_ptrs = aligned16(A) && aligned16(B) && aligned16(C) && (!d_bias || aligned16(d_bias)) &&
+                        (!d_col_scale || aligned16(d_col_scale));
+  const bool tc_ok = g_policy.load() == 0 && K > 0 && vec_ptrs && (ta ? M % 16 == 0 : K % 16 == 0) &&
+                     (tb ? K % 16 == 0 : N % 16 == 0);
+  if (tc_ok) {
+    TcArgs a{};
+    a.mode = 0;
+    a.BK = 128;
+    a.a_major = ta ? 1 : 0;
+    a.b_major = tb ? 0 : 1;  // B stored [K][N] (no transpose) is N-contiguous = MN-major
+    a.BN = pick_bn(N, a.b_major);
+    a.M = M;
+    a.N = N;
+    a.batch = batch;
+    a.b_batched = 1;
+    a.num_kb = (K + a.BK - 1) / a.BK;
+    a.epi = e;
+    a.out = C;
+    a.ldc = N;
+    a.batch_stride = static_cast<long long>(M) * N;
+    a.vec_ok = N % 16 == 0;
+    CUtensorMap ma, mb;
+    if (!ta)
+      rc = encode_tiled_3d(&ma, A, (uint64_t)K, (uint64_t)M, (uint64_t)batch, a.BK, kTcBM, 128);
+    else
+      rc = encode_tiled_3d(&ma, A, (uint64_t)M, (uint64_t)K, (uint64_t)batch, kTcBM, a.BK, 128);
+    if (rc) return rc;
+    if (tb)
+      rc = encode_tiled_3d(&mb, B, (uint64_t)K, (uint64_t)N, (uint64_t)batch, a.BK, a.BN, 128);
+    else
+      rc = encode_tiled_3d(&mb, B, (uint64_t)N, (uint64_t)K, (uint64_t)batch, 128, a.BK, 128);
+    if (rc) return rc;
+    g_last_path = 2;
+    return launch_tc(*st, ma, mb, a, cs);
+  }
+  for (int b0 = 0; b0 < batch; b0 += 65535) {
+    const int nb = batch - b0 < 65535 ? batch - b0 : 65535;
+    dim3 grid((N + 63) / 64, (M + 63) / 64, nb);
+    if (grid.y > 65535) return fail(B200Q_ERR_UNSUPPORTED, "M too large for the CUDA-core bmm");
+    const size_t osz = out_elem_size(e.out_kind);
+    bmm_simt_kernel<int8_t><<<grid, 256, 0, cs>>>(A + static_cast<size_t>(b0) * M * K, B + static_cast<size_t>(b0) * K * N,
+                                                  static_cast<char*>(C) + static_cast<size_t>(b0) * M * N * osz, M, N, K,
+                                                  ta, tb, e);
+    rc = check_launch("bmm_simt_kernel<int8> launch");
+    if (rc) return rc;
+  }
+  g_last_path = 3;
+  return B200Q_OK;
+}
+
+int b200q_device_error(void) {
+  DeviceState* st = nullptr;
+  int rc = device_state(&st);
+  if (rc) return rc;
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceSynchronize");
+  int v = 0;
+  e = cudaMemcpy(&v, st->err, sizeof(int), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_fail(e, "read device error word");
+  if (v != 0) {
+    const int zero = 0;
+    cudaMemcpy(st->err, &zero, sizeof(int), cudaMemcpyHostToDevice);
+    return fail(B200Q_ERR_TIMEOUT, "device wait ran out (code 0x%x)", v);
+  }
+  return B200Q_OK;
+}
+
+int b200q_selftest_wait_timeout(long long cycles) {
+  DeviceState* st = nullptr;
+  int rc = device_state(&st);
+  if (rc) return rc;
+  wait_timeout_probe_kernel<<<1, 32>>>(cycles > 0 ? cycles : 1000, st->err);
+  rc = check_launch("wait_timeout_probe_kernel launch");
+  if (rc) return rc;
+  return b200q_device_error();
+}
+
+int b200q_fill_s8_uniform(int8_t* d_out, size_t count, uint64_t seed, uint64_t tensor_id, int lo, int hi,
+                          void* stream) {
+  if (!d_out || lo > hi || lo < -128 || hi > 127) return fail(B200Q_ERR_INVALID_ARG, "bad fill arguments");
+  DeviceState* st = nullptr;
+  int rc = device_state(&st);
+  if (rc) return rc;
+  const uint64_t key = mix64(seed * 0x9E3779B97F4A7C15ull ^ mix64(tensor_id + 0x632BE59BD9B4E019ull));
+  fill_s8_uniform_kernel<<<grid_for(count, 256, st->sms), 256, 0, as_stream(stream)>>>(
+      d_out, count, key, lo, static_cast<uint64_t>(hi - lo + 1));
+  return check_launch("fill_s8_uniform_kernel launch");
+}
+
+int b200q_fill_i32_uniform(int32_t* d_out, size_t count, uint64_t seed, uint64_t tensor_id, int32_t lo, int32_t hi,
+                           void* stream) {
+  if (!d_out || lo > hi) return fail(B200Q_ERR_INVALID_ARG, "bad fill arguments");
+  DeviceState* st = nullptr;
+  int rc = device_state(&st);
+  if (rc) return rc;
+  const uint64_t key = mix64(seed * 0x9E3779B97F4A7C15ull ^ mix64(tensor_id + 0x632BE59BD9B4E019ull));
+  fill_i32_uniform_kernel<<<grid_for(count, 256, st->sms), 256, 0, as_stream(stream)>>>(
+      d_out, count, key, lo, static_cast<uint64_t>(static_cast<long long>(hi) - lo + 1));
+  return check_launch("fill_i32_uniform_kernel launch");
+}
+
+int b200q_fill_s8_table(int8_t* d_out, size_t count, uint64_t seed, uint64_t tensor_id, const int8_t* d_table,
+                        void* stream) {
+  if (!d_out || !d_table) return fail(B200Q_ERR_INVALID_ARG, "bad fill arguments");
+  DeviceState* st = nullptr;
+  int rc = device_state(&st);
+  if (rc) return rc;
+  const uint64_t key = mix64(seed * 0x9E3779B97F4A7C15ull ^ mix64(tensor_id + 0x632BE59BD9B4E019ull));
+  fill_s8_table_kernel<<<grid_for(count, 256, st->sms), 256, 0, as_stream(stream)>>>(d_out, count, key, d_table);
+  return check_launch("fill_s8_table_kernel launch");
+}
+
+}  // extern "C"

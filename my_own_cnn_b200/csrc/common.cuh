@@ -1,0 +1,53 @@
+// Shared definitions of the b200q CUDA library: epilogue semantics, device error codes.
+#pragma once
+#include <cstdint>
+
+namespace b200q {
+
+constexpr int kOutS32 = 0;
+constexpr int kOutS8 = 1;
+constexpr int kOutF32 = 2;
+
+// Device error word values (first writer wins).
+constexpr int kDevErrTimeoutProducer = 0x101;
+constexpr int kDevErrTimeoutMma = 0x102;
+constexpr int kDevErrTimeoutEpilogue = 0x103;
+constexpr int kDevErrTimeoutProbe = 0x104;
+
+struct Epilogue {
+  int out_kind;
+  int zp;
+  int lo;  // clamp bounds in the output code domain
+  int hi;
+  const int32_t* bias;  // may be null
+  const float* scale;   // required for S8 / F32
+};
+
+// Requantize one int32 value (bias already added, wrapping):
+//   p = (float)t * scale   (both IEEE round-to-nearest-even, no contraction)
+//   q = rint(clamp(p, lo - zp, hi - zp)) + zp   (half to even)
+// Clamping before the float->int conversion keeps the conversion in range; it gives the same
+// code as rounding first, because the bounds are integers.
+__device__ __forceinline__ int requant_one(int32_t t, float sc, const Epilogue& e) {
+  float p = __fmul_rn(__int2float_rn(t), sc);
+  p = fminf(fmaxf(p, static_cast<float>(e.lo - e.zp)), static_cast<float>(e.hi - e.zp));
+  return __float2int_rn(p) + e.zp;
+}
+
+__device__ __forceinline__ int32_t wrap_add(int32_t a, int32_t b) {
+  return static_cast<int32_t>(static_cast<uint32_t>(a) + static_cast<uint32_t>(b));
+}
+
+// Apply the epilogue to one accumulator and store it at out[idx] (element index).
+__device__ __forceinline__ void epilogue_store(const Epilogue& e, void* out, size_t idx, int32_t acc, int col) {
+  const int32_t t = e.bias ? wrap_add(acc, __ldg(e.bias + col)) : acc;
+  if (e.out_kind == kOutS32) {
+    static_cast<int32_t*>(out)[idx] = t;
+  } else if (e.out_kind == kOutF32) {
+    static_cast<float*>(out)[idx] = __fmul_rn(__int2float_rn(t), __ldg(e.scale + col));
+  } else {
+    static_cast<int8_t*>(out)[idx] = static_cast<int8_t>(requant_one(t, __ldg(e.scale + col), e));
+  }
+}
+
+}  // namespace b200q

@@ -1,0 +1,355 @@
+// Persistent, warp-specialised tcgen05 int8 GEMM engine for sm_100a.
+//
+// One CTA per SM, 192 threads:
+//   warp 0      TMA producer (one elected lane): A tile (tiled 3-D map, or im2col 4-D map for
+//               convolutions) and B tile into a `stages`-deep shared-memory ring;
+//   warp 1      owns TMEM (alloc/dealloc) and issues tcgen05.mma.kind::i8 from one lane;
+//               accumulators are double-buffered in TMEM (2 x BN columns of int32);
+//   warps 2..5  epilogue: tcgen05.ld of the accumulator rows (warp w reads TMEM lanes
+//               32*(w%4)..+31), fused bias / scale / round / clamp / pack, 16-byte stores.
+// The GEMM is C[b][m][n] = sum_k A[b][m][k] * B[b][n][k] with M tile 128, N tile BN, K block BK
+// bytes (= int8 elements).  For a convolution, m = (image, ho, wo), n = output channel,
+// k = (r, s, c) -- the im2col TMA gathers the activation rows directly from NHWC memory, with
+// zero fill for padding, so no im2col matrix is ever written.
+//
+// Every mbarrier wait is bounded (clock64 limit); on expiry a role records an error code in the
+// device error word and leaves its loop; the CTA then drains its MMAs and frees TMEM.
+#pragma once
+#include "common.cuh"
+#include "ptx.cuh"
+
+namespace b200q {
+
+constexpr int kTcThreads = 192;
+constexpr int kTcBM = 128;
+
+struct TcArgs {
+  int mode;  // 0 = tiled 3-D A map, 1 = im2col A map
+  int M, N;  // GEMM rows / cols per batch item
+  int batch;
+  int BN, BK, stages, num_kb;
+  int m_tiles, n_tiles, total_tiles;
+  int a_major, b_major;  // 0 = K-major, 1 = MN-major (bmm transposes)
+  int b_batched;         // B map has a batch dimension (bmm); conv weights are shared
+  // im2col geometry
+  int Ho, Wo, S, cchunks, stride_h, stride_w, pad_h, pad_w, dil_h, dil_w;
+  // epilogue
+  Epilogue epi;
+  void* out;
+  long long ldc;            // elements between output rows
+  long long batch_stride;   // elements between output batch items
+  int vec_ok;               // rows and bias/scale allow 16-byte vector stores
+  uint32_t idesc;
+  uint32_t tmem_cols;
+  long long wait_limit;
+  int* err;
+};
+
+__device__ __forceinline__ uint32_t kmajor_layout(int bk) {
+  return bk == 128 ? 2u : (bk == 64 ? 4u : 6u);  // SWIZZLE_128B / 64B / 32B
+}
+
+// Fused epilogue for one row and 32 consecutive output columns [n, n + valid).
+__device__ __forceinline__ void store_chunk(const TcArgs& a, const uint32_t (&v)[32], int b, int m,
+                                            int n, int valid) {
+  const Epilogue& e = a.epi;
+  const size_t off = static_cast<size_t>(b) * a.batch_stride + static_cast<size_t>(m) * a.ldc + n;
+  int32_t t[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) t[j] = static_cast<int32_t>(v[j]);
+  if (e.bias) {
+    if (valid == 32 && a.vec_ok) {
+      const int4* bp = reinterpret_cast<const int4*>(e.bias + n);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const int4 bb = __ldg(bp + q);
+        t[4 * q + 0] = static_cast<int32_t>(static_cast<uint32_t>(t[4 * q + 0]) + static_cast<uint32_t>(bb.x));
+        t[4 * q + 1] = static_cast<int32_t>(static_cast<uint32_t>(t[4 * q + 1]) + static_cast<uint32_t>(bb.y));
+        t[4 * q + 2] = static_cast<int32_t>(static_cast<uint32_t>(t[4 * q + 2]) + static_cast<uint32_t>(bb.z));
+        t[4 * q + 3] = static_cast<int32_t>(static_cast<uint32_t>(t[4 * q + 3]) + static_cast<uint32_t>(bb.w));
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (j < valid)
+          t[j] = static_cast<int32_t>(static_cast<uint32_t>(t[j]) + static_cast<uint32_t>(__ldg(e.bias + n + j)));
+    }
+  }
+  if (e.out_kind == kOutS32) {
+    int32_t* o = static_cast<int32_t*>(a.out) + off;
+    if (valid == 32 && a.vec_ok) {
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        reinterpret_cast<int4*>(o)[q] = make_int4(t[4 * q], t[4 * q + 1], t[4 * q + 2], t[4 * q + 3]);
+    } else {
+      for (int j = 0; j < valid; ++j) o[j] = t[j];
+    }
+    return;
+  }
+  float sc[32];
+  if (valid == 32 && a.vec_ok) {
+    const float4* sp = reinterpret_cast<const float4*>(e.scale + n);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const float4 s4 = __ldg(sp + q);
+      sc[4 * q] = s4.x; sc[4 * q + 1] = s4.y; sc[4 * q + 2] = s4.z; sc[4 * q + 3] = s4.w;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) sc[j] = (j < valid) ? __ldg(e.scale + n + j) : 0.0f;
+  }
+  if (e.out_kind == kOutF32) {
+    float* o = static_cast<float*>(a.out) + off;
+    float f[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) f[j] = __fmul_rn(__int2float_rn(t[j]), sc[j]);
+    if (valid == 32 && a.vec_ok) {
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        reinterpret_cast<float4*>(o)[q] = make_float4(f[4 * q], f[4 * q + 1], f[4 * q + 2], f[4 * q + 3]);
+    } else {
+      for (int j = 0; j < valid; ++j) o[j] = f[j];
+    }
+    return;
+  }
+  // int8 requantization
+  uint32_t packed[8];
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    uint32_t w = 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int code = requant_one(t[4 * q + i], sc[4 * q + i], e);
+      w |= (static_cast<uint32_t>(code) & 0xFFu) << (8 * i);
+    }
+    packed[q] = w;
+  }
+  int8_t* o = static_cast<int8_t*>(a.out) + off;
+  if (valid == 32 && a.vec_ok) {
+    reinterpret_cast<int4*>(o)[0] = make_int4(packed[0], packed[1], packed[2], packed[3]);
+    reinterpret_cast<int4*>(o)[1] = make_int4(packed[4], packed[5], packed[6], packed[7]);
+  } else {
+    for (int j = 0; j < valid; ++j) o[j] = static_cast<int8_t>((packed[j >> 2] >> (8 * (j & 3))) & 0xFFu);
+  }
+}
+
+__global__ void __launch_bounds__(kTcThreads, 1)
+    tc_gemm_s8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                      const TcArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t stage_a = kTcBM * a.BK;
+  const uint32_t stage_b = a.BN * a.BK;
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + a.stages * stage_a;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + a.stages * stage_b);
+  // bars: full[stages], empty[stages], acc_full[2], acc_empty[2], drain[1]
+  const uint32_t full0 = smem_u32(bars);
+  const uint32_t empty0 = smem_u32(bars + a.stages);
+  const uint32_t accf0 = smem_u32(bars + 2 * a.stages);
+  const uint32_t acce0 = smem_u32(bars + 2 * a.stages + 2);
+  const uint32_t drain = smem_u32(bars + 2 * a.stages + 4);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * a.stages + 5);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < a.stages; ++i) {
+      mbar_init(full0 + 8 * i, 1);
+      mbar_init(empty0 + 8 * i, 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(accf0 + 8 * i, 1);
+      mbar_init(acce0 + 8 * i, 4);
+    }
+    mbar_init(drain, 1);
+    fence_mbar_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), a.tmem_cols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int tiles_per_batch = a.m_tiles * a.n_tiles;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ producer
+      int stage = 0;
+      uint32_t ph = 0;
+      uint32_t issued_mask = 0;  // stages that received a load
+      uint32_t last_ph = 0;      // parity of the last load into each stage (bit per stage)
+      bool ok = true;
+      const uint32_t tx = stage_a + stage_b;
+      for (int tile = blockIdx.x; tile < a.total_tiles && ok; tile += gridDim.x) {
+        const int b = tile / tiles_per_batch;
+        const int rem = tile - b * tiles_per_batch;
+        const int mt = rem / a.n_tiles;
+        const int nt = rem - mt * a.n_tiles;
+        const int m0 = mt * kTcBM, n0 = nt * a.BN;
+        int img = 0, wbase = 0, hbase = 0;
+        if (a.mode == 1) {
+          const int hw = a.Ho * a.Wo;
+          img = m0 / hw;
+          const int r0 = m0 - img * hw;
+          const int ho = r0 / a.Wo;
+          const int wo = r0 - ho * a.Wo;
+          wbase = wo * a.stride_w - a.pad_w;
+          hbase = ho * a.stride_h - a.pad_h;
+        }
+        for (int kb = 0; kb < a.num_kb; ++kb) {
+          if (!mbar_wait_bounded(empty0 + 8 * stage, ph ^ 1u, a.wait_limit, a.err, kDevErrTimeoutProducer)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb = full0 + 8 * stage;
+          mbar_arrive_expect_tx(fb, tx);
+          const uint32_t dA = smem_u32(sA + stage * stage_a);
+          const uint32_t dB = smem_u32(sB + stage * stage_b);
+          if (a.mode == 1) {
+            const int tap = kb / a.cchunks;
+            const int cc = kb - tap * a.cchunks;
+            const int r = tap / a.S;
+            const int s = tap - r * a.S;
+            tma_load_im2col_4d(dA, &tmA, fb, cc * a.BK, wbase, hbase, img,
+                               static_cast<uint16_t>(s * a.dil_w), static_cast<uint16_t>(r * a.dil_h));
+          } else if (a.a_major == 0) {
+            tma_load_3d(dA, &tmA, fb, kb * a.BK, m0, b);
+          } else {
+            tma_load_3d(dA, &tmA, fb, m0, kb * a.BK, b);
+          }
+          const int bb = a.b_batched ? b : 0;
+          if (a.b_major == 0) {
+            tma_load_3d(dB, &tmB, fb, kb * a.BK, n0, bb);
+          } else {
+            for (int i = 0; i < a.BN / 128; ++i)
+              tma_load_3d(dB + i * a.BK * 128, &tmB, fb, n0 + 128 * i, kb * a.BK, bb);
+          }
+          issued_mask |= 1u << stage;
+          last_ph = (last_ph & ~(1u << stage)) | (ph << stage);
+          if (++stage == a.stages) {
+            stage = 0;
+            ph ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        // Let every copy already issued land before the CTA exits.
+        for (int i = 0; i < a.stages; ++i)
+          if (issued_mask & (1u << i))
+            mbar_wait_bounded(full0 + 8 * i, (last_ph >> i) & 1u, a.wait_limit, a.err, kDevErrTimeoutProducer);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ----------------------------------------------------------------- MMA
+      int stage = 0;
+      uint32_t ph = 0;
+      int buf = 0;
+      uint32_t acc_ph = 0;
+      bool ok = true;
+      const uint32_t a_layout = a.a_major == 0 ? kmajor_layout(a.BK) : 2u;
+      const uint32_t b_layout = a.b_major == 0 ? kmajor_layout(a.BK) : 2u;
+      const uint32_t a_lbo = a.a_major == 0 ? 16u : static_cast<uint32_t>(a.BK) * 128u;
+      const uint32_t a_sbo = a.a_major == 0 ? 8u * a.BK : 1024u;
+      const uint32_t b_lbo = a.b_major == 0 ? 16u : static_cast<uint32_t>(a.BK) * 128u;
+      const uint32_t b_sbo = a.b_major == 0 ? 8u * a.BK : 1024u;
+      const uint32_t a_step = a.a_major == 0 ? 32u : 4096u;  // bytes per K=32 slice
+      const uint32_t b_step = a.b_major == 0 ? 32u : 4096u;
+      const int ksteps = a.BK / 32;
+      for (int tile = blockIdx.x; tile < a.total_tiles && ok; tile += gridDim.x) {
+        if (!mbar_wait_bounded(acce0 + 8 * buf, acc_ph ^ 1u, a.wait_limit, a.err, kDevErrTimeoutMma)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * a.BN);
+        for (int kb = 0; kb < a.num_kb; ++kb) {
+          if (!mbar_wait_bounded(full0 + 8 * stage, ph, a.wait_limit, a.err, kDevErrTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t aB = smem_u32(sA + stage * stage_a);
+          const uint32_t bB = smem_u32(sB + stage * stage_b);
+          for (int j = 0; j < ksteps; ++j) {
+            const uint64_t ad = make_smem_desc(aB + j * a_step, a_lbo, a_sbo, a_layout);
+            const uint64_t bd = make_smem_desc(bB + j * b_step, b_lbo, b_sbo, b_layout);
+            tc_mma_i8(d_tmem, ad, bd, a.idesc, (kb | j) != 0 ? 1u : 0u);
+          }
+          tc_commit(empty0 + 8 * stage);
+          if (++stage == a.stages) {
+            stage = 0;
+            ph ^= 1u;
+          }
+        }
+        if (!ok) break;
+        tc_commit(accf0 + 8 * buf);
+        if (++buf == 2) {
+          buf = 0;
+          acc_ph ^= 1u;
+        }
+      }
+      // Wait for every MMA issued by this thread before TMEM is released.
+      tc_commit(drain);
+      mbar_wait_bounded(drain, 0, a.wait_limit, a.err, kDevErrTimeoutMma);
+    }
+  } else {
+    // ------------------------------------------------------------- epilogue
+    const int q = warp & 3;
+    const int row = q * 32 + lane;
+    int buf = 0;
+    uint32_t acc_ph = 0;
+    for (int tile = blockIdx.x; tile < a.total_tiles; tile += gridDim.x) {
+      const int b = tile / tiles_per_batch;
+      const int rem = tile - b * tiles_per_batch;
+      const int mt = rem / a.n_tiles;
+      const int nt = rem - mt * a.n_tiles;
+      const int m = mt * kTcBM + row;
+      const int n0 = nt * a.BN;
+      // All lanes wait (the tcgen05.ld below is warp-collective).
+      if (!mbar_wait_bounded(accf0 + 8 * buf, acc_ph, a.wait_limit, a.err, kDevErrTimeoutEpilogue)) break;
+      tc_fence_after();
+      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(buf * a.BN);
+      for (int c = 0; c < a.BN / 32; ++c) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(tbase + c * 32, v);
+        tmem_ld_wait();
+        const int n = n0 + c * 32;
+        if (m < a.M && n < a.N) store_chunk(a, v, b, m, n, min(32, a.N - n));
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(acce0 + 8 * buf);
+      if (++buf == 2) {
+        buf = 0;
+        acc_ph ^= 1u;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, a.tmem_cols);
+  }
+}
+
+// Failure-path probe: one thread waits on a barrier nobody completes, with a small limit.
+__global__ void wait_timeout_probe_kernel(long long limit, int* err) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(smem_u32(&bar), 1);
+    fence_mbar_init();
+    mbar_wait_bounded(smem_u32(&bar), 0, limit, err, kDevErrTimeoutProbe);
+  }
+}
+
+}  // namespace b200q

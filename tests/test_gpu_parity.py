@@ -1,0 +1,309 @@
+"""GPU parity tests: every kernel family against the CPU oracle, through the C ABI.
+
+Bar: bit-exact for int32 accumulators and int8 requantized outputs; the fp32 dequantized output
+is compared with a relative tolerance of 1e-5 (it is in fact computed by the same IEEE ops)."""
+from __future__ import annotations
+
+import os
+import subprocess
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle
+from tests.kat import kat_cases, rng_s8
+
+pytestmark = pytest.mark.gpu
+ROOT = Path(__file__).resolve().parents[1]
+FP32_RTOL = 1e-5
+
+
+def _b2q():
+    import my_own_cnn_b200 as b2q
+
+    return b2q
+
+
+def _qparams(kind, zps):
+    b2q = _b2q()
+    if kind == 0:
+        return [b2q.QuantizationParametersU8(int(z) & 0xFF, 0.25) for z in zps]
+    return [b2q.QuantizationParametersS5(int(z), 31, 0.5) for z in zps]
+
+
+# ------------------------------------------------------------------ drop-in (reference API)
+
+def test_dropin_qi32_known_answers(cuda_lib, golden):
+    b2q = _b2q()
+    for kc in kat_cases(golden):
+        dev = torch.device("cuda")
+        x = torch.from_numpy(kc.x.reshape(-1)).to(dev)
+        w = torch.from_numpy(kc.wt.reshape(-1)).to(dev)
+        y = torch.full(kc.y.shape, 0x7EADBEEF, dtype=torch.int32, device=dev)
+        in_qp = b2q.qparams_to_device(_qparams(kc.kind, kc.zp_in))
+        f_qp = b2q.qparams_to_device(_qparams(kc.kind, [kc.zp_f]))
+        qt = b2q.DataType.LinQuantU8 if kc.kind == 0 else b2q.DataType.LinQuantS5
+        p = b2q.Conv2DParams(kc.pad_h, kc.pad_w, kc.stride_h, kc.stride_w, kc.dil_h, kc.dil_w, kc.groups)
+        if kc.blocked:
+            b2q.launch_block_fprop_nhwc_qi32(x, w, y, kc.n, kc.h, kc.w, kc.c, kc.r, kc.s, kc.k,
+                                             b2q.BlockConv2DParams(p, kc.by, kc.bx), in_qp, f_qp, qtype=qt)
+        else:
+            b2q.launch_fprop_nhwc_qi32(x, w, y, kc.n, kc.h, kc.w, kc.c, kc.r, kc.s, kc.k, p, in_qp, f_qp, qtype=qt)
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(y.cpu().numpy(), kc.y, err_msg=kc.name)
+
+
+def test_reference_quant_conv_test_links_and_passes(cuda_lib):
+    """The reference's unmodified quant_conv_test.cu, linked against the shim (no reference kernels)."""
+    binary = ROOT / "oracle" / "_ref" / "quant_conv_test_b200"
+    if not binary.exists():
+        pytest.skip("reference test binary not built (needs the reference sources at build time)")
+    proc = subprocess.run([str(binary)], capture_output=True, text=True, timeout=120)
+    assert proc.returncode == 0, proc.stdout + proc.stderr
+    assert "quant_conv_test passed" in proc.stdout
+
+
+def test_dropin_rejects_null_qparams(cuda_lib):
+    b2q = _b2q()
+    x = torch.zeros(16, device="cuda")
+    y = torch.zeros(16, dtype=torch.int32, device="cuda")
+    with pytest.raises(RuntimeError, match="non-null quantization parameters"):
+        b2q.launch_fprop_nhwc_qi32(x, x, y, 1, 2, 2, 4, 1, 1, 4, b2q.Conv2DParams(0, 0), None, None)
+
+
+def test_bmm_matmul_i32_exact_wraparound(cuda_lib):
+    b2q = _b2q()
+    rng = np.random.default_rng(11)
+    for ta in (0, 1):
+        for tb in (0, 1):
+            for batch, M, N, K in [(1, 1, 1, 1), (2, 17, 19, 13), (3, 64, 70, 33)]:
+                A = rng.integers(-2**31, 2**31, size=(batch, K, M) if ta else (batch, M, K), dtype=np.int64).astype(np.int32)
+                B = rng.integers(-2**31, 2**31, size=(batch, N, K) if tb else (batch, K, N), dtype=np.int64).astype(np.int32)
+                C = torch.empty((batch, M, N), dtype=torch.int32, device="cuda")
+                b2q.bmm_matmul_i32(torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda(), C, batch, M, N, K, ta, tb)
+                torch.cuda.synchronize()
+                np.testing.assert_array_equal(C.cpu().numpy(), oracle.bmm_i32(A, B, batch, M, N, K, ta, tb))
+
+
+# ------------------------------------------------------------------ int8 conv
+
+def _conv_case(n, h, w, c, r, s, k, p, seed, epi_kind="all", groups=1):
+    """Run conv2d_s8 for each epilogue and compare with the oracle; returns the dispatched paths."""
+    b2q = _b2q()
+    x = rng_s8(seed, (n, h, w, c))
+    wt = rng_s8(seed + 1, (k, r, s, c // groups))
+    rng = np.random.default_rng(seed + 2)
+    bias = rng.integers(-2**15, 2**15 + 1, size=k).astype(np.int32)
+    scale = rng.uniform(1e-4, 1e-3, size=k).astype(np.float32)
+    a = oracle.conv_args(n, h, w, c, r, s, k, p.pad_h, p.pad_w, p.stride_h, p.stride_w, p.dilation_h,
+                         p.dilation_w, groups)
+    acc = oracle.conv_s8(a, x, wt, threads=4)
+    xd, wd = torch.from_numpy(x).cuda(), torch.from_numpy(wt).cuda()
+    bd, sd = torch.from_numpy(bias).cuda(), torch.from_numpy(scale).cuda()
+    paths = set()
+    kinds = ["s32", "s8", "relu", "f32"] if epi_kind == "all" else [epi_kind]
+    for kind in kinds:
+        if kind == "s32":
+            y = b2q.conv2d_s8(xd, wd, None, None, p, b2q.Epilogue.int32())
+            torch.cuda.synchronize()
+            np.testing.assert_array_equal(y.cpu().numpy(), acc)
+        elif kind == "s8":
+            y = b2q.conv2d_s8(xd, wd, bd, sd, p, b2q.Epilogue.int8())
+            torch.cuda.synchronize()
+            np.testing.assert_array_equal(y.cpu().numpy(), oracle.requant_s8(acc, bias, scale))
+        elif kind == "relu":
+            y = b2q.conv2d_s8(xd, wd, bd, sd, p, b2q.Epilogue.int8(relu6_q=97))
+            torch.cuda.synchronize()
+            np.testing.assert_array_equal(y.cpu().numpy(), oracle.requant_s8(acc, bias, scale, 0, 0, 97))
+        else:
+            y = b2q.conv2d_s8(xd, wd, bd, sd, p, b2q.Epilogue.fp32())
+            torch.cuda.synchronize()
+            np.testing.assert_allclose(y.cpu().numpy(), oracle.dequant_f32(acc, bias, scale), rtol=FP32_RTOL, atol=0)
+        paths.add(b2q.last_path())
+    return paths
+
+
+@pytest.mark.parametrize("shape", [
+    # n, h, w, c, r, s, k, pad, stride, dil
+    (1, 56, 56, 64, 3, 3, 64, 1, 1, 1),
+    (2, 28, 28, 128, 3, 3, 128, 1, 1, 1),  # ResNet stage-2 3x3
+    (2, 34, 34, 64, 3, 3, 80, 1, 2, 1),    # stride 2, K edge (80 = 64 + 16)
+    (1, 40, 36, 96, 3, 3, 48, 2, 1, 2),    # dilation 2, BK 32 chunks
+    (2, 24, 24, 256, 1, 1, 272, 0, 2, 1),  # 1x1 stride 2 (projection shortcut) through im2col
+    (1, 64, 64, 32, 5, 5, 32, 2, 1, 1),    # 5x5, C = 32
+])
+def test_conv_s8_tcgen05_im2col(cuda_lib, shape):
+    b2q = _b2q()
+    n, h, w, c, r, s, k, pad, st, dil = shape
+    p = b2q.Conv2DParams(pad, pad, st, st, dil, dil, 1)
+    paths = _conv_case(n, h, w, c, r, s, k, p, seed=sum(shape))
+    assert paths == {"tcgen05-im2col"}, paths
+
+
+@pytest.mark.parametrize("shape", [
+    (2, 14, 14, 1024, 256),  # config 4 shape family, small batch
+    (1, 14, 14, 512, 2048),
+    (3, 7, 9, 64, 16),       # M edge (189 rows), tiny N
+    (1, 13, 11, 160, 96),    # BK 32 chunks, N edge
+])
+def test_conv_s8_tcgen05_pointwise(cuda_lib, shape):
+    b2q = _b2q()
+    n, h, w, c, k = shape
+    p = b2q.Conv2DParams(0, 0, 1, 1, 1, 1, 1)
+    paths = _conv_case(n, h, w, c, 1, 1, k, p, seed=sum(shape))
+    assert paths == {"tcgen05-tiled"}, paths
+
+
+@pytest.mark.parametrize("shape,groups,expect", [
+    ((2, 20, 20, 48, 3, 3, 48, 1, 2, 1), 48, "cuda-core-depthwise"),   # depthwise s2
+    ((1, 17, 19, 96, 3, 3, 96, 1, 1, 1), 96, "cuda-core-depthwise"),
+    ((2, 23, 23, 3, 7, 7, 64, 3, 2, 1), 1, "cuda-core-generic"),      # stem C = 3
+    ((1, 12, 12, 24, 1, 1, 40, 0, 1, 1), 1, "cuda-core-generic"),     # C % 32 != 0
+    ((2, 9, 9, 32, 3, 3, 64, 1, 1, 1), 2, "cuda-core-generic"),       # grouped
+    ((1, 8, 8, 64, 3, 3, 64, 1, 1, 1), 1, "cuda-core-generic"),       # tiny tensor (< 128 KiB)
+])
+def test_conv_s8_cuda_core_paths(cuda_lib, shape, groups, expect):
+    b2q = _b2q()
+    n, h, w, c, r, s, k, pad, st, dil = shape
+    p = b2q.Conv2DParams(pad, pad, st, st, dil, dil, groups)
+    paths = _conv_case(n, h, w, c, r, s, k, p, seed=7 + sum(shape), groups=groups)
+    assert paths == {expect}, paths
+
+
+def test_conv_forced_cuda_core_matches_tcgen05(cuda_lib):
+    b2q = _b2q()
+    x = torch.from_numpy(rng_s8(5, (2, 28, 28, 64))).cuda()
+    w = torch.from_numpy(rng_s8(6, (64, 3, 3, 64))).cuda()
+    p = b2q.Conv2DParams()
+    y_tc = b2q.conv2d_s8(x, w, None, None, p, b2q.Epilogue.int32())
+    assert b2q.last_path() == "tcgen05-im2col"
+    b2q.set_path_policy(1)
+    try:
+        y_cc = b2q.conv2d_s8(x, w, None, None, p, b2q.Epilogue.int32())
+        assert b2q.last_path() == "cuda-core-generic"
+    finally:
+        b2q.set_path_policy(0)
+    torch.cuda.synchronize()
+    assert torch.equal(y_tc, y_cc)
+
+
+def test_conv_output_guard_band(cuda_lib):
+    """Nothing is written past the output tensor (4 KiB poisoned tail)."""
+    b2q = _b2q()
+    n, h, w, c, k = 1, 30, 30, 64, 48
+    x = torch.from_numpy(rng_s8(9, (n, h, w, c))).cuda()
+    wt = torch.from_numpy(rng_s8(10, (k, 3, 3, c))).cuda()
+    scale = torch.full((k,), 1e-3, device="cuda")
+    numel = n * h * w * k
+    buf = torch.full((numel + 4096,), 0x5A, dtype=torch.int8, device="cuda")
+    b2q.conv2d_s8_into(buf, x, wt, None, scale, n, h, w, c, 3, 3, k, b2q.Conv2DParams(), b2q.Epilogue.int8())
+    torch.cuda.synchronize()
+    assert b2q.last_path() == "tcgen05-im2col"
+    assert torch.all(buf[numel:] == 0x5A)
+
+
+# ------------------------------------------------------------------ int8 bmm
+
+@pytest.mark.parametrize("ta,tb", [(0, 0), (0, 1), (1, 0), (1, 1)])
+def test_bmm_s8_tcgen05_transposes(cuda_lib, ta, tb):
+    b2q = _b2q()
+    batch, M, N, K = 3, 256, 384, 320
+    A = rng_s8(20 + ta, (batch, K, M) if ta else (batch, M, K))
+    B = rng_s8(30 + tb, (batch, N, K) if tb else (batch, K, N))
+    acc = oracle.bmm_s8(A, B, batch, M, N, K, ta, tb, threads=4)
+    Ad, Bd = torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda()
+    C = b2q.bmm_s8(Ad, Bd, ta, tb, b2q.Epilogue.int32())
+    torch.cuda.synchronize()
+    assert b2q.last_path() == "tcgen05-tiled"
+    np.testing.assert_array_equal(C.cpu().numpy(), acc)
+    scale = np.random.default_rng(3).uniform(1e-4, 1e-3, size=N).astype(np.float32)
+    C8 = b2q.bmm_s8(Ad, Bd, ta, tb, b2q.Epilogue.int8(), col_scale=torch.from_numpy(scale).cuda())
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(C8.cpu().numpy(), oracle.requant_s8(acc, None, scale))
+
+
+@pytest.mark.parametrize("dims", [(1, 1, 1, 1), (2, 17, 19, 13), (2, 100, 36, 48), (1, 130, 64, 200)])
+def test_bmm_s8_edges(cuda_lib, dims):
+    b2q = _b2q()
+    batch, M, N, K = dims
+    for ta in (0, 1):
+        for tb in (0, 1):
+            A = rng_s8(M + ta, (batch, K, M) if ta else (batch, M, K))
+            B = rng_s8(N + tb, (batch, N, K) if tb else (batch, K, N))
+            C = b2q.bmm_s8(torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda(), ta, tb, b2q.Epilogue.int32())
+            torch.cuda.synchronize()
+            np.testing.assert_array_equal(C.cpu().numpy(), oracle.bmm_s8(A, B, batch, M, N, K, ta, tb), err_msg=str((ta, tb)))
+
+
+# ------------------------------------------------------------------ full-size properties
+
+def test_config2_bmm_full_size_sampled(cuda_lib):
+    """BASELINE config 2 at full size (64 x 1024^3, NN): tcgen05 == CUDA-core path bit for bit,
+    and sampled rows equal an int64 numpy product."""
+    b2q = _b2q()
+    from my_own_cnn_b200 import synth
+
+    batch, M, N, K = 64, 1024, 1024, 1024
+    A = synth.fill_s8_uniform(torch.empty((batch, M, K), dtype=torch.int8, device="cuda"), 42, 101)
+    B = synth.fill_s8_uniform(torch.empty((batch, K, N), dtype=torch.int8, device="cuda"), 42, 102)
+    C = b2q.bmm_s8(A, B, 0, 0, b2q.Epilogue.int32())
+    assert b2q.last_path() == "tcgen05-tiled"
+    b2q.set_path_policy(1)
+    try:
+        C2 = b2q.bmm_s8(A, B, 0, 0, b2q.Epilogue.int32())
+    finally:
+        b2q.set_path_policy(0)
+    torch.cuda.synchronize()
+    assert torch.equal(C, C2)
+    for b in (0, 31, 63):
+        Ah = synth.s8_uniform_host(42, 101, -127, 127, b * M * K, M * K).reshape(M, K)
+        Bh = synth.s8_uniform_host(42, 102, -127, 127, b * K * N, K * N).reshape(K, N)
+        rows = [0, 511, 1023]
+        np.testing.assert_array_equal(C[b, rows].cpu().numpy(), Ah[rows].astype(np.int64) @ Bh.astype(np.int64))
+
+
+def test_config4_pointwise_full_batch_sampled_images(cuda_lib):
+    """BASELINE config 4a at full size (b512, 14x14, 1024->2048): sampled images vs the oracle."""
+    b2q = _b2q()
+    from my_own_cnn_b200 import synth
+
+    n, h, w, c, k = 512, 14, 14, 1024, 2048
+    x = synth.fill_s8_uniform(torch.empty((n, h, w, c), dtype=torch.int8, device="cuda"), 42, 401)
+    wt = synth.fill_s8_uniform(torch.empty((k, 1, 1, c), dtype=torch.int8, device="cuda"), 42, 402)
+    bias = synth.fill_i32_uniform(torch.empty(k, dtype=torch.int32, device="cuda"), 42, 403, -2**15, 2**15)
+    scale_h = synth.scales_f32(k, 42, 404)
+    y = b2q.conv2d_s8(x, wt, bias, torch.from_numpy(scale_h).cuda(), b2q.Conv2DParams(0, 0), b2q.Epilogue.int8())
+    torch.cuda.synchronize()
+    assert b2q.last_path() == "tcgen05-tiled"
+    wh = synth.s8_uniform_host(42, 402, -127, 127, 0, k * c).reshape(k, 1, 1, c)
+    bh = synth.i32_uniform_host(42, 403, -2**15, 2**15, 0, k)
+    for img in (0, 257, 511):
+        xh = synth.s8_uniform_host(42, 401, -127, 127, img * h * w * c, h * w * c).reshape(1, h, w, c)
+        acc = oracle.conv_s8(oracle.conv_args(1, h, w, c, 1, 1, k, 0, 0), xh, wh)
+        np.testing.assert_array_equal(y[img:img + 1].cpu().numpy(), oracle.requant_s8(acc, bh, scale_h))
+
+
+# ------------------------------------------------------------------ failure path
+
+def test_bounded_wait_timeout_reports_and_context_survives(cuda_lib):
+    b2q = _b2q()
+    from my_own_cnn_b200 import _lib
+
+    rc = _lib.lib().b200q_selftest_wait_timeout(20000)
+    assert rc == _lib.B200Q_ERR_TIMEOUT
+    assert b"wait ran out" in _lib.lib().b200q_last_error()
+    assert _lib.lib().b200q_device_error() == 0  # cleared
+    # the context is still usable
+    x = torch.from_numpy(rng_s8(1, (1, 8, 8, 64))).cuda()
+    w = torch.from_numpy(rng_s8(2, (16, 1, 1, 64))).cuda()
+    y = b2q.conv2d_s8(x, w, None, None, b2q.Conv2DParams(0, 0), b2q.Epilogue.int32())
+    torch.cuda.synchronize()
+    assert y.shape == (1, 8, 8, 16)
+
+
+def test_no_device_error_after_suite(cuda_lib):
+    from my_own_cnn_b200 import _lib
+
+    assert _lib.lib().b200q_device_error() == 0, _lib.lib().b200q_last_error()
