@@ -1,12 +1,13 @@
 // Persistent, warp-specialised tcgen05 int8 GEMM engine for sm_100a.
 //
-// One CTA per SM, 192 threads:
+// One CTA per SM, 320 threads:
 //   warp 0      TMA producer (one elected lane): A tile (tiled 3-D map, or im2col 4-D map for
 //               convolutions) and B tile into a `stages`-deep shared-memory ring;
 //   warp 1      owns TMEM (alloc/dealloc) and issues tcgen05.mma.kind::i8 from one lane;
 //               accumulators are double-buffered in TMEM (2 x BN columns of int32);
-//   warps 2..5  epilogue: tcgen05.ld of the accumulator rows (warp w reads TMEM lanes
-//               32*(w%4)..+31), fused bias / scale / round / clamp / pack, 16-byte stores.
+//   warps 2..9  epilogue: tcgen05.ld of the accumulator rows (warp w reads TMEM lanes
+//               32*(w%4)..+31; two warps per lane quarter take alternating 32-column chunks),
+//               fused bias / scale / round / clamp / pack, 16-byte stores.
 // The GEMM is C[b][m][n] = sum_k A[b][m][k] * B[b][n][k] with M tile 128, N tile BN, K block BK
 // bytes (= int8 elements).  For a convolution, m = (image, ho, wo), n = output channel,
 // k = (r, s, c) -- the im2col TMA gathers the activation rows directly from NHWC memory, with
@@ -20,7 +21,8 @@
 
 namespace b200q {
 
-constexpr int kTcThreads = 192;
+constexpr int kTcThreads = 320;  // producer warp, MMA warp, 8 epilogue warps
+constexpr int kTcEpiWarps = 8;
 constexpr int kTcBM = 128;
 
 struct TcArgs {
@@ -49,87 +51,105 @@ __device__ __forceinline__ uint32_t kmajor_layout(int bk) {
   return bk == 128 ? 2u : (bk == 64 ? 4u : 6u);  // SWIZZLE_128B / 64B / 32B
 }
 
+// Pack the low bytes of four ints into one word (byte i = value i).
+__device__ __forceinline__ uint32_t pack4_s8(int a, int b, int c, int d) {
+  const uint32_t lo = __byte_perm(static_cast<uint32_t>(a), static_cast<uint32_t>(b), 0x0040);
+  const uint32_t hi = __byte_perm(static_cast<uint32_t>(c), static_cast<uint32_t>(d), 0x0040);
+  return __byte_perm(lo, hi, 0x5410);
+}
+
 // Fused epilogue for one row and 32 consecutive output columns [n, n + valid).
-__device__ __forceinline__ void store_chunk(const TcArgs& a, const uint32_t (&v)[32], int b, int m,
-                                            int n, int valid) {
+// All array indices are compile-time constants after unrolling, so nothing spills to local memory.
+template <int KIND>
+__device__ __forceinline__ void store_chunk(const TcArgs& a, const uint32_t (&v)[32], size_t off, int n,
+                                            int valid) {
   const Epilogue& e = a.epi;
-  const size_t off = static_cast<size_t>(b) * a.batch_stride + static_cast<size_t>(m) * a.ldc + n;
-  int32_t t[32];
-#pragma unroll
-  for (int j = 0; j < 32; ++j) t[j] = static_cast<int32_t>(v[j]);
-  if (e.bias) {
-    if (valid == 32 && a.vec_ok) {
-      const int4* bp = reinterpret_cast<const int4*>(e.bias + n);
-#pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        const int4 bb = __ldg(bp + q);
-        t[4 * q + 0] = static_cast<int32_t>(static_cast<uint32_t>(t[4 * q + 0]) + static_cast<uint32_t>(bb.x));
-        t[4 * q + 1] = static_cast<int32_t>(static_cast<uint32_t>(t[4 * q + 1]) + static_cast<uint32_t>(bb.y));
-        t[4 * q + 2] = static_cast<int32_t>(static_cast<uint32_t>(t[4 * q + 2]) + static_cast<uint32_t>(bb.z));
-        t[4 * q + 3] = static_cast<int32_t>(static_cast<uint32_t>(t[4 * q + 3]) + static_cast<uint32_t>(bb.w));
-      }
-    } else {
-#pragma unroll
-      for (int j = 0; j < 32; ++j)
-        if (j < valid)
-          t[j] = static_cast<int32_t>(static_cast<uint32_t>(t[j]) + static_cast<uint32_t>(__ldg(e.bias + n + j)));
-    }
-  }
-  if (e.out_kind == kOutS32) {
-    int32_t* o = static_cast<int32_t*>(a.out) + off;
-    if (valid == 32 && a.vec_ok) {
-#pragma unroll
-      for (int q = 0; q < 8; ++q)
-        reinterpret_cast<int4*>(o)[q] = make_int4(t[4 * q], t[4 * q + 1], t[4 * q + 2], t[4 * q + 3]);
-    } else {
-      for (int j = 0; j < valid; ++j) o[j] = t[j];
-    }
-    return;
-  }
-  float sc[32];
   if (valid == 32 && a.vec_ok) {
+    const int4* bp = reinterpret_cast<const int4*>(e.bias + n);
     const float4* sp = reinterpret_cast<const float4*>(e.scale + n);
+    uint32_t packed[8];
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
-      const float4 s4 = __ldg(sp + q);
-      sc[4 * q] = s4.x; sc[4 * q + 1] = s4.y; sc[4 * q + 2] = s4.z; sc[4 * q + 3] = s4.w;
+      int t0 = static_cast<int>(v[4 * q + 0]), t1 = static_cast<int>(v[4 * q + 1]);
+      int t2 = static_cast<int>(v[4 * q + 2]), t3 = static_cast<int>(v[4 * q + 3]);
+      if (e.bias) {
+        const int4 bb = __ldg(bp + q);
+        t0 = wrap_add(t0, bb.x); t1 = wrap_add(t1, bb.y); t2 = wrap_add(t2, bb.z); t3 = wrap_add(t3, bb.w);
+      }
+      if constexpr (KIND == kOutS32) {
+        reinterpret_cast<int4*>(static_cast<int32_t*>(a.out) + off)[q] = make_int4(t0, t1, t2, t3);
+      } else {
+        const float4 s4 = __ldg(sp + q);
+        if constexpr (KIND == kOutF32) {
+          reinterpret_cast<float4*>(static_cast<float*>(a.out) + off)[q] =
+              make_float4(__fmul_rn(__int2float_rn(t0), s4.x), __fmul_rn(__int2float_rn(t1), s4.y),
+                          __fmul_rn(__int2float_rn(t2), s4.z), __fmul_rn(__int2float_rn(t3), s4.w));
+        } else {
+          packed[q] = pack4_s8(requant_one(t0, s4.x, e), requant_one(t1, s4.y, e), requant_one(t2, s4.z, e),
+                               requant_one(t3, s4.w, e));
+        }
+      }
     }
-  } else {
-#pragma unroll
-    for (int j = 0; j < 32; ++j) sc[j] = (j < valid) ? __ldg(e.scale + n + j) : 0.0f;
-  }
-  if (e.out_kind == kOutF32) {
-    float* o = static_cast<float*>(a.out) + off;
-    float f[32];
-#pragma unroll
-    for (int j = 0; j < 32; ++j) f[j] = __fmul_rn(__int2float_rn(t[j]), sc[j]);
-    if (valid == 32 && a.vec_ok) {
-#pragma unroll
-      for (int q = 0; q < 8; ++q)
-        reinterpret_cast<float4*>(o)[q] = make_float4(f[4 * q], f[4 * q + 1], f[4 * q + 2], f[4 * q + 3]);
-    } else {
-      for (int j = 0; j < valid; ++j) o[j] = f[j];
+    if constexpr (KIND == kOutS8) {
+      int4* o = reinterpret_cast<int4*>(static_cast<int8_t*>(a.out) + off);
+      o[0] = make_int4(packed[0], packed[1], packed[2], packed[3]);
+      o[1] = make_int4(packed[4], packed[5], packed[6], packed[7]);
     }
     return;
   }
-  // int8 requantization
-  uint32_t packed[8];
 #pragma unroll
-  for (int q = 0; q < 8; ++q) {
-    uint32_t w = 0;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int code = requant_one(t[4 * q + i], sc[4 * q + i], e);
-      w |= (static_cast<uint32_t>(code) & 0xFFu) << (8 * i);
+  for (int j = 0; j < 32; ++j) {
+    if (j < valid) {
+      int t = static_cast<int>(v[j]);
+      if (e.bias) t = wrap_add(t, __ldg(e.bias + n + j));
+      if constexpr (KIND == kOutS32) {
+        static_cast<int32_t*>(a.out)[off + j] = t;
+      } else if constexpr (KIND == kOutF32) {
+        static_cast<float*>(a.out)[off + j] = __fmul_rn(__int2float_rn(t), __ldg(e.scale + n + j));
+      } else {
+        static_cast<int8_t*>(a.out)[off + j] = static_cast<int8_t>(requant_one(t, __ldg(e.scale + n + j), e));
+      }
     }
-    packed[q] = w;
   }
-  int8_t* o = static_cast<int8_t*>(a.out) + off;
-  if (valid == 32 && a.vec_ok) {
-    reinterpret_cast<int4*>(o)[0] = make_int4(packed[0], packed[1], packed[2], packed[3]);
-    reinterpret_cast<int4*>(o)[1] = make_int4(packed[4], packed[5], packed[6], packed[7]);
-  } else {
-    for (int j = 0; j < valid; ++j) o[j] = static_cast<int8_t>((packed[j >> 2] >> (8 * (j & 3))) & 0xFFu);
+}
+
+// Epilogue role: 8 warps; warp w reads TMEM lanes 32*(w%4)..+31 (the hardware restricts a warp
+// to the lane quarter w%4) and the chunks of 32 columns with chunk % 2 == (w-2)/4.
+template <int KIND>
+__device__ __forceinline__ void epilogue_role(const TcArgs& a, uint32_t tmem_base, uint32_t accf0, uint32_t acce0,
+                                              int warp, int lane) {
+  const int q = warp & 3;
+  const int half = (warp - 2) >> 2;
+  const int row = q * 32 + lane;
+  const int tiles_per_batch = a.m_tiles * a.n_tiles;
+  const int nchunks = a.BN / 32;
+  int buf = 0;
+  uint32_t acc_ph = 0;
+  for (int tile = blockIdx.x; tile < a.total_tiles; tile += gridDim.x) {
+    const int b = tile / tiles_per_batch;
+    const int rem = tile - b * tiles_per_batch;
+    const int mt = rem / a.n_tiles;
+    const int nt = rem - mt * a.n_tiles;
+    const int m = mt * kTcBM + row;
+    const int n0 = nt * a.BN;
+    if (!mbar_wait_bounded(accf0 + 8 * buf, acc_ph, a.wait_limit, a.err, kDevErrTimeoutEpilogue)) break;
+    tc_fence_after();
+    const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(buf * a.BN);
+    const size_t row_off = static_cast<size_t>(b) * a.batch_stride + static_cast<size_t>(m) * a.ldc;
+    for (int c = half; c < nchunks; c += 2) {
+      uint32_t v[32];
+      tmem_ld_32x32b_x32(tbase + c * 32, v);
+      tmem_ld_wait();
+      const int n = n0 + c * 32;
+      if (m < a.M && n < a.N) store_chunk<KIND>(a, v, row_off + n, n, min(32, a.N - n));
+    }
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(acce0 + 8 * buf);
+    if (++buf == 2) {
+      buf = 0;
+      acc_ph ^= 1u;
+    }
   }
 }
 
@@ -161,7 +181,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(accf0 + 8 * i, 1);
-      mbar_init(acce0 + 8 * i, 4);
+      mbar_init(acce0 + 8 * i, kTcEpiWarps);
     }
     mbar_init(drain, 1);
     fence_mbar_init();
@@ -302,36 +322,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
   } else {
     // ------------------------------------------------------------- epilogue
-    const int q = warp & 3;
-    const int row = q * 32 + lane;
-    int buf = 0;
-    uint32_t acc_ph = 0;
-    for (int tile = blockIdx.x; tile < a.total_tiles; tile += gridDim.x) {
-      const int b = tile / tiles_per_batch;
-      const int rem = tile - b * tiles_per_batch;
-      const int mt = rem / a.n_tiles;
-      const int nt = rem - mt * a.n_tiles;
-      const int m = mt * kTcBM + row;
-      const int n0 = nt * a.BN;
-      // All lanes wait (the tcgen05.ld below is warp-collective).
-      if (!mbar_wait_bounded(accf0 + 8 * buf, acc_ph, a.wait_limit, a.err, kDevErrTimeoutEpilogue)) break;
-      tc_fence_after();
-      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(buf * a.BN);
-      for (int c = 0; c < a.BN / 32; ++c) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(tbase + c * 32, v);
-        tmem_ld_wait();
-        const int n = n0 + c * 32;
-        if (m < a.M && n < a.N) store_chunk(a, v, b, m, n, min(32, a.N - n));
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(acce0 + 8 * buf);
-      if (++buf == 2) {
-        buf = 0;
-        acc_ph ^= 1u;
-      }
-    }
+    if (a.epi.out_kind == kOutS8)
+      epilogue_role<kOutS8>(a, tmem_base, accf0, acce0, warp, lane);
+    else if (a.epi.out_kind == kOutS32)
+      epilogue_role<kOutS32>(a, tmem_base, accf0, acce0, warp, lane);
+    else
+      epilogue_role<kOutF32>(a, tmem_base, accf0, acce0, warp, lane);
   }
 
   tc_fence_before();

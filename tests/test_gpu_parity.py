@@ -174,7 +174,7 @@ def test_conv_s8_cuda_core_paths(cuda_lib, shape, groups, expect):
 
 def test_conv_forced_cuda_core_matches_tcgen05(cuda_lib):
     b2q = _b2q()
-    x = torch.from_numpy(rng_s8(5, (2, 28, 28, 64))).cuda()
+    x = torch.from_numpy(rng_s8(5, (2, 32, 32, 64))).cuda()
     w = torch.from_numpy(rng_s8(6, (64, 3, 3, 64))).cuda()
     p = b2q.Conv2DParams()
     y_tc = b2q.conv2d_s8(x, w, None, None, p, b2q.Epilogue.int32())
@@ -192,7 +192,7 @@ def test_conv_forced_cuda_core_matches_tcgen05(cuda_lib):
 def test_conv_output_guard_band(cuda_lib):
     """Nothing is written past the output tensor (4 KiB poisoned tail)."""
     b2q = _b2q()
-    n, h, w, c, k = 1, 30, 30, 64, 48
+    n, h, w, c, k = 1, 48, 48, 64, 48
     x = torch.from_numpy(rng_s8(9, (n, h, w, c))).cuda()
     wt = torch.from_numpy(rng_s8(10, (k, 3, 3, c))).cuda()
     scale = torch.full((k,), 1e-3, device="cuda")
