@@ -195,7 +195,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem_base = *tmem_slot;
+  // Broadcast from lane 0 so the compiler treats the TMEM base as warp-uniform.
+  const uint32_t tmem_base = __shfl_sync(0xFFFFFFFFu, *tmem_slot, 0);
   const int tiles_per_batch = a.m_tiles * a.n_tiles;
 
   if (warp == 0) {
@@ -267,8 +268,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
+    {
       // ----------------------------------------------------------------- MMA
+      // The whole warp runs the loop converged; an elected lane issues each tcgen05 instruction.
       int stage = 0;
       uint32_t ph = 0;
       int buf = 0;
@@ -283,41 +285,46 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const uint32_t a_step = a.a_major == 0 ? 32u : 4096u;  // bytes per K=32 slice
       const uint32_t b_step = a.b_major == 0 ? 32u : 4096u;
       const int ksteps = a.BK / 32;
+      // Stage-0 descriptors; stage / K-slice offsets are added to the 14-bit start-address field
+      // (shared addresses stay below 256 KiB, so the add never carries out of the field).
+      const uint64_t a_desc0 = make_smem_desc(smem_u32(sA), a_lbo, a_sbo, a_layout);
+      const uint64_t b_desc0 = make_smem_desc(smem_u32(sB), b_lbo, b_sbo, b_layout);
       for (int tile = blockIdx.x; tile < a.total_tiles && ok; tile += gridDim.x) {
-        if (!mbar_wait_bounded(acce0 + 8 * buf, acc_ph ^ 1u, a.wait_limit, a.err, kDevErrTimeoutMma)) {
+        if (!__all_sync(0xFFFFFFFFu,
+                        mbar_wait_bounded(acce0 + 8 * buf, acc_ph ^ 1u, a.wait_limit, a.err, kDevErrTimeoutMma))) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * a.BN);
         for (int kb = 0; kb < a.num_kb; ++kb) {
-          if (!mbar_wait_bounded(full0 + 8 * stage, ph, a.wait_limit, a.err, kDevErrTimeoutMma)) {
+          // The TMA completion on the mbarrier orders the tiles for the tensor core; a tcgen05
+          // fence per stage is not needed.
+          if (!__all_sync(0xFFFFFFFFu,
+                          mbar_wait_bounded(full0 + 8 * stage, ph, a.wait_limit, a.err, kDevErrTimeoutMma))) {
             ok = false;
             break;
           }
-          tc_fence_after();
-          const uint32_t aB = smem_u32(sA + stage * stage_a);
-          const uint32_t bB = smem_u32(sB + stage * stage_b);
-          for (int j = 0; j < ksteps; ++j) {
-            const uint64_t ad = make_smem_desc(aB + j * a_step, a_lbo, a_sbo, a_layout);
-            const uint64_t bd = make_smem_desc(bB + j * b_step, b_lbo, b_sbo, b_layout);
-            tc_mma_i8(d_tmem, ad, bd, a.idesc, (kb | j) != 0 ? 1u : 0u);
-          }
-          tc_commit(empty0 + 8 * stage);
+          const uint64_t ad_s = a_desc0 + ((stage * stage_a) >> 4);
+          const uint64_t bd_s = b_desc0 + ((stage * stage_b) >> 4);
+          for (int j = 0; j < ksteps; ++j)
+            tc_mma_i8_elect(d_tmem, ad_s + ((j * a_step) >> 4), bd_s + ((j * b_step) >> 4), a.idesc,
+                            (kb | j) != 0 ? 1u : 0u);
+          tc_commit_elect(empty0 + 8 * stage);
           if (++stage == a.stages) {
             stage = 0;
             ph ^= 1u;
           }
         }
         if (!ok) break;
-        tc_commit(accf0 + 8 * buf);
+        tc_commit_elect(accf0 + 8 * buf);
         if (++buf == 2) {
           buf = 0;
           acc_ph ^= 1u;
         }
       }
-      // Wait for every MMA issued by this thread before TMEM is released.
-      tc_commit(drain);
+      // Wait for every MMA issued by this warp before TMEM is released.
+      tc_commit_elect(drain);
       mbar_wait_bounded(drain, 0, a.wait_limit, a.err, kDevErrTimeoutMma);
     }
   } else {
