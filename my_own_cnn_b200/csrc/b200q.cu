@@ -194,7 +194,11 @@ int pick_bn(int n, int mn_major_b) {
 
 int launch_tc(const DeviceState& st, const CUtensorMap& ma, const CUtensorMap& mb, TcArgs a, cudaStream_t stream) {
   const int stage_bytes = kTcBM * a.BK + a.BN * a.BK;
-  int stages = (kSmemLimit - kSmemReserve) / stage_bytes;
+  // Stage per-column bias / scale in shared memory when they fit (4096 columns = 32 KiB).
+  a.stage_cols = (a.epi.out_kind != kOutS32 || a.epi.bias) && a.N <= 4096 ? (a.N + 31) / 32 * 32 : 0;
+  a.default_clamp = a.epi.out_kind == kOutS8 && a.epi.zp == 0 && a.epi.lo == -128 && a.epi.hi == 127;
+  const int epi_bytes = a.stage_cols * 8;
+  int stages = (kSmemLimit - kSmemReserve - epi_bytes) / stage_bytes;
   if (stages > 8) stages = 8;
   if (stages < 2) return fail(B200Q_ERR_UNSUPPORTED, "tile does not fit shared memory");
   a.stages = stages;
@@ -213,7 +217,7 @@ int launch_tc(const DeviceState& st, const CUtensorMap& ma, const CUtensorMap& m
   a.wait_limit = wait_limit();
   a.err = st.err;
   const int grid = a.total_tiles < st.sms ? a.total_tiles : st.sms;
-  const size_t smem = static_cast<size_t>(stages) * stage_bytes + kSmemReserve;
+  const size_t smem = static_cast<size_t>(stages) * stage_bytes + kSmemReserve + epi_bytes;
   tc_gemm_s8_kernel<<<grid, kTcThreads, smem, stream>>>(ma, mb, a);
   g_tc_launches.fetch_add(1, std::memory_order_relaxed);
   return check_launch("tc_gemm_s8_kernel launch");

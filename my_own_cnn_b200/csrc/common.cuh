@@ -24,14 +24,13 @@ struct Epilogue {
 };
 
 // Requantize one int32 value (bias already added, wrapping):
-//   p = (float)t * scale   (both IEEE round-to-nearest-even, no contraction)
-//   q = rint(clamp(p, lo - zp, hi - zp)) + zp   (half to even)
-// Clamping before the float->int conversion keeps the conversion in range; it gives the same
-// code as rounding first, because the bounds are integers.
+//   p = (float)t * scale          (both IEEE round-to-nearest-even, no contraction)
+//   r = rint_sat(p)               (cvt.rni.s32.f32: half to even, saturating, NaN -> 0)
+//   q = clamp(r, lo - zp, hi - zp) + zp
+// The bounds are integers, so clamping after rounding equals rounding after clamping.
 __device__ __forceinline__ int requant_one(int32_t t, float sc, const Epilogue& e) {
-  float p = __fmul_rn(__int2float_rn(t), sc);
-  p = fminf(fmaxf(p, static_cast<float>(e.lo - e.zp)), static_cast<float>(e.hi - e.zp));
-  return __float2int_rn(p) + e.zp;
+  const int r = __float2int_rn(__fmul_rn(__int2float_rn(t), sc));
+  return min(max(r, e.lo - e.zp), e.hi - e.zp) + e.zp;
 }
 
 __device__ __forceinline__ int32_t wrap_add(int32_t a, int32_t b) {

@@ -45,6 +45,8 @@ struct TcArgs {
   uint32_t tmem_cols;
   long long wait_limit;
   int* err;
+  int stage_cols;     // bias/scale columns copied to shared memory at start (0 = read from global)
+  int default_clamp;  // int8 output with zp 0 and bounds [-128, 127]: saturating pack does the clamp
 };
 
 __device__ __forceinline__ uint32_t kmajor_layout(int bk) {
@@ -57,36 +59,52 @@ __device__ __forceinline__ uint32_t pack4_s8(int a, int b, int c, int d) {
   const uint32_t hi = __byte_perm(static_cast<uint32_t>(c), static_cast<uint32_t>(d), 0x0040);
   return __byte_perm(lo, hi, 0x5410);
 }
+// Pack four int32 into int8 bytes (byte i = value i) with saturation to [-128, 127].
+__device__ __forceinline__ uint32_t pack4_sat_s8(int a, int b, int c, int d) {
+  uint32_t out;
+  asm("{\n\t.reg .b32 hi;\n\t"
+      "cvt.pack.sat.s8.s32.b32 hi, %4, %3, 0;\n\t"
+      "cvt.pack.sat.s8.s32.b32 %0, %2, %1, hi;\n\t}"
+      : "=r"(out)
+      : "r"(a), "r"(b), "r"(c), "r"(d));
+  return out;
+}
 
 // Fused epilogue for one row and 32 consecutive output columns [n, n + valid).
-// All array indices are compile-time constants after unrolling, so nothing spills to local memory.
+// bias / scale point at shared memory (staged) or global memory; bias may be null.
+// All array indices are compile-time constants after unrolling: nothing spills to local memory.
 template <int KIND>
-__device__ __forceinline__ void store_chunk(const TcArgs& a, const uint32_t (&v)[32], size_t off, int n,
-                                            int valid) {
+__device__ __forceinline__ void store_chunk(const TcArgs& a, const uint32_t (&v)[32], size_t off, int n, int valid,
+                                            const int32_t* bias, const float* scale) {
   const Epilogue& e = a.epi;
   if (valid == 32 && a.vec_ok) {
-    const int4* bp = reinterpret_cast<const int4*>(e.bias + n);
-    const float4* sp = reinterpret_cast<const float4*>(e.scale + n);
+    const int4* bp = reinterpret_cast<const int4*>(bias + n);
+    const float4* sp = reinterpret_cast<const float4*>(scale + n);
     uint32_t packed[8];
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
       int t0 = static_cast<int>(v[4 * q + 0]), t1 = static_cast<int>(v[4 * q + 1]);
       int t2 = static_cast<int>(v[4 * q + 2]), t3 = static_cast<int>(v[4 * q + 3]);
-      if (e.bias) {
-        const int4 bb = __ldg(bp + q);
+      if (bias) {
+        const int4 bb = bp[q];
         t0 = wrap_add(t0, bb.x); t1 = wrap_add(t1, bb.y); t2 = wrap_add(t2, bb.z); t3 = wrap_add(t3, bb.w);
       }
       if constexpr (KIND == kOutS32) {
         reinterpret_cast<int4*>(static_cast<int32_t*>(a.out) + off)[q] = make_int4(t0, t1, t2, t3);
       } else {
-        const float4 s4 = __ldg(sp + q);
+        const float4 s4 = sp[q];
+        const float p0 = __fmul_rn(__int2float_rn(t0), s4.x), p1 = __fmul_rn(__int2float_rn(t1), s4.y);
+        const float p2 = __fmul_rn(__int2float_rn(t2), s4.z), p3 = __fmul_rn(__int2float_rn(t3), s4.w);
         if constexpr (KIND == kOutF32) {
-          reinterpret_cast<float4*>(static_cast<float*>(a.out) + off)[q] =
-              make_float4(__fmul_rn(__int2float_rn(t0), s4.x), __fmul_rn(__int2float_rn(t1), s4.y),
-                          __fmul_rn(__int2float_rn(t2), s4.z), __fmul_rn(__int2float_rn(t3), s4.w));
+          reinterpret_cast<float4*>(static_cast<float*>(a.out) + off)[q] = make_float4(p0, p1, p2, p3);
         } else {
-          packed[q] = pack4_s8(requant_one(t0, s4.x, e), requant_one(t1, s4.y, e), requant_one(t2, s4.z, e),
-                               requant_one(t3, s4.w, e));
+          int r0 = __float2int_rn(p0), r1 = __float2int_rn(p1), r2 = __float2int_rn(p2), r3 = __float2int_rn(p3);
+          if (!a.default_clamp) {
+            const int lo = e.lo - e.zp, hi = e.hi - e.zp;
+            r0 = min(max(r0, lo), hi) + e.zp; r1 = min(max(r1, lo), hi) + e.zp;
+            r2 = min(max(r2, lo), hi) + e.zp; r3 = min(max(r3, lo), hi) + e.zp;
+          }
+          packed[q] = pack4_sat_s8(r0, r1, r2, r3);
         }
       }
     }
@@ -101,28 +119,29 @@ __device__ __forceinline__ void store_chunk(const TcArgs& a, const uint32_t (&v)
   for (int j = 0; j < 32; ++j) {
     if (j < valid) {
       int t = static_cast<int>(v[j]);
-      if (e.bias) t = wrap_add(t, __ldg(e.bias + n + j));
+      if (bias) t = wrap_add(t, bias[n + j]);
       if constexpr (KIND == kOutS32) {
         static_cast<int32_t*>(a.out)[off + j] = t;
       } else if constexpr (KIND == kOutF32) {
-        static_cast<float*>(a.out)[off + j] = __fmul_rn(__int2float_rn(t), __ldg(e.scale + n + j));
+        static_cast<float*>(a.out)[off + j] = __fmul_rn(__int2float_rn(t), scale[n + j]);
       } else {
-        static_cast<int8_t*>(a.out)[off + j] = static_cast<int8_t>(requant_one(t, __ldg(e.scale + n + j), e));
+        static_cast<int8_t*>(a.out)[off + j] = static_cast<int8_t>(requant_one(t, scale[n + j], e));
       }
     }
   }
 }
 
 // Epilogue role: 8 warps; warp w reads TMEM lanes 32*(w%4)..+31 (the hardware restricts a warp
-// to the lane quarter w%4) and the chunks of 32 columns with chunk % 2 == (w-2)/4.
+// to the lane quarter w%4) and the chunks of 32 columns with chunk % 2 == (w-2)/4.  The TMEM load
+// of the next chunk is issued before the current chunk is processed (two register buffers).
 template <int KIND>
 __device__ __forceinline__ void epilogue_role(const TcArgs& a, uint32_t tmem_base, uint32_t accf0, uint32_t acce0,
-                                              int warp, int lane) {
+                                              int warp, int lane, const int32_t* bias, const float* scale) {
   const int q = warp & 3;
   const int half = (warp - 2) >> 2;
   const int row = q * 32 + lane;
   const int tiles_per_batch = a.m_tiles * a.n_tiles;
-  const int nchunks = a.BN / 32;
+  const int nmine = (a.BN / 32 - half + 1) / 2;  // chunks half, half+2, ...
   int buf = 0;
   uint32_t acc_ph = 0;
   for (int tile = blockIdx.x; tile < a.total_tiles; tile += gridDim.x) {
@@ -136,12 +155,23 @@ __device__ __forceinline__ void epilogue_role(const TcArgs& a, uint32_t tmem_bas
     tc_fence_after();
     const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(buf * a.BN);
     const size_t row_off = static_cast<size_t>(b) * a.batch_stride + static_cast<size_t>(m) * a.ldc;
-    for (int c = half; c < nchunks; c += 2) {
-      uint32_t v[32];
-      tmem_ld_32x32b_x32(tbase + c * 32, v);
+    uint32_t va[32], vb[32];
+    tmem_ld_32x32b_x32(tbase + half * 32, va);
+    tmem_ld_wait();
+    for (int i = 0; i < nmine; i += 2) {
+      const int ca = half + 2 * i, cb = ca + 2;
+      if (i + 1 < nmine) tmem_ld_32x32b_x32(tbase + cb * 32, vb);
+      {
+        const int n = n0 + ca * 32;
+        if (m < a.M && n < a.N) store_chunk<KIND>(a, va, row_off + n, n, min(32, a.N - n), bias, scale);
+      }
       tmem_ld_wait();
-      const int n = n0 + c * 32;
-      if (m < a.M && n < a.N) store_chunk<KIND>(a, v, row_off + n, n, min(32, a.N - n));
+      if (i + 1 < nmine) {
+        if (i + 2 < nmine) tmem_ld_32x32b_x32(tbase + (cb + 2) * 32, va);
+        const int n = n0 + cb * 32;
+        if (m < a.M && n < a.N) store_chunk<KIND>(a, vb, row_off + n, n, min(32, a.N - n), bias, scale);
+        tmem_ld_wait();
+      }
     }
     tc_fence_before();
     __syncwarp();
@@ -170,6 +200,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const uint32_t acce0 = smem_u32(bars + 2 * a.stages + 2);
   const uint32_t drain = smem_u32(bars + 2 * a.stages + 4);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * a.stages + 5);
+  // bias[stage_cols] then scale[stage_cols], 16-byte aligned, after the barriers
+  int32_t* s_bias = reinterpret_cast<int32_t*>(bars + 2 * a.stages + 6);
+  float* s_scale = reinterpret_cast<float*>(s_bias + a.stage_cols);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -329,12 +362,24 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
   } else {
     // ------------------------------------------------------------- epilogue
+    const int32_t* bias = a.epi.bias;
+    const float* scale = a.epi.scale;
+    if (a.stage_cols > 0) {
+      // Copy the per-column bias / scale into shared memory once per CTA (epilogue warps only).
+      for (int i = threadIdx.x - 64; i < a.stage_cols; i += kTcEpiWarps * 32) {
+        s_bias[i] = (a.epi.bias && i < a.N) ? __ldg(a.epi.bias + i) : 0;
+        s_scale[i] = (a.epi.scale && i < a.N) ? __ldg(a.epi.scale + i) : 0.0f;
+      }
+      asm volatile("bar.sync 1, %0;" ::"n"(kTcEpiWarps * 32) : "memory");
+      bias = a.epi.bias ? s_bias : nullptr;
+      scale = s_scale;
+    }
     if (a.epi.out_kind == kOutS8)
-      epilogue_role<kOutS8>(a, tmem_base, accf0, acce0, warp, lane);
+      epilogue_role<kOutS8>(a, tmem_base, accf0, acce0, warp, lane, bias, scale);
     else if (a.epi.out_kind == kOutS32)
-      epilogue_role<kOutS32>(a, tmem_base, accf0, acce0, warp, lane);
+      epilogue_role<kOutS32>(a, tmem_base, accf0, acce0, warp, lane, bias, scale);
     else
-      epilogue_role<kOutF32>(a, tmem_base, accf0, acce0, warp, lane);
+      epilogue_role<kOutF32>(a, tmem_base, accf0, acce0, warp, lane, bias, scale);
   }
 
   tc_fence_before();

@@ -16,8 +16,8 @@
  *       t = acc + bias[k]            (int32, wrapping)
  *       f = (float)t                 (round to nearest even)
  *       p = f * scale[k]             (one fp32 multiply, no contraction)
- *       p = clamp(p, lo - zp, hi - zp)
- *       q = rint(p) + zp             (round half to even)
+ *       r = rint_sat(p)              (round half to even, saturated to int32, NaN -> 0)
+ *       q = clamp(r, lo - zp, hi - zp) + zp
  *     and the dequantized fp32 output  y = (float)(acc + bias[k]) * scale[k].
  *   - a counter-based splitmix64 generator that the CUDA library implements
  *     identically, so any slice of a synthetic tensor can be regenerated here.
@@ -199,18 +199,26 @@ int orc_conv_s8(const orc_conv_t* p, const int8_t* x, const int8_t* w, int32_t* 
 
 /* ------------------------------------------------------------- epilogue */
 
+/* float -> int32, round half to even, saturating, NaN -> 0 (the PTX cvt.rni.s32.f32 rule). */
+static int32_t rint_sat(float p) {
+  if (p != p) return 0;
+  if (p >= 2147483648.0f) return INT32_MAX;
+  if (p < -2147483648.0f) return INT32_MIN;
+  return (int32_t)nearbyintf(p);
+}
+
 /* Requantize int32 accumulators [rows][k] to int8 codes.  bias may be NULL (0). */
 void orc_requant_s8(const int32_t* acc, size_t rows, int k, const int32_t* bias, const float* scale,
                     int zp, int lo, int hi, int8_t* out) {
-  const float flo = (float)(lo - zp), fhi = (float)(hi - zp);
   for (size_t i = 0; i < rows; ++i)
     for (int j = 0; j < k; ++j) {
       const uint32_t t = (uint32_t)acc[i * k + j] + (uint32_t)(bias ? bias[j] : 0);
       const float f = (float)(int32_t)t;
-      float pr = f * scale[j];
-      pr = fminf(fmaxf(pr, flo), fhi);
-      const int q = (int)nearbyintf(pr) + zp;
-      out[i * k + j] = (int8_t)q;
+      const float pr = f * scale[j];
+      int32_t r = rint_sat(pr);
+      if (r < lo - zp) r = lo - zp;
+      if (r > hi - zp) r = hi - zp;
+      out[i * k + j] = (int8_t)(r + zp);
     }
 }
 

@@ -69,6 +69,16 @@ def test_requant_round_half_even_and_clamp():
     np.testing.assert_array_equal(q2, expect2)
 
 
+def test_requant_nonfinite_rules():
+    # rint_sat: NaN -> 0 before the clamp; +-inf and huge values saturate to the bounds
+    acc = np.array([[0, 5, -5, 2**30]], dtype=np.int32)
+    scale = np.array([np.inf, np.inf, np.inf, 1e30], dtype=np.float32)
+    q = oracle.requant_s8(acc, None, scale)
+    np.testing.assert_array_equal(q, np.array([[0, 127, -128, 127]], dtype=np.int8))
+    q2 = oracle.requant_s8(acc, None, scale, zp=0, lo=3, hi=9)
+    np.testing.assert_array_equal(q2, np.array([[3, 9, 3, 9]], dtype=np.int8))
+
+
 def test_requant_bias_wraps_int32():
     acc = np.array([[2**31 - 1]], dtype=np.int32)
     q = oracle.dequant_f32(acc, np.array([1], np.int32), np.array([1.0], np.float32))
