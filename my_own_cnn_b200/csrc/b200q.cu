@@ -165,6 +165,19 @@ int encode_tiled_3d(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1
   return B200Q_OK;
 }
 
+// Output map for 4-byte results: dims {N, M, batch} (int32 elements), box {32, 32, 1}, 128B swizzle.
+int encode_out_4b(CUtensorMap* map, void* base, uint64_t n, uint64_t m, uint64_t batch) {
+  cuuint64_t dims[3] = {n, m, batch};
+  cuuint64_t strides[2] = {n * 4, n * m * 4};
+  cuuint32_t box[3] = {32, 32, 1};
+  cuuint32_t es[3] = {1, 1, 1};
+  CUresult r = g_encode_tiled(map, CU_TENSOR_MAP_DATA_TYPE_INT32, 3, base, dims, strides, box, es,
+                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                              CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(B200Q_ERR_CUDA, "cuTensorMapEncodeTiled (output) failed (%d)", (int)r);
+  return B200Q_OK;
+}
+
 int encode_im2col(CUtensorMap* map, const int8_t* x, const ConvGeom& g, int bk) {
   cuuint64_t dims[4] = {(cuuint64_t)g.c, (cuuint64_t)g.w, (cuuint64_t)g.h, (cuuint64_t)g.n};
   cuuint64_t strides[3] = {(cuuint64_t)g.c, (cuuint64_t)g.c * g.w, (cuuint64_t)g.c * g.w * g.h};
@@ -193,11 +206,20 @@ int pick_bn(int n, int mn_major_b) {
 }
 
 int launch_tc(const DeviceState& st, const CUtensorMap& ma, const CUtensorMap& mb, TcArgs a, cudaStream_t stream) {
+  // 4-byte outputs go through shared memory and TMA stores when the row pitch allows a tensor map.
+  CUtensorMap mc = ma;  // unused placeholder when tma_store == 0
+  a.tma_store = 0;
+  if (a.epi.out_kind != kOutS8 && a.ldc == a.N && a.N % 4 == 0 && aligned16(a.out)) {
+    const uint64_t rows = a.batch_stride ? static_cast<uint64_t>(a.M) : static_cast<uint64_t>(a.M);
+    int rc = encode_out_4b(&mc, a.out, static_cast<uint64_t>(a.N), rows, static_cast<uint64_t>(a.batch));
+    if (rc) return rc;
+    a.tma_store = 1;
+  }
   const int stage_bytes = kTcBM * a.BK + a.BN * a.BK;
   // Stage per-column bias / scale in shared memory when they fit (4096 columns = 32 KiB).
   a.stage_cols = (a.epi.out_kind != kOutS32 || a.epi.bias) && a.N <= 4096 ? (a.N + 31) / 32 * 32 : 0;
   a.default_clamp = a.epi.out_kind == kOutS8 && a.epi.zp == 0 && a.epi.lo == -128 && a.epi.hi == 127;
-  const int epi_bytes = a.stage_cols * 8;
+  const int epi_bytes = a.stage_cols * 8 + (a.tma_store ? 1024 + kTcEpiWarps * 2 * kEpiStageBytes : 0);
   int stages = (kSmemLimit - kSmemReserve - epi_bytes) / stage_bytes;
   if (stages > 8) stages = 8;
   if (stages < 2) return fail(B200Q_ERR_UNSUPPORTED, "tile does not fit shared memory");
@@ -218,7 +240,7 @@ int launch_tc(const DeviceState& st, const CUtensorMap& ma, const CUtensorMap& m
   a.err = st.err;
   const int grid = a.total_tiles < st.sms ? a.total_tiles : st.sms;
   const size_t smem = static_cast<size_t>(stages) * stage_bytes + kSmemReserve + epi_bytes;
-  tc_gemm_s8_kernel<<<grid, kTcThreads, smem, stream>>>(ma, mb, a);
+  tc_gemm_s8_kernel<<<grid, kTcThreads, smem, stream>>>(ma, mb, mc, a);
   g_tc_launches.fetch_add(1, std::memory_order_relaxed);
   return check_launch("tc_gemm_s8_kernel launch");
 }

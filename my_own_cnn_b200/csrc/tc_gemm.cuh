@@ -47,7 +47,10 @@ struct TcArgs {
   int* err;
   int stage_cols;     // bias/scale columns copied to shared memory at start (0 = read from global)
   int default_clamp;  // int8 output with zp 0 and bounds [-128, 127]: saturating pack does the clamp
+  int tma_store;      // 4-byte outputs leave through shared memory + TMA tensor stores (map tmC)
 };
+
+constexpr int kEpiStageBytes = 32 * 128;  // one warp's 32 rows x 32 four-byte columns
 
 __device__ __forceinline__ uint32_t kmajor_layout(int bk) {
   return bk == 128 ? 2u : (bk == 64 ? 4u : 6u);  // SWIZZLE_128B / 64B / 32B
@@ -131,12 +134,70 @@ __device__ __forceinline__ void store_chunk(const TcArgs& a, const uint32_t (&v)
   }
 }
 
+// 4-byte outputs through shared memory: the warp's 32x32 block is written into a 128B-swizzled
+// buffer (16-byte chunk j of row r at chunk j ^ (r % 8), the layout of a SWIZZLE_128B tensor map)
+// and stored by one TMA instruction, which also clips rows >= M and columns >= N.
+template <int KIND>
+__device__ __forceinline__ void stage_chunk_4b(const TcArgs& a, const uint32_t (&v)[32], int n, int lane,
+                                               uint8_t* sbuf, const int32_t* bias, const float* scale) {
+  const bool full = n + 32 <= a.N;
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    int t[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int col = n + 4 * q + i;
+      t[i] = static_cast<int>(v[4 * q + i]);
+      if (bias && (full || col < a.N)) t[i] = wrap_add(t[i], bias[col]);
+    }
+    uint4 w;
+    if constexpr (KIND == kOutS32) {
+      w = make_uint4(t[0], t[1], t[2], t[3]);
+    } else {
+      float f[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int col = n + 4 * q + i;
+        f[i] = (full || col < a.N) ? __fmul_rn(__int2float_rn(t[i]), scale[col]) : 0.0f;
+      }
+      w = make_uint4(__float_as_uint(f[0]), __float_as_uint(f[1]), __float_as_uint(f[2]), __float_as_uint(f[3]));
+    }
+    *reinterpret_cast<uint4*>(sbuf + lane * 128 + ((q ^ (lane & 7)) << 4)) = w;
+  }
+}
+
 // Epilogue role: 8 warps; warp w reads TMEM lanes 32*(w%4)..+31 (the hardware restricts a warp
 // to the lane quarter w%4) and the chunks of 32 columns with chunk % 2 == (w-2)/4.  The TMEM load
 // of the next chunk is issued before the current chunk is processed (two register buffers).
 template <int KIND>
-__device__ __forceinline__ void epilogue_role(const TcArgs& a, uint32_t tmem_base, uint32_t accf0, uint32_t acce0,
-                                              int warp, int lane, const int32_t* bias, const float* scale) {
+__device__ __forceinline__ void emit_chunk(const TcArgs& a, const CUtensorMap* tmC, const uint32_t (&v)[32], int b,
+                                           int m, int mrow0, size_t row_off, int n, int lane, uint8_t* sbufs,
+                                           int& sb, const int32_t* bias, const float* scale) {
+  if (n >= a.N) return;
+  if constexpr (KIND != kOutS8) {
+    if (a.tma_store) {
+      uint8_t* buf = sbufs + sb * kEpiStageBytes;
+      if (lane == 0) bulk_wait_group_read<1>();  // the store that used this buffer has read it
+      __syncwarp();
+      stage_chunk_4b<KIND>(a, v, n, lane, buf, bias, scale);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        tma_store_3d(tmC, smem_u32(buf), n, mrow0, b);
+        bulk_commit_group();
+      }
+      sb ^= 1;
+      return;
+    }
+  }
+  if (m < a.M) store_chunk<KIND>(a, v, row_off + n, n, min(32, a.N - n), bias, scale);
+}
+
+template <int KIND>
+__device__ __forceinline__ void epilogue_role(const TcArgs& a, const CUtensorMap* tmC, uint32_t tmem_base,
+                                              uint32_t accf0, uint32_t acce0, int warp, int lane,
+                                              const int32_t* bias, const float* scale, uint8_t* sbufs) {
+  int sb = 0;
   const int q = warp & 3;
   const int half = (warp - 2) >> 2;
   const int row = q * 32 + lane;
@@ -161,15 +222,12 @@ __device__ __forceinline__ void epilogue_role(const TcArgs& a, uint32_t tmem_bas
     for (int i = 0; i < nmine; i += 2) {
       const int ca = half + 2 * i, cb = ca + 2;
       if (i + 1 < nmine) tmem_ld_32x32b_x32(tbase + cb * 32, vb);
-      {
-        const int n = n0 + ca * 32;
-        if (m < a.M && n < a.N) store_chunk<KIND>(a, va, row_off + n, n, min(32, a.N - n), bias, scale);
-      }
+      const int mrow0 = mt * kTcBM + q * 32;
+      emit_chunk<KIND>(a, tmC, va, b, m, mrow0, row_off, n0 + ca * 32, lane, sbufs, sb, bias, scale);
       tmem_ld_wait();
       if (i + 1 < nmine) {
         if (i + 2 < nmine) tmem_ld_32x32b_x32(tbase + (cb + 2) * 32, va);
-        const int n = n0 + cb * 32;
-        if (m < a.M && n < a.N) store_chunk<KIND>(a, vb, row_off + n, n, min(32, a.N - n), bias, scale);
+        emit_chunk<KIND>(a, tmC, vb, b, m, mrow0, row_off, n0 + cb * 32, lane, sbufs, sb, bias, scale);
         tmem_ld_wait();
       }
     }
@@ -181,11 +239,12 @@ __device__ __forceinline__ void epilogue_role(const TcArgs& a, uint32_t tmem_bas
       acc_ph ^= 1u;
     }
   }
+  if (KIND != kOutS8 && a.tma_store && lane == 0) bulk_wait_group_all();
 }
 
 __global__ void __launch_bounds__(kTcThreads, 1)
     tc_gemm_s8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                      const TcArgs a) {
+                      const __grid_constant__ CUtensorMap tmC, const TcArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t stage_a = kTcBM * a.BK;
@@ -203,6 +262,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   // bias[stage_cols] then scale[stage_cols], 16-byte aligned, after the barriers
   int32_t* s_bias = reinterpret_cast<int32_t*>(bars + 2 * a.stages + 6);
   float* s_scale = reinterpret_cast<float*>(s_bias + a.stage_cols);
+  // TMA-store staging: 2 x 4 KiB per epilogue warp, 1024-byte aligned, after the bias / scale copy
+  uint8_t* s_out = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(s_scale + a.stage_cols) + 1023) & ~uintptr_t(1023));
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -374,12 +436,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       bias = a.epi.bias ? s_bias : nullptr;
       scale = s_scale;
     }
+    uint8_t* sbufs = s_out + (warp - 2) * 2 * kEpiStageBytes;
     if (a.epi.out_kind == kOutS8)
-      epilogue_role<kOutS8>(a, tmem_base, accf0, acce0, warp, lane, bias, scale);
+      epilogue_role<kOutS8>(a, &tmC, tmem_base, accf0, acce0, warp, lane, bias, scale, sbufs);
     else if (a.epi.out_kind == kOutS32)
-      epilogue_role<kOutS32>(a, tmem_base, accf0, acce0, warp, lane, bias, scale);
+      epilogue_role<kOutS32>(a, &tmC, tmem_base, accf0, acce0, warp, lane, bias, scale, sbufs);
     else
-      epilogue_role<kOutF32>(a, tmem_base, accf0, acce0, warp, lane, bias, scale);
+      epilogue_role<kOutF32>(a, &tmC, tmem_base, accf0, acce0, warp, lane, bias, scale, sbufs);
   }
 
   tc_fence_before();
