@@ -186,18 +186,13 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     barrier()
     e2e_ms = s_ev.elapsed_time(e_ev) / e2e_steps
 
-    # ---- verification gather (untimed): per-rank output checksums to every rank over NCCL
-    chk = torch.stack([y2.view(torch.uint8).to(torch.int64).sum(), y1.view(torch.uint8).to(torch.int64).sum()])
-    if world > 1:
-        gathered = [torch.zeros_like(chk) for _ in range(world)]
-        dist.all_gather(gathered, chk)
-        checksums = [g.tolist() for g in gathered]
-        tt = torch.tensor([total_ms, e2e_ms], dtype=torch.float64, device=dev)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        total_ms, e2e_ms = tt.tolist()
-        step_ms = total_ms / args.steps
-    else:
-        checksums = [chk.tolist()]
+    # ---- after timing: max over ranks of the device times, and a checksum gather (verification)
+    from my_own_cnn_b200.shard import checksum, gather_tensors, max_over_ranks
+
+    total_ms, e2e_ms = max_over_ranks([total_ms, e2e_ms], device=dev)
+    step_ms = total_ms / args.steps
+    chk = torch.cat([checksum(y2), checksum(y1)])
+    checksums = [g.tolist() for g in gather_tensors(chk)]
     if rank != 0:
         return None
 
