@@ -307,3 +307,31 @@ def test_no_device_error_after_suite(cuda_lib):
     from my_own_cnn_b200 import _lib
 
     assert _lib.lib().b200q_device_error() == 0, _lib.lib().b200q_last_error()
+
+
+def test_conv_stack_pipelined_host_pass_matches_oracle(cuda_lib):
+    """ConvStack.run_host (chunked H2D / kernels / D2H on three streams, ragged last chunk)
+    equals the device-resident pass and the oracle."""
+    b2q = _b2q()
+    from my_own_cnn_b200.stack import ConvLayer, ConvStack
+
+    n, h, w, c, k1, k2 = 37, 20, 20, 64, 96, 32
+    x = rng_s8(50, (n, h, w, c))
+    w1, w2 = rng_s8(51, (k1, 3, 3, c)), rng_s8(52, (k2, 1, 1, k1))
+    rng = np.random.default_rng(53)
+    b1 = rng.integers(-2**15, 2**15, size=k1).astype(np.int32)
+    s1 = rng.uniform(1e-4, 1e-3, size=k1).astype(np.float32)
+    s2 = rng.uniform(1e-3, 1e-2, size=k2).astype(np.float32)
+    cu = lambda a: torch.from_numpy(a).cuda()
+    net = ConvStack([ConvLayer(cu(w1), cu(b1), cu(s1), b2q.Conv2DParams(), b2q.Epilogue.int8(relu=True)),
+                     ConvLayer(cu(w2), None, cu(s2), b2q.Conv2DParams(0, 0), b2q.Epilogue.int32())], (h, w, c))
+    xh = torch.from_numpy(x).pin_memory()
+    yh = torch.empty((n, h, w, k2), dtype=torch.int32).pin_memory()
+    net.run_host(xh, yh, chunk=8)
+    torch.cuda.synchronize()
+    y_dev = net.forward(cu(x)).cpu()
+    acc1 = oracle.conv_s8(oracle.conv_args(n, h, w, c, 3, 3, k1), x, w1, threads=4)
+    y1 = oracle.requant_s8(acc1, b1, s1, 0, 0, 127)
+    ref = oracle.conv_s8(oracle.conv_args(n, h, w, k1, 1, 1, k2, 0, 0), y1, w2, threads=4)
+    np.testing.assert_array_equal(yh.numpy(), ref)
+    np.testing.assert_array_equal(y_dev.numpy(), ref)
