@@ -3,7 +3,8 @@
 // Validation follows the reference's own checks (infer_conv_shape / infer_block_conv_shape,
 // src/conv_types.h:125-169) but returns status codes instead of throwing.  Dispatch:
 //   conv2d_s8 : tcgen05 implicit GEMM (im2col TMA, or plain tiled TMA for 1x1/s1/p0) when
-//               groups == 1, C % 32 == 0, K % 16 == 0 and the tensors are 16-byte aligned;
+//               groups == 1, C % 16 == 0 and the tensors are 16-byte aligned (channels past C in
+//               the last K block are zero-filled by TMA in both operands);
 //               depthwise CUDA-core kernel for groups == C == K, C % 16 == 0;
 //               CUDA-core direct kernel otherwise.
 //   bmm_s8    : tcgen05 tiled GEMM (K-major or MN-major operands) when the TMA stride rules hold,
@@ -148,10 +149,10 @@ size_t out_elem_size(int kind) { return kind == B200Q_OUT_S8 ? 1 : 4; }
 
 // ------------------------------------------------------------------ TMA maps
 int encode_tiled_3d(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2, uint32_t b0,
-                    uint32_t b1, int swizzle_bytes) {
+                    uint32_t b1, int swizzle_bytes, uint32_t b2 = 1) {
   cuuint64_t dims[3] = {d0, d1, d2};
   cuuint64_t strides[2] = {d0, d0 * d1};  // bytes (uint8 elements)
-  cuuint32_t box[3] = {b0, b1, 1};
+  cuuint32_t box[3] = {b0, b1, b2};
   cuuint32_t es[3] = {1, 1, 1};
   CUtensorMapSwizzle sw = swizzle_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
                           : swizzle_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
@@ -377,11 +378,21 @@ int b200q_conv2d_s8(const int8_t* d_x, const int8_t* d_w, const int32_t* d_bias,
                           g.stride_h <= 8 && g.stride_w <= 8;
   // Small activations take the CUDA-core path: the im2col TMA mode is only used on tensors of
   // at least 128 KiB (a driver limitation on small im2col maps).
-  const bool tc_ok = g_policy.load() == 0 && g.groups == 1 && c % 32 == 0 && k % 16 == 0 && vec_ptrs &&
+  const bool tc_ok = g_policy.load() == 0 && g.groups == 1 && c % 16 == 0 && vec_ptrs &&
                      M < (1ll << 31) && (is_1x1_plain || (corners_ok && x_bytes >= (128u << 10)));
   if (tc_ok) {
     TcArgs a{};
-    a.BK = c % 128 == 0 ? 128 : (c % 64 == 0 ? 64 : 32);
+    // K block per stage: the largest of 128/64/32 bytes whose channel padding (zero-filled by TMA
+    // past C) stays within 1/8 of C; 32 otherwise.
+    a.BK = 32;
+    for (int bk : {128, 64}) {
+      const int padded = (c + bk - 1) / bk * bk;
+      if (padded * 8 <= c * 9) {
+        a.BK = bk;
+        break;
+      }
+    }
+    a.cchunks = (c + a.BK - 1) / a.BK;
     a.BN = pick_bn(k, 0);
     a.M = static_cast<int>(M);
     a.N = k;
@@ -393,20 +404,24 @@ int b200q_conv2d_s8(const int8_t* d_x, const int8_t* d_w, const int32_t* d_bias,
     a.out = d_y;
     a.ldc = k;
     a.batch_stride = 0;
-    a.vec_ok = 1;
+    a.vec_ok = k % 16 == 0;
+    a.conv_b = c % a.BK != 0;  // 3-D weight map only when the last K block needs zero fill
     CUtensorMap ma, mb;
     const int kdim = r * s * c;
-    rc = encode_tiled_3d(&mb, d_w, static_cast<uint64_t>(kdim), static_cast<uint64_t>(k), 1, a.BK, a.BN, a.BK);
+    if (a.conv_b)  // weights as {C, R*S, K}: a box of BK channels x 1 tap x BN output channels
+      rc = encode_tiled_3d(&mb, d_w, static_cast<uint64_t>(c), static_cast<uint64_t>(r * s),
+                           static_cast<uint64_t>(k), a.BK, 1, a.BK, a.BN);
+    else  // weights as the K-major matrix [K][R*S*C]
+      rc = encode_tiled_3d(&mb, d_w, static_cast<uint64_t>(kdim), static_cast<uint64_t>(k), 1, a.BK, a.BN, a.BK);
     if (rc) return rc;
     if (is_1x1_plain) {
       a.mode = 0;
-      a.num_kb = (c + a.BK - 1) / a.BK;
+      a.num_kb = a.cchunks;
       rc = encode_tiled_3d(&ma, d_x, static_cast<uint64_t>(c), static_cast<uint64_t>(M), 1, a.BK, kTcBM, a.BK);
       if (rc) return rc;
       g_last_path = 2;
     } else {
       a.mode = 1;
-      a.cchunks = c / a.BK;
       a.num_kb = r * s * a.cchunks;
       a.Ho = g.ho; a.Wo = g.wo; a.S = s;
       a.stride_h = g.stride_h; a.stride_w = g.stride_w;

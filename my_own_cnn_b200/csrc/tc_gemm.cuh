@@ -33,6 +33,7 @@ struct TcArgs {
   int m_tiles, n_tiles, total_tiles;
   int a_major, b_major;  // 0 = K-major, 1 = MN-major (bmm transposes)
   int b_batched;         // B map has a batch dimension (bmm); conv weights are shared
+  int conv_b;            // B is conv weights as a 3-D map {C, R*S, K}: channels past C read as zero
   // im2col geometry
   int Ho, Wo, S, cchunks, stride_h, stride_w, pad_h, pad_w, dil_h, dil_w;
   // epilogue
@@ -341,7 +342,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             tma_load_3d(dA, &tmA, fb, m0, kb * a.BK, b);
           }
           const int bb = a.b_batched ? b : 0;
-          if (a.b_major == 0) {
+          if (a.conv_b) {
+            const int tap = a.mode == 1 ? kb / a.cchunks : 0;
+            const int cc = kb - tap * a.cchunks;
+            tma_load_3d(dB, &tmB, fb, cc * a.BK, tap, n0);
+          } else if (a.b_major == 0) {
             tma_load_3d(dB, &tmB, fb, kb * a.BK, n0, bb);
           } else {
             for (int i = 0; i < a.BN / 128; ++i)

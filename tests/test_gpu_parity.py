@@ -133,6 +133,9 @@ def _conv_case(n, h, w, c, r, s, k, p, seed, epi_kind="all", groups=1):
     (1, 40, 36, 96, 3, 3, 48, 2, 1, 2),    # dilation 2, BK 32 chunks
     (2, 24, 24, 256, 1, 1, 272, 0, 2, 1),  # 1x1 stride 2 (projection shortcut) through im2col
     (1, 64, 64, 32, 5, 5, 32, 2, 1, 1),    # 5x5, C = 32
+    (2, 96, 96, 16, 3, 3, 24, 1, 1, 1),    # C = 16 (zero-filled half K block), K = 24 (scalar stores)
+    (2, 30, 30, 144, 3, 3, 144, 1, 2, 1),  # C = 144 = 4.5 x 32 (MobileNetV2 expand width), stride 2
+    (2, 40, 40, 48, 3, 3, 64, 1, 1, 1),    # C = 48
 ])
 def test_conv_s8_tcgen05_im2col(cuda_lib, shape):
     b2q = _b2q()
@@ -147,6 +150,8 @@ def test_conv_s8_tcgen05_im2col(cuda_lib, shape):
     (1, 14, 14, 512, 2048),
     (3, 7, 9, 64, 16),       # M edge (189 rows), tiny N
     (1, 13, 11, 160, 96),    # BK 32 chunks, N edge
+    (4, 28, 28, 16, 96),     # C = 16 (MobileNetV2 expand 16 -> 96)
+    (2, 28, 28, 144, 24),    # C = 144, K = 24 (project 144 -> 24)
 ])
 def test_conv_s8_tcgen05_pointwise(cuda_lib, shape):
     b2q = _b2q()
