@@ -29,6 +29,7 @@ PATH_NAMES = {
     4: "cuda-core-depthwise",
     5: "cuda-core-qi32",
     6: "cuda-core-bmm-i32",
+    7: "tcgen05-packed",
 }
 
 

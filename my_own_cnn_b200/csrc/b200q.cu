@@ -6,6 +6,8 @@
 //               groups == 1, C % 16 == 0 and the tensors are 16-byte aligned (channels past C in
 //               the last K block are zero-filled by TMA in both operands);
 //               depthwise CUDA-core kernel for groups == C == K, C % 16 == 0;
+//               low channel counts (C % 16 != 0, e.g. the C = 3 stems): im2col pack into a
+//               per-stream workspace + the same tcgen05 GEMM;
 //               CUDA-core direct kernel otherwise.
 //   bmm_s8    : tcgen05 tiled GEMM (K-major or MN-major operands) when the TMA stride rules hold,
 //               CUDA-core tiled GEMM otherwise.
@@ -19,7 +21,9 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <map>
 #include <mutex>
+#include <utility>
 
 #include "../../include/b200q.h"
 #include "common.cuh"
@@ -286,6 +290,84 @@ int qi32_common(int qtype, const float* x, const float* w, int32_t* y, const Con
   return check_launch("qi32_conv_kernel launch");
 }
 
+// ------------------------------------------------------------- workspace
+// Grow-only scratch per (device, stream), allocated stream-ordered (cudaMallocAsync /
+// cudaFreeAsync on that stream), so calls on one stream may reuse it without synchronising and
+// calls on different streams never share it.
+struct Workspace {
+  void* ptr = nullptr;
+  size_t cap = 0;
+};
+std::map<std::pair<int, cudaStream_t>, Workspace> g_ws;
+std::mutex g_ws_mu;
+
+int get_workspace(size_t bytes, cudaStream_t stream, void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  std::lock_guard<std::mutex> lk(g_ws_mu);
+  Workspace& w = g_ws[{dev, stream}];
+  if (w.cap < bytes) {
+    if (w.ptr) {
+      e = cudaFreeAsync(w.ptr, stream);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaFreeAsync(workspace)");
+      w.ptr = nullptr;
+      w.cap = 0;
+    }
+    size_t nb = bytes + bytes / 4;
+    nb = (nb + (2u << 20) - 1) & ~static_cast<size_t>((2u << 20) - 1);
+    e = cudaMallocAsync(&w.ptr, nb, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMallocAsync(workspace)");
+    w.cap = nb;
+  }
+  *out = w.ptr;
+  return B200Q_OK;
+}
+
+size_t round256(size_t v) { return (v + 255) & ~static_cast<size_t>(255); }
+
+// Bytes of scratch the packed low-channel path needs: the im2col matrix then the padded weights.
+size_t packed_scratch_bytes(long long rows, int k, int kp) {
+  return round256(static_cast<size_t>(rows) * kp) + round256(static_cast<size_t>(k) * kp);
+}
+
+// Low-channel conv through scratch: pack im2col rows and zero-padded weights, then run the
+// tcgen05 GEMM in tiled mode (M = N*Ho*Wo rows, K = kp, N = output channels).
+int run_packed_conv(const DeviceState& st, const int8_t* x, const int8_t* w, void* y, const ConvGeom& g,
+                    const Epilogue& e, int8_t* scratch, cudaStream_t stream) {
+  const long long rows = static_cast<long long>(g.n) * g.ho * g.wo;
+  const int rsc = g.r * g.s * g.c;
+  const int kp = (rsc + 31) / 32 * 32;
+  int8_t* a_buf = scratch;
+  int8_t* w_buf = scratch + round256(static_cast<size_t>(rows) * kp);
+  im2col_pack_s8_kernel<<<grid_for(static_cast<size_t>(rows) * (kp / 4), 256, st.sms), 256, 0, stream>>>(
+      x, a_buf, g, kp, rows);
+  int rc = check_launch("im2col_pack_s8_kernel launch");
+  if (rc) return rc;
+  weight_pad_s8_kernel<<<grid_for(static_cast<size_t>(g.k) * kp, 256, st.sms), 256, 0, stream>>>(w, w_buf, g.k, rsc,
+                                                                                                   kp);
+  rc = check_launch("weight_pad_s8_kernel launch");
+  if (rc) return rc;
+  TcArgs a{};
+  a.mode = 0;
+  a.BK = kp % 128 == 0 ? 128 : (kp % 64 == 0 ? 64 : 32);
+  a.BN = pick_bn(g.k, 0);
+  a.M = static_cast<int>(rows);
+  a.N = g.k;
+  a.batch = 1;
+  a.num_kb = kp / a.BK;
+  a.epi = e;
+  a.out = y;
+  a.ldc = g.k;
+  a.vec_ok = g.k % 16 == 0;
+  CUtensorMap ma, mb;
+  rc = encode_tiled_3d(&ma, a_buf, static_cast<uint64_t>(kp), static_cast<uint64_t>(rows), 1, a.BK, kTcBM, a.BK);
+  if (rc) return rc;
+  rc = encode_tiled_3d(&mb, w_buf, static_cast<uint64_t>(kp), static_cast<uint64_t>(g.k), 1, a.BK, a.BN, a.BK);
+  if (rc) return rc;
+  return launch_tc(st, ma, mb, a, stream);
+}
+
 }  // namespace
 }  // namespace b200q
 
@@ -432,6 +514,16 @@ int b200q_conv2d_s8(const int8_t* d_x, const int8_t* d_w, const int32_t* d_bias,
       g_last_path = 1;
     }
     return launch_tc(*st, ma, mb, a, cs);
+  }
+  // Low-channel convolutions (C % 16 != 0): im2col pack into the stream's workspace, then tcgen05.
+  const int kp_packed = (r * s * c + 31) / 32 * 32;
+  if (g_policy.load() == 0 && g.groups == 1 && c % 16 != 0 && M >= 4096 && M < (1ll << 31) && kp_packed <= 4096 &&
+      aligned16(d_y) && (!d_bias || aligned16(d_bias)) && (!d_scale || aligned16(d_scale))) {
+    void* ws = nullptr;
+    rc = get_workspace(packed_scratch_bytes(M, k, kp_packed), cs, &ws);
+    if (rc) return rc;
+    g_last_path = 7;
+    return run_packed_conv(*st, d_x, d_w, d_y, g, e, static_cast<int8_t*>(ws), cs);
   }
   const size_t total = static_cast<size_t>(M) * k;
   if (g.groups == c && k == c && c % 16 == 0 && r * s * c <= 48 * 1024 && aligned16(d_x) && aligned16(d_y)) {

@@ -251,3 +251,55 @@ __global__ void fill_s8_table_kernel(int8_t* out, size_t count, uint64_t key, co
 }
 
 }  // namespace b200q
+
+namespace b200q {
+
+// Low-channel convolutions (C % 16 != 0, e.g. the C = 3 stems) on the tensor cores: the
+// activation rows are gathered into an im2col matrix a[m][kp] with kp = round_up(R*S*C, 32),
+// columns ordered (r, s, c) like the KRSC weights, zero at padding taps and past R*S*C.
+// One thread writes 4 consecutive bytes of a row.
+__global__ void im2col_pack_s8_kernel(const int8_t* __restrict__ x, int8_t* __restrict__ a, ConvGeom g, int kp,
+                                      long long rows) {
+  const int words = kp >> 2;
+  const int rsc = g.r * g.s * g.c;
+  const size_t total = static_cast<size_t>(rows) * words;
+  for (size_t idx = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; idx < total;
+       idx += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const long long m = static_cast<long long>(idx / words);
+    const int k0 = static_cast<int>(idx - static_cast<size_t>(m) * words) * 4;
+    const int wo = static_cast<int>(m % g.wo);
+    const long long t = m / g.wo;
+    const int ho = static_cast<int>(t % g.ho);
+    const int n = static_cast<int>(t / g.ho);
+    uint32_t word = 0;
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+      const int kk = k0 + b;
+      if (kk < rsc) {
+        const int c = kk % g.c;
+        const int tap = kk / g.c;
+        const int ss = tap % g.s, rr = tap / g.s;
+        const int hi = ho * g.stride_h - g.pad_h + rr * g.dil_h;
+        const int wi = wo * g.stride_w - g.pad_w + ss * g.dil_w;
+        if (hi >= 0 && hi < g.h && wi >= 0 && wi < g.w) {
+          const int8_t v = __ldg(x + ((static_cast<size_t>(n) * g.h + hi) * g.w + wi) * g.c + c);
+          word |= (static_cast<uint32_t>(static_cast<uint8_t>(v))) << (8 * b);
+        }
+      }
+    }
+    reinterpret_cast<uint32_t*>(a)[idx] = word;
+  }
+}
+
+// Weights [k][R*S*C] -> [k][kp] with zero columns past R*S*C.
+__global__ void weight_pad_s8_kernel(const int8_t* __restrict__ w, int8_t* __restrict__ wp, int k, int rsc, int kp) {
+  const size_t total = static_cast<size_t>(k) * kp;
+  for (size_t idx = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; idx < total;
+       idx += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const int row = static_cast<int>(idx / kp);
+    const int col = static_cast<int>(idx - static_cast<size_t>(row) * kp);
+    wp[idx] = col < rsc ? w[static_cast<size_t>(row) * rsc + col] : static_cast<int8_t>(0);
+  }
+}
+
+}  // namespace b200q

@@ -177,6 +177,20 @@ def test_conv_s8_cuda_core_paths(cuda_lib, shape, groups, expect):
     assert paths == {expect}, paths
 
 
+@pytest.mark.parametrize("shape", [
+    (4, 64, 64, 3, 7, 7, 64, 3, 2, 1),     # ResNet-50 stem geometry (7x7/2, C = 3)
+    (2, 128, 128, 3, 3, 3, 32, 1, 2, 1),   # MobileNetV2 stem (3x3/2, C = 3 -> 32)
+    (2, 56, 56, 24, 1, 1, 144, 0, 1, 1),   # MobileNetV2 expand 24 -> 144
+    (2, 48, 48, 24, 3, 3, 40, 1, 1, 1),    # C = 24, 3x3, K = 40 (scalar edge stores)
+])
+def test_conv_s8_packed_low_channel(cuda_lib, shape):
+    b2q = _b2q()
+    n, h, w, c, r, s, k, pad, st, dil = shape
+    p = b2q.Conv2DParams(pad, pad, st, st, dil, dil, 1)
+    paths = _conv_case(n, h, w, c, r, s, k, p, seed=3 + sum(shape))
+    assert paths == {"tcgen05-packed"}, paths
+
+
 def test_conv_forced_cuda_core_matches_tcgen05(cuda_lib):
     b2q = _b2q()
     x = torch.from_numpy(rng_s8(5, (2, 32, 32, 64))).cuda()
