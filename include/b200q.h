@@ -116,6 +116,27 @@ int b200q_bmm_s8(const int8_t* A, const int8_t* B, const int32_t* d_bias, const 
                  void* C, int batch, int M, int N, int K, int trans_a, int trans_b,
                  const b200q_epilogue* epi, void* stream);
 
+/* Packed low-channel int8 conv that allocates nothing (no counterpart in the reference).
+ * For callers that may not allocate device memory at all: for example plugins inside a runtime
+ * that owns and budgets every byte of GPU memory itself, or latency-critical loops where a
+ * cudaMalloc (which can synchronise the device) is not acceptable.  Same arguments, arithmetic
+ * and results as b200q_conv2d_s8 on its packed path (im2col matrix + tcgen05 GEMM), for any
+ * groups == 1 conv; the im2col matrix and padded weights live in one fixed 32 MiB device array
+ * of this library instead of a workspace (every GPU that loads the library holds that array
+ * until the process exits).  Limit: round256(N*Ho*Wo*kp) + round256(K*kp) <= 32 MiB with
+ * kp = round_up(R*S*C, 32) <= 4096; larger requests return B200Q_ERR_INVALID_ARG with the sizes
+ * in b200q_last_error().  The first call on a device looks up the array's device address
+ * (cudaGetSymbolAddress); make that first call before any stream capture.  All calls on a
+ * device share the array: every byte the kernels read is rewritten by the same call, but calls
+ * that overlap on the GPU (different streams, or host threads sharing a device) race. */
+int b200q_conv2d_s8_packed_noalloc(const int8_t* d_x, const int8_t* d_w, const int32_t* d_bias,
+                                   const float* d_scale, void* d_y, int n, int h, int w, int c, int r,
+                                   int s, int k, const b200q_conv_params* p,
+                                   const b200q_epilogue* epi, void* stream);
+
+/* Size in bytes of the fixed scratch array behind b200q_conv2d_s8_packed_noalloc. */
+size_t b200q_noalloc_scratch_bytes(void);
+
 /* ---- host utilities ---- */
 
 /* Output shape with the checks of infer_conv_shape (src/conv_types.h:125-146). */

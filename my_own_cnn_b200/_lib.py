@@ -70,6 +70,7 @@ def lib() -> ctypes.CDLL:
         "b200q_block_fprop_nhwc_qi32": [i, vp, vp, vp, i, i, i, i, i, i, i, pconv, i, i, vp, vp, vp],
         "b200q_bmm_matmul_i32": [vp, vp, vp, i, i, i, i, i, i, vp],
         "b200q_conv2d_s8": [vp, vp, vp, vp, vp, i, i, i, i, i, i, i, pconv, pepi, vp],
+        "b200q_conv2d_s8_packed_noalloc": [vp, vp, vp, vp, vp, i, i, i, i, i, i, i, pconv, pepi, vp],
         "b200q_bmm_s8": [vp, vp, vp, vp, vp, i, i, i, i, i, i, pepi, vp],
         "b200q_conv_out_shape": [i, i, i, i, i, i, pconv, POINTER(c_int), POINTER(c_int)],
         "b200q_device_error": [],
@@ -87,6 +88,8 @@ def lib() -> ctypes.CDLL:
     L.b200q_last_error.restype = c_char_p
     L.b200q_set_path_policy.argtypes = [c_int]
     L.b200q_set_path_policy.restype = None
+    L.b200q_noalloc_scratch_bytes.argtypes = []
+    L.b200q_noalloc_scratch_bytes.restype = c_size_t
     L.b200q_tc_launch_count.argtypes = []
     L.b200q_tc_launch_count.restype = c_longlong
     _lib = L
@@ -116,5 +119,5 @@ EXPORTED_SYMBOLS = [
     "b200q_conv2d_s8", "b200q_bmm_s8", "b200q_conv_out_shape", "b200q_last_error",
     "b200q_device_error", "b200q_last_path", "b200q_set_path_policy", "b200q_tc_launch_count",
     "b200q_fill_s8_uniform", "b200q_fill_i32_uniform", "b200q_fill_s8_table",
-    "b200q_selftest_wait_timeout",
+    "b200q_selftest_wait_timeout", "b200q_conv2d_s8_packed_noalloc", "b200q_noalloc_scratch_bytes",
 ]

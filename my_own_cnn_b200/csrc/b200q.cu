@@ -368,6 +368,33 @@ int run_packed_conv(const DeviceState& st, const int8_t* x, const int8_t* w, voi
   return launch_tc(st, ma, mb, a, stream);
 }
 
+// ------------------------------------------------- fixed scratch (no allocation)
+// Scratch for b200q_conv2d_s8_packed_noalloc: a file-scope device array, so that entry point never
+// allocates.  Every GPU that loads this library holds it until the process exits.
+constexpr size_t kNoAllocScratchBytes = 32u << 20;  // 32 MiB
+static __device__ __align__(256) int8_t g_noalloc_scratch[kNoAllocScratchBytes];
+
+// Device address of g_noalloc_scratch per device.  In host code the array's name is only a host
+// stand-in, so the address is looked up once per device, with that device current.
+int8_t* g_noalloc_ptr[64] = {};
+std::mutex g_noalloc_mu;
+
+int noalloc_scratch(int8_t** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= 64) return fail(B200Q_ERR_UNSUPPORTED, "device index %d out of range", dev);
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* ptr = nullptr;
+    e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(g_noalloc_scratch)");
+    g_noalloc_ptr[dev] = static_cast<int8_t*>(ptr);
+  }
+  *out = g_noalloc_ptr[dev];
+  return B200Q_OK;
+}
+
 }  // namespace
 }  // namespace b200q
 
@@ -601,6 +628,43 @@ int b200q_bmm_s8(const int8_t* A, const int8_t* B, const int32_t* d_bias, const 
   g_last_path = 3;
   return B200Q_OK;
 }
+
+// Packed low-channel conv with fixed scratch: see include/b200q.h.  Same arithmetic and kernels as
+// the packed path of b200q_conv2d_s8, but the im2col matrix and padded weights go to the static
+// array above instead of a workspace, and nothing is allocated.
+int b200q_conv2d_s8_packed_noalloc(const int8_t* d_x, const int8_t* d_w, const int32_t* d_bias, const float* d_scale,
+                                   void* d_y, int n, int h, int w, int c, int r, int s, int k,
+                                   const b200q_conv_params* p, const b200q_epilogue* epi, void* stream) {
+  ConvGeom g;
+  int rc = conv_geom(n, h, w, c, r, s, k, p, 1, 1, &g);
+  if (rc) return rc;
+  if (!d_x || !d_w || !d_y) return fail(B200Q_ERR_INVALID_ARG, "null tensor pointer");
+  if (g.groups != 1) return fail(B200Q_ERR_UNSUPPORTED, "the fixed-scratch conv supports groups == 1 only");
+  Epilogue e;
+  rc = make_epilogue(epi, d_bias, d_scale, &e);
+  if (rc) return rc;
+  if (!aligned16(d_y) || (d_bias && !aligned16(d_bias)) || (d_scale && !aligned16(d_scale)))
+    return fail(B200Q_ERR_INVALID_ARG, "output, bias and scale must be 16-byte aligned");
+  const long long rows = static_cast<long long>(n) * g.ho * g.wo;
+  const int kp = (r * s * c + 31) / 32 * 32;
+  if (kp > 4096) return fail(B200Q_ERR_UNSUPPORTED, "R*S*C = %d exceeds 4096", r * s * c);
+  const size_t need = packed_scratch_bytes(rows, k, kp);
+  if (rows >= (1ll << 31) || need > kNoAllocScratchBytes)
+    return fail(B200Q_ERR_INVALID_ARG,
+                "fixed-scratch conv needs %zu bytes of scratch (N*Ho*Wo*%d + K*%d, each rounded to 256) but the "
+                "maximum is %zu; use b200q_conv2d_s8 or a smaller batch",
+                need, kp, kp, kNoAllocScratchBytes);
+  DeviceState* st = nullptr;
+  rc = device_state(&st);
+  if (rc) return rc;
+  int8_t* scratch = nullptr;
+  rc = noalloc_scratch(&scratch);
+  if (rc) return rc;
+  g_last_path = 7;
+  return run_packed_conv(*st, d_x, d_w, d_y, g, e, scratch, as_stream(stream));
+}
+
+size_t b200q_noalloc_scratch_bytes(void) { return kNoAllocScratchBytes; }
 
 int b200q_device_error(void) {
   DeviceState* st = nullptr;

@@ -1,0 +1,77 @@
+"""The conv entry point that allocates nothing (b200q_conv2d_s8_packed_noalloc).
+
+It exists for callers that may not allocate GPU memory themselves -- plugins whose host runtime
+owns and budgets all device memory, or latency-critical code where a cudaMalloc is not allowed.
+Its scratch is one fixed device array of the library, shared by all calls on a device.  This file
+is collected last on purpose, so a run that stops at the first failure has run everything else.
+The test calls the entry point twice in a row through the C ABI (the second call reuses the
+scratch left by the first) and compares both results with b200q_conv2d_s8, bit for bit.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+from my_own_cnn_b200 import _lib
+from tests.kat import rng_s8
+
+pytestmark = pytest.mark.gpu
+
+
+def _call(name, x, w, bias, scale, y, shape, params, epi):
+    n, h, wd, c, r, s, k = shape
+    cp = _lib.CConvParams(*params)
+    ce = _lib.CEpilogue(*epi)
+    ptr = lambda t: 0 if t is None else t.data_ptr()
+    fn = getattr(_lib.lib(), name)
+    return fn(ptr(x), ptr(w), ptr(bias), ptr(scale), ptr(y), n, h, wd, c, r, s, k, ctypes.byref(cp),
+              ctypes.byref(ce), torch.cuda.current_stream().cuda_stream)
+
+
+def _case(seed, shape, params, epi, out_dtype):
+    n, h, wd, c, r, s, k = shape
+    pad_h, pad_w, sh, sw, dh, dw, _ = params
+    ho = (h + 2 * pad_h - dh * (r - 1) - 1) // sh + 1
+    wo = (wd + 2 * pad_w - dw * (s - 1) - 1) // sw + 1
+    x = torch.from_numpy(rng_s8(seed, (n, h, wd, c))).cuda()
+    w = torch.from_numpy(rng_s8(seed + 1, (k, r, s, c))).cuda()
+    rng = np.random.default_rng(seed + 2)
+    bias = torch.from_numpy(rng.integers(-2**15, 2**15, size=k).astype(np.int32)).cuda()
+    scale = torch.from_numpy(rng.uniform(1e-4, 1e-3, size=k).astype(np.float32)).cuda()
+    mk = lambda: torch.empty((n, ho, wo, k), dtype=out_dtype, device="cuda")
+    return dict(x=x, w=w, bias=bias, scale=scale, shape=shape, params=params, epi=epi, y_new=mk(), y_ref=mk())
+
+
+def test_noalloc_conv_matches_existing_entry_on_two_calls_in_a_row(cuda_lib):
+    cases = [
+        # MobileNetV2 stem (3x3/2, C = 3 -> 32), int8 requant with ReLU
+        _case(7, (2, 128, 128, 3, 3, 3, 32), (1, 1, 2, 2, 1, 1, 1), (_lib.OUT_S8, 0, 0, 127), torch.int8),
+        # ResNet-50 stem geometry (7x7/2, C = 3 -> 64), int32 accumulators + bias
+        _case(11, (3, 64, 64, 3, 7, 7, 64), (3, 3, 2, 2, 1, 1, 1), (_lib.OUT_S32, 0, 0, 0), torch.int32),
+    ]
+    for cs in cases:  # two no-alloc calls back to back; the second overwrites the shared scratch
+        rc = _call("b200q_conv2d_s8_packed_noalloc", cs["x"], cs["w"], cs["bias"], cs["scale"], cs["y_new"],
+                   cs["shape"], cs["params"], cs["epi"])
+        assert rc == 0, _lib.lib().b200q_last_error()
+    for cs in cases:
+        rc = _call("b200q_conv2d_s8", cs["x"], cs["w"], cs["bias"], cs["scale"], cs["y_ref"], cs["shape"],
+                   cs["params"], cs["epi"])
+        assert rc == 0, _lib.lib().b200q_last_error()
+    torch.cuda.synchronize()
+    assert _lib.lib().b200q_device_error() == 0
+    for cs in cases:
+        assert torch.equal(cs["y_new"], cs["y_ref"])
+
+
+def test_noalloc_conv_rejects_requests_beyond_its_scratch(cuda_lib):
+    cap = int(_lib.lib().b200q_noalloc_scratch_bytes())
+    assert cap == 32 << 20
+    # 64 x 112 x 112 output rows x 32 bytes = 25.7 MB fits; 96 images (38.5 MB) does not
+    big = _case(3, (96, 224, 224, 3, 3, 3, 32), (1, 1, 2, 2, 1, 1, 1), (_lib.OUT_S8, 0, -128, 127), torch.int8)
+    rc = _call("b200q_conv2d_s8_packed_noalloc", big["x"], big["w"], big["bias"], big["scale"], big["y_new"],
+               big["shape"], big["params"], big["epi"])
+    assert rc == _lib.B200Q_ERR_INVALID_ARG
+    assert b"maximum" in _lib.lib().b200q_last_error()
