@@ -543,8 +543,11 @@ int b200q_conv2d_s8(const int8_t* d_x, const int8_t* d_w, const int32_t* d_bias,
     return launch_tc(*st, ma, mb, a, cs);
   }
   // Low-channel convolutions (C % 16 != 0): im2col pack into the stream's workspace, then tcgen05.
+  // (tc_ok was false here, so a C % 16 == 0 conv reaching this point is one im2col TMA cannot take.)
   const int kp_packed = (r * s * c + 31) / 32 * 32;
-  if (g_policy.load() == 0 && g.groups == 1 && c % 16 != 0 && M >= 4096 && M < (1ll << 31) && kp_packed <= 4096 &&
+  // Also taken by groups == 1 convs the im2col TMA cannot read (activations < 128 KiB, corner limits).
+  if (g_policy.load() == 0 && g.groups == 1 && (c % 16 != 0 ? M >= 4096 : M >= 64) && M < (1ll << 31) &&
+      kp_packed <= 16384 &&
       aligned16(d_y) && (!d_bias || aligned16(d_bias)) && (!d_scale || aligned16(d_scale))) {
     void* ws = nullptr;
     rc = get_workspace(packed_scratch_bytes(M, k, kp_packed), cs, &ws);

@@ -167,7 +167,8 @@ def test_conv_s8_tcgen05_pointwise(cuda_lib, shape):
     ((2, 23, 23, 3, 7, 7, 64, 3, 2, 1), 1, "cuda-core-generic"),      # stem C = 3
     ((1, 12, 12, 24, 1, 1, 40, 0, 1, 1), 1, "cuda-core-generic"),     # C % 32 != 0
     ((2, 9, 9, 32, 3, 3, 64, 1, 1, 1), 2, "cuda-core-generic"),       # grouped
-    ((1, 8, 8, 64, 3, 3, 64, 1, 1, 1), 1, "cuda-core-generic"),       # tiny tensor (< 128 KiB)
+    ((1, 6, 6, 64, 3, 3, 64, 1, 1, 1), 1, "cuda-core-generic"),       # tiny tensor (36 output rows)
+    ((2, 14, 14, 256, 3, 3, 256, 1, 1, 1), 1, "tcgen05-packed"),      # < 128 KiB: packed, not im2col
 ])
 def test_conv_s8_cuda_core_paths(cuda_lib, shape, groups, expect):
     b2q = _b2q()
