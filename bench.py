@@ -340,6 +340,163 @@ def run_reference(args) -> dict:
     }
 
 
+# ------------------------------------------------------------------ other BASELINE configs
+
+NET_BATCH = {"resnet50": 256, "mobilenetv2": 512}
+
+
+def run_net(args, rank: int, world: int, local_rank: int) -> dict | None:
+    """Configs 3 / 5: every conv of the network once per step over the per-GPU batch, each layer on
+    its own resident synthetic input (max-pool and residual adds are not part of the conv path)."""
+    import torch
+
+    import my_own_cnn_b200 as b2q
+    from my_own_cnn_b200 import _lib, nets
+    from my_own_cnn_b200.shard import checksum, gather_tensors, max_over_ranks
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    stream = torch.cuda.current_stream()
+    specs = nets.NETS[args.config]()
+    batch = args.batch or NET_BATCH[args.config]
+    data = nets.NetData(specs, batch, SEED, dev, image_offset=rank)
+    flush = torch.empty(256 << 20, dtype=torch.int8, device=dev)
+    for _ in range(args.warmup):
+        data.run()
+    paths = []
+    for i in range(len(specs)):
+        data.run_layer(i)
+        paths.append(b2q.last_path())
+    torch.cuda.synchronize()
+    n = len(specs)
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(n + 1)] for _ in range(args.steps)]
+    sampler = ClockSampler()
+    if rank == 0:
+        sampler.start()
+    launches0 = b2q.tc_launch_count()
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    for st in range(args.steps):
+        flush.fill_(st & 0x7F)
+        evs[st][0].record(stream)
+        for i in range(n):
+            data.run_layer(i)
+            evs[st][i + 1].record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    clocks = sampler.stop() if rank == 0 else None
+    launches = b2q.tc_launch_count() - launches0
+    if _lib.lib().b200q_device_error() != 0:
+        raise RuntimeError(_lib.lib().b200q_last_error().decode())
+    layer_ms = [sum(evs[st][i].elapsed_time(evs[st][i + 1]) for st in range(args.steps)) / args.steps
+                for i in range(n)]
+    step_ms = sum(layer_ms)
+    (step_ms,) = max_over_ranks([step_ms], device=dev)
+    chk = torch.cat([checksum(data.layers[-1][5]), checksum(data.layers[0][5])])
+    checksums = [g.tolist() for g in gather_tensors(chk)]
+    if rank != 0:
+        return None
+    peaks = load_peaks()
+    int8_peak = 2.0 * peaks["bf16_tflops"]
+    ops = [sp.ops_per_image() * batch for sp in specs]
+    by_path = {}
+    for sp, pth, ms, o in zip(specs, paths, layer_ms, ops):
+        d = by_path.setdefault(pth, {"layers": 0, "ms": 0.0, "gop": 0.0, "bytes": 0})
+        ho, wo = sp.out_hw()
+        d["layers"] += 1
+        d["ms"] += ms
+        d["gop"] += o / 1e9
+        d["bytes"] += batch * (sp.h * sp.w * sp.c + ho * wo * sp.k) + sp.k * sp.r * sp.r * (sp.c // sp.groups)
+    for d in by_path.values():
+        d["share"] = round(d["ms"] / step_ms, 4)
+        d["tops"] = round(d["gop"] / d["ms"], 1) if d["ms"] else None
+        d["gbs"] = round(d["bytes"] / d["ms"] / 1e6, 1) if d["ms"] else None
+        d["ms"] = round(d["ms"], 4)
+        d["gop"] = round(d["gop"], 2)
+    tc = [v for k, v in by_path.items() if k.startswith("tcgen05")]
+    tc_ms = sum(v["ms"] for v in tc)
+    tc_tops = sum(v["gop"] for v in tc) / tc_ms if tc_ms else 0.0
+    out = {
+        "metric": METRIC, "value": round(world * batch / (step_ms * 1e-3), 1), "unit": "images/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_ms, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "s8xs8->s32",
+        "data": "synthetic (seeded splitmix64; half-normal / normal int8 codes via quantile tables)",
+        "config": {"workload": f"{args.config} conv stack, per-GPU batch {batch}, every conv on fresh input",
+                   "global_batch": batch * world, "per_gpu_batch": batch, "parallelism": f"dp{world} (batch shards)",
+                   "l2": "flushed between timed steps (256 MiB write outside the events)"},
+        "tops_per_gpu": round(sum(ops) / (step_ms * 1e-3) / 1e12, 1),
+        "frac_of_int8_peak": round(sum(ops) / (step_ms * 1e-3) / 1e12 / int8_peak, 4),
+        "by_path": by_path,
+        "roofline": {"bound": "tensor", "achieved": round(tc_tops, 1), "peak": round(int8_peak, 1), "unit": "TOP/s",
+                     "frac": round(tc_tops / int8_peak, 4), "traffic": None, "kernel": "tc_gemm_s8_kernel (all layers)",
+                     "peak_source": f"2 x bf16_tflops ({peaks['source']})"},
+        "gpu_launches": int(launches), "clocks": clocks,
+        "slowest_layers": sorted(({"layer": sp.name, "path": pth, "ms": round(ms, 4),
+                                   "tops": round(o / ms / 1e9, 1)} for sp, pth, ms, o in zip(specs, paths, layer_ms, ops)),
+                                 key=lambda d: -d["ms"])[:6],
+        "verify": {"checksums_last_first_per_rank": checksums},
+    }
+    if "cuda-core-depthwise" in by_path:
+        d = by_path["cuda-core-depthwise"]
+        out["roofline_depthwise"] = {"bound": "hbm", "achieved": d["gbs"], "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                                     "frac": round(d["gbs"] / peaks["hbm_gbs"], 4)}
+    return out
+
+
+def run_bmm(args, rank: int, world: int, local_rank: int) -> dict | None:
+    """Config 2: batch 64 of 1024^3 int8 NN GEMMs per GPU, int32 accumulators and the per-column
+    requantized int8 variant (two launches per step)."""
+    import torch
+
+    import my_own_cnn_b200 as b2q
+    from my_own_cnn_b200 import synth
+    from my_own_cnn_b200.shard import max_over_ranks
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    stream = torch.cuda.current_stream()
+    batch, M = 64, 1024
+    A = synth.fill_s8_uniform(torch.empty((batch, M, M), dtype=torch.int8, device=dev), SEED + rank, 101)
+    B = synth.fill_s8_uniform(torch.empty((batch, M, M), dtype=torch.int8, device=dev), SEED + rank, 102)
+    sc = torch.from_numpy(synth.scales_f32(M, SEED, 103)).to(dev)
+    C32 = torch.empty((batch, M, M), dtype=torch.int32, device=dev)
+    C8 = torch.empty((batch, M, M), dtype=torch.int8, device=dev)
+    flush = torch.empty(256 << 20, dtype=torch.int8, device=dev)
+    e32, e8 = b2q.Epilogue.int32(), b2q.Epilogue.int8()
+    for _ in range(args.warmup):
+        b2q.bmm_s8_into(C32, A, B, None, None, batch, M, M, M, 0, 0, e32)
+        b2q.bmm_s8_into(C8, A, B, None, sc, batch, M, M, M, 0, 0, e8)
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    torch.cuda.synchronize()
+    for st in range(args.steps):
+        flush.fill_(st & 0x7F)
+        ev[st][0].record(stream)
+        b2q.bmm_s8_into(C32, A, B, None, None, batch, M, M, M, 0, 0, e32)
+        ev[st][1].record(stream)
+        b2q.bmm_s8_into(C8, A, B, None, sc, batch, M, M, M, 0, 0, e8)
+        ev[st][2].record(stream)
+    torch.cuda.synchronize()
+    t32 = sum(e[0].elapsed_time(e[1]) for e in ev) / args.steps
+    t8 = sum(e[1].elapsed_time(e[2]) for e in ev) / args.steps
+    t32, t8 = max_over_ranks([t32, t8], device=dev)
+    if rank != 0:
+        return None
+    peaks = load_peaks()
+    ops = 2 * batch * M ** 3
+    bytes32 = 2 * batch * M * M + 4 * batch * M * M
+    return {"metric": "int8 bmm TOPS/GPU (config 2)", "value": round(world * 2 * ops / ((t32 + t8) * 1e-3) / 1e12, 1),
+            "unit": "TOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(t32 + t8, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "s8xs8->s32", "data": "synthetic (seeded splitmix64)",
+            "config": {"workload": "config2 bmm batch 64, M=N=K=1024, NN, int32 out + per-column int8 requant out"},
+            "int32_out": {"ms": round(t32, 4), "tops": round(ops / t32 / 1e9, 1),
+                          "hbm_gbs": round(bytes32 / t32 / 1e6, 1), "hbm_frac": round(bytes32 / t32 / 1e6 / peaks["hbm_gbs"], 4)},
+            "int8_out": {"ms": round(t8, 4), "tops": round(ops / t8 / 1e9, 1),
+                         "frac_of_int8_peak": round(ops / t8 / 1e9 / (2 * peaks["bf16_tflops"]), 4)}}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -349,6 +506,9 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--chunk", type=int, default=64, help="images per chunk of the e2e pipeline")
+    ap.add_argument("--config", default="pointwise", choices=["pointwise", "resnet50", "mobilenetv2", "bmm"],
+                    help="pointwise (BASELINE config 4, the default bench line); the others report configs 3 / 5 / 2")
+    ap.add_argument("--batch", type=int, default=0, help="per-GPU batch for the network configs (0 = BASELINE)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -368,7 +528,12 @@ def main():
 
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
-    out = run_ours(args, rank, world, local_rank)
+    if args.config in NET_BATCH:
+        out = run_net(args, rank, world, local_rank)
+    elif args.config == "bmm":
+        out = run_bmm(args, rank, world, local_rank)
+    else:
+        out = run_ours(args, rank, world, local_rank)
     if out is not None:
         print(json.dumps(out), flush=True)
     if world > 1:
