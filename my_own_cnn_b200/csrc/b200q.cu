@@ -340,8 +340,13 @@ int run_packed_conv(const DeviceState& st, const int8_t* x, const int8_t* w, voi
   const int kp = (rsc + 31) / 32 * 32;
   int8_t* a_buf = scratch;
   int8_t* w_buf = scratch + round256(static_cast<size_t>(rows) * kp);
-  im2col_pack_s8_kernel<<<grid_for(static_cast<size_t>(rows) * (kp / 4), 256, st.sms), 256, 0, stream>>>(
-      x, a_buf, g, kp, rows);
+  int tile_rows = 16384 / kp;
+  if (tile_rows > 64) tile_rows = 64;
+  if (tile_rows < 1) tile_rows = 1;
+  const long long blocks_needed = (rows + tile_rows - 1) / tile_rows;
+  const int pack_grid = static_cast<int>(blocks_needed < st.sms * 16ll ? blocks_needed : st.sms * 16ll);
+  im2col_pack_s8_kernel<<<pack_grid, 256, static_cast<size_t>(tile_rows) * kp, stream>>>(x, a_buf, g, kp, rows,
+                                                                                        tile_rows);
   int rc = check_launch("im2col_pack_s8_kernel launch");
   if (rc) return rc;
   weight_pad_s8_kernel<<<grid_for(static_cast<size_t>(g.k) * kp, 256, st.sms), 256, 0, stream>>>(w, w_buf, g.k, rsc,
@@ -556,9 +561,19 @@ int b200q_conv2d_s8(const int8_t* d_x, const int8_t* d_w, const int32_t* d_bias,
     return run_packed_conv(*st, d_x, d_w, d_y, g, e, static_cast<int8_t*>(ws), cs);
   }
   const size_t total = static_cast<size_t>(M) * k;
-  if (g.groups == c && k == c && c % 16 == 0 && r * s * c <= 48 * 1024 && aligned16(d_x) && aligned16(d_y)) {
-    const size_t items = static_cast<size_t>(M) * (c / 16);
-    dw_conv_s8_kernel<<<grid_for(items, 256, st->sms), 256, r * s * c, cs>>>(d_x, d_w, d_y, g, e);
+  if (g.groups == c && k == c && c % 8 == 0 && c <= 8 * 256 && r == 3 && s == 3 && M < (1ll << 31) &&
+      aligned16(d_x) &&
+      aligned16(d_y)) {
+    const int groups8 = c / 8;
+    const int lanes = 256 / groups8;
+    const long long blocks = (M + lanes - 1) / lanes;
+    const int grid = static_cast<int>(blocks < st->sms * 8ll ? blocks : st->sms * 8ll);
+    if (e.out_kind == kOutS8)
+      dw_conv_s8_kernel<kOutS8><<<grid, 256, 0, cs>>>(d_x, d_w, d_y, g, e);
+    else if (e.out_kind == kOutS32)
+      dw_conv_s8_kernel<kOutS32><<<grid, 256, 0, cs>>>(d_x, d_w, d_y, g, e);
+    else
+      dw_conv_s8_kernel<kOutF32><<<grid, 256, 0, cs>>>(d_x, d_w, d_y, g, e);
     g_last_path = 4;
     return check_launch("dw_conv_s8_kernel launch");
   }

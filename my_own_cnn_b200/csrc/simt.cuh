@@ -99,69 +99,99 @@ __global__ void conv_s8_generic_kernel(const int8_t* __restrict__ x, const int8_
   }
 }
 
-// Depthwise int8 conv (groups == C == K): one thread = one output pixel x 16 channels.
-// Weights [C][R][S] are staged transposed as [R*S][C] in shared memory.
-__global__ void dw_conv_s8_kernel(const int8_t* __restrict__ x, const int8_t* __restrict__ w,
-                                  void* __restrict__ y, ConvGeom g, Epilogue e) {
-  extern __shared__ __align__(16) int8_t wsm[];  // [r*s][c]
-  const int taps = g.r * g.s;
-  for (int i = threadIdx.x; i < taps * g.c; i += blockDim.x) {
-    const int ch = i % g.c, t = i / g.c;
-    wsm[i] = w[static_cast<size_t>(ch) * taps + t];
+// Depthwise int8 conv, 3x3 taps (groups == C == K, C % 8 == 0).  A thread owns 8 channels
+// (cgroup) for a strided set of output pixels.  Per pixel it loads the 8 channels of each tap
+// (one 8-byte load; consecutive threads take consecutive channel groups of the same pixel, so a
+// warp's loads are contiguous), byte-transposes the words of taps 0-3 and 4-7 with 8 prmt per
+// 4x4 block so that one word holds one channel's 4 taps, and accumulates with dp4a against the
+// channel's packed weights (4 MACs per instruction).  Tap 8 uses a weight pre-shifted into the
+// channel's byte lane, so a dp4a with the raw activation word picks exactly that channel.
+constexpr int kDwMaxTaps = 9;
+
+// 4x4 byte transpose: in[i] byte j -> out[j] byte i.
+__device__ __forceinline__ void transpose4x4_bytes(uint32_t a, uint32_t b, uint32_t c, uint32_t d, uint32_t& o0,
+                                                   uint32_t& o1, uint32_t& o2, uint32_t& o3) {
+  const uint32_t t0 = __byte_perm(a, b, 0x5140), t1 = __byte_perm(c, d, 0x5140);
+  const uint32_t t2 = __byte_perm(a, b, 0x7362), t3 = __byte_perm(c, d, 0x7362);
+  o0 = __byte_perm(t0, t1, 0x5410);
+  o1 = __byte_perm(t0, t1, 0x7632);
+  o2 = __byte_perm(t2, t3, 0x5410);
+  o3 = __byte_perm(t2, t3, 0x7632);
+}
+
+template <int KIND>
+__global__ void __launch_bounds__(256) dw_conv_s8_kernel(const int8_t* __restrict__ x, const int8_t* __restrict__ w,
+                                                         void* __restrict__ y, ConvGeom g, Epilogue e) {
+  const int groups8 = g.c >> 3;
+  const int lanes_per_block = blockDim.x / groups8;  // pixels handled by one block at a time
+  const int cg = threadIdx.x % groups8;
+  const int pl = threadIdx.x / groups8;
+  if (pl >= lanes_per_block) return;
+  const int c0 = cg * 8;
+  // packed weights: wq[j][0] = taps 0-3 of channel c0+j, wq[j][1] = taps 4-7; w8[j] = tap 8 shifted
+  uint32_t wq[8][2], w8[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int8_t* wp = w + static_cast<size_t>(c0 + j) * 9;
+    uint32_t v[9];
+#pragma unroll
+    for (int t = 0; t < 9; ++t) v[t] = static_cast<uint8_t>(__ldg(wp + t));
+    wq[j][0] = v[0] | (v[1] << 8) | (v[2] << 16) | (v[3] << 24);
+    wq[j][1] = v[4] | (v[5] << 8) | (v[6] << 16) | (v[7] << 24);
+    w8[j] = v[8] << (8 * (j & 3));
   }
-  __syncthreads();
-  const int cgroups = g.c >> 4;
-  const size_t total = static_cast<size_t>(g.n) * g.ho * g.wo * cgroups;
-  for (size_t idx = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; idx < total;
-       idx += static_cast<size_t>(gridDim.x) * blockDim.x) {
-    const int cgi = static_cast<int>(idx % cgroups);
-    size_t pix = idx / cgroups;
-    const int wo = static_cast<int>(pix % g.wo);
-    pix /= g.wo;
-    const int ho = static_cast<int>(pix % g.ho);
-    const int n = static_cast<int>(pix / g.ho);
-    const int c0 = cgi << 4;
-    int32_t acc[16];
+  int32_t bsum[8];
+  float sc[8];
 #pragma unroll
-    for (int j = 0; j < 16; ++j) acc[j] = 0;
-    for (int rr = 0; rr < g.r; ++rr) {
-      const int hi = ho * g.stride_h - g.pad_h + rr * g.dil_h;
-      if (hi < 0 || hi >= g.h) continue;
-      for (int ss = 0; ss < g.s; ++ss) {
-        const int wi = wo * g.stride_w - g.pad_w + ss * g.dil_w;
-        if (wi < 0 || wi >= g.w) continue;
-        const int4 xv = __ldg(reinterpret_cast<const int4*>(x + ((static_cast<size_t>(n) * g.h + hi) * g.w + wi) * g.c + c0));
-        const int4 wv = *reinterpret_cast<const int4*>(wsm + (rr * g.s + ss) * g.c + c0);
-        const int xa[4] = {xv.x, xv.y, xv.z, xv.w};
-        const int wa[4] = {wv.x, wv.y, wv.z, wv.w};
+  for (int j = 0; j < 8; ++j) {
+    bsum[j] = e.bias ? __ldg(e.bias + c0 + j) : 0;
+    sc[j] = e.scale ? __ldg(e.scale + c0 + j) : 0.0f;
+  }
+  const int npix = g.n * g.ho * g.wo;  // < 2^31 (checked by the caller)
+  const int row_pitch = g.w * g.c;
+  for (int pix = blockIdx.x * lanes_per_block + pl; pix < npix; pix += gridDim.x * lanes_per_block) {
+    const int wo = pix % g.wo;
+    const int t2 = pix / g.wo;
+    const int ho = t2 % g.ho;
+    const int n = t2 / g.ho;
+    const int h0 = ho * g.stride_h - g.pad_h, w0 = wo * g.stride_w - g.pad_w;
+    const int8_t* base = x + (static_cast<size_t>(n) * g.h * g.w) * g.c + c0;
+    uint32_t xl[9], xh[9];  // channels 0-3 / 4-7 of each tap (0 at padding)
 #pragma unroll
-        for (int q = 0; q < 4; ++q)
+    for (int t = 0; t < 9; ++t) {
+      const int hi = h0 + (t / 3) * g.dil_h, wi = w0 + (t % 3) * g.dil_w;
+      uint2 v = make_uint2(0u, 0u);
+      if (hi >= 0 && hi < g.h && wi >= 0 && wi < g.w)
+        v = __ldg(reinterpret_cast<const uint2*>(base + hi * row_pitch + wi * g.c));
+      xl[t] = v.x;
+      xh[t] = v.y;
+    }
+    int acc[8];
 #pragma unroll
-          for (int b = 0; b < 4; ++b) {
-            const int xb = static_cast<int>(static_cast<uint32_t>(xa[q]) << (24 - 8 * b)) >> 24;  // sign-extended byte b
-            const int wb = static_cast<int>(static_cast<uint32_t>(wa[q]) << (24 - 8 * b)) >> 24;
-            acc[4 * q + b] += xb * wb;
-          }
+    for (int half = 0; half < 2; ++half) {
+      const uint32_t* xs = half ? xh : xl;
+      uint32_t c[4], d[4];
+      transpose4x4_bytes(xs[0], xs[1], xs[2], xs[3], c[0], c[1], c[2], c[3]);
+      transpose4x4_bytes(xs[4], xs[5], xs[6], xs[7], d[0], d[1], d[2], d[3]);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int ch = half * 4 + j;
+        int a = __dp4a(static_cast<int>(c[j]), static_cast<int>(wq[ch][0]), 0);
+        a = __dp4a(static_cast<int>(d[j]), static_cast<int>(wq[ch][1]), a);
+        acc[ch] = __dp4a(static_cast<int>(xs[8]), static_cast<int>(w8[ch]), a);
       }
     }
-    const size_t obase = idx << 4;  // == ((n*ho + ho)*wo + wo)*C + c0
-    if (e.out_kind == kOutS8) {
-      uint32_t pk[4];
+    const size_t o = static_cast<size_t>(pix) * g.c + c0;
+    if constexpr (KIND == kOutS8) {
+      int q[8];
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        uint32_t word = 0;
-#pragma unroll
-        for (int b = 0; b < 4; ++b) {
-          const int ch = c0 + 4 * q + b;
-          const int32_t t = e.bias ? wrap_add(acc[4 * q + b], __ldg(e.bias + ch)) : acc[4 * q + b];
-          word |= (static_cast<uint32_t>(requant_one(t, __ldg(e.scale + ch), e)) & 0xFFu) << (8 * b);
-        }
-        pk[q] = word;
-      }
-      *reinterpret_cast<int4*>(static_cast<int8_t*>(y) + obase) = make_int4(pk[0], pk[1], pk[2], pk[3]);
+      for (int j = 0; j < 8; ++j) q[j] = requant_one(wrap_add(acc[j], bsum[j]), sc[j], e);
+      const uint32_t lo = __byte_perm(__byte_perm(q[0], q[1], 0x0040), __byte_perm(q[2], q[3], 0x0040), 0x5410);
+      const uint32_t hi = __byte_perm(__byte_perm(q[4], q[5], 0x0040), __byte_perm(q[6], q[7], 0x0040), 0x5410);
+      *reinterpret_cast<uint2*>(static_cast<int8_t*>(y) + o) = make_uint2(lo, hi);
     } else {
 #pragma unroll
-      for (int j = 0; j < 16; ++j) epilogue_store(e, y, obase + j, acc[j], c0 + j);
+      for (int j = 0; j < 8; ++j) epilogue_store(e, y, o + j, acc[j], c0 + j);
     }
   }
 }
@@ -257,37 +287,51 @@ namespace b200q {
 // Low-channel convolutions (C % 16 != 0, e.g. the C = 3 stems) on the tensor cores: the
 // activation rows are gathered into an im2col matrix a[m][kp] with kp = round_up(R*S*C, 32),
 // columns ordered (r, s, c) like the KRSC weights, zero at padding taps and past R*S*C.
-// One thread writes 4 consecutive bytes of a row.
-__global__ void im2col_pack_s8_kernel(const int8_t* __restrict__ x, int8_t* __restrict__ a, ConvGeom g, int kp,
-                                      long long rows) {
-  const int words = kp >> 2;
+// A block builds `rows` consecutive matrix rows in shared memory (one thread per (row, tap)
+// copies the tap's C channels) and then writes the tile -- contiguous in the matrix -- with
+// 16-byte stores.
+__global__ void __launch_bounds__(256) im2col_pack_s8_kernel(const int8_t* __restrict__ x, int8_t* __restrict__ a,
+                                                             ConvGeom g, int kp, long long total_rows, int rows) {
+  extern __shared__ __align__(16) int8_t tile[];
   const int rsc = g.r * g.s * g.c;
-  const size_t total = static_cast<size_t>(rows) * words;
-  for (size_t idx = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; idx < total;
-       idx += static_cast<size_t>(gridDim.x) * blockDim.x) {
-    const long long m = static_cast<long long>(idx / words);
-    const int k0 = static_cast<int>(idx - static_cast<size_t>(m) * words) * 4;
-    const int wo = static_cast<int>(m % g.wo);
-    const long long t = m / g.wo;
-    const int ho = static_cast<int>(t % g.ho);
-    const int n = static_cast<int>(t / g.ho);
-    uint32_t word = 0;
-#pragma unroll
-    for (int b = 0; b < 4; ++b) {
-      const int kk = k0 + b;
-      if (kk < rsc) {
-        const int c = kk % g.c;
-        const int tap = kk / g.c;
-        const int ss = tap % g.s, rr = tap / g.s;
-        const int hi = ho * g.stride_h - g.pad_h + rr * g.dil_h;
+  for (long long m0 = static_cast<long long>(blockIdx.x) * rows; m0 < total_rows;
+       m0 += static_cast<long long>(gridDim.x) * rows) {
+    const int nrows = static_cast<int>(min(static_cast<long long>(rows), total_rows - m0));
+    // zero the padding columns [rsc, kp) of every row
+    const int padw = kp - rsc;
+    if (padw > 0)
+      for (int i = threadIdx.x; i < nrows * padw; i += blockDim.x) tile[(i / padw) * kp + rsc + i % padw] = 0;
+    // one work item = (row, filter row rr): S taps x C channels, coordinates decoded once
+    for (int it = threadIdx.x; it < nrows * g.r; it += blockDim.x) {
+      const int lr = it / g.r;
+      const int rr = it - lr * g.r;
+      const int m = static_cast<int>(m0) + lr;  // < 2^31 (checked by the caller)
+      const int wo = m % g.wo;
+      const int t = m / g.wo;
+      const int ho = t % g.ho;
+      const int n = t / g.ho;
+      const int hi = ho * g.stride_h - g.pad_h + rr * g.dil_h;
+      int8_t* dst = tile + lr * kp + rr * g.s * g.c;
+      if (hi < 0 || hi >= g.h) {
+        for (int i = 0; i < g.s * g.c; ++i) dst[i] = 0;
+        continue;
+      }
+      const int8_t* row = x + (static_cast<size_t>(n) * g.h + hi) * g.w * g.c;
+      for (int ss = 0; ss < g.s; ++ss) {
         const int wi = wo * g.stride_w - g.pad_w + ss * g.dil_w;
-        if (hi >= 0 && hi < g.h && wi >= 0 && wi < g.w) {
-          const int8_t v = __ldg(x + ((static_cast<size_t>(n) * g.h + hi) * g.w + wi) * g.c + c);
-          word |= (static_cast<uint32_t>(static_cast<uint8_t>(v))) << (8 * b);
+        if (wi >= 0 && wi < g.w) {
+          const int8_t* src = row + static_cast<size_t>(wi) * g.c;
+          for (int c = 0; c < g.c; ++c) dst[ss * g.c + c] = __ldg(src + c);
+        } else {
+          for (int c = 0; c < g.c; ++c) dst[ss * g.c + c] = 0;
         }
       }
     }
-    reinterpret_cast<uint32_t*>(a)[idx] = word;
+    __syncthreads();
+    int4* out = reinterpret_cast<int4*>(a + m0 * kp);
+    const int4* src = reinterpret_cast<const int4*>(tile);
+    for (int i = threadIdx.x; i < nrows * kp / 16; i += blockDim.x) out[i] = src[i];
+    __syncthreads();
   }
 }
 
