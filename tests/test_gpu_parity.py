@@ -355,3 +355,31 @@ def test_conv_stack_pipelined_host_pass_matches_oracle(cuda_lib):
     ref = oracle.conv_s8(oracle.conv_args(n, h, w, k1, 1, 1, k2, 0, 0), y1, w2, threads=4)
     np.testing.assert_array_equal(yh.numpy(), ref)
     np.testing.assert_array_equal(y_dev.numpy(), ref)
+
+
+def test_matches_reference_gpu_implementation(cuda_lib):
+    """The reference's own CUDA quantized conv (compiled unmodified into oracle/_ref/libref_gpu.so)
+    and this library give identical int32 accumulators, on the tensor-core and CUDA-core paths."""
+    import ctypes
+
+    b2q = _b2q()
+    lib = ROOT / "oracle" / "_ref" / "libref_gpu.so"
+    if not lib.exists():
+        pytest.skip("reference GPU library not built (needs the reference sources at build time)")
+    ref = ctypes.CDLL(str(lib))
+    ref.refgpu_fprop_qi32_s5.argtypes = [ctypes.c_void_p] * 3 + [ctypes.c_int] * 9 + [ctypes.c_void_p] * 2
+    for (n, h, w, c, r, k, pad, st) in [(2, 40, 40, 64, 3, 96, 1, 1), (3, 14, 14, 256, 1, 128, 0, 1),
+                                        (2, 23, 23, 3, 7, 64, 3, 2), (1, 9, 9, 24, 3, 8, 1, 2)]:
+        x8 = torch.from_numpy(rng_s8(n + c, (n, h, w, c))).cuda()
+        w8 = torch.from_numpy(rng_s8(k + r, (k, r, r, c))).cuda()
+        p = b2q.Conv2DParams(pad, pad, st, st, 1, 1, 1)
+        ho, wo = b2q.conv_out_shape(h, w, c, r, r, k, p)
+        y_ref = torch.zeros((n, ho, wo, k), dtype=torch.int32, device="cuda")
+        qp_in = b2q.qparams_to_device([b2q.QuantizationParametersS5(0, 31, 1.0)] * n)
+        qp_f = b2q.qparams_to_device([b2q.QuantizationParametersS5(0, 31, 1.0)])
+        xf, wf = x8.float(), w8.float()
+        assert ref.refgpu_fprop_qi32_s5(xf.data_ptr(), wf.data_ptr(), y_ref.data_ptr(), n, h, w, c, r, r, k, pad, st,
+                                        qp_in.data_ptr(), qp_f.data_ptr()) == 0
+        y = b2q.conv2d_s8(x8, w8, None, None, p, b2q.Epilogue.int32())
+        torch.cuda.synchronize()
+        assert torch.equal(y, y_ref), (n, h, w, c, r, k)
