@@ -183,6 +183,20 @@ int encode_out_4b(CUtensorMap* map, void* base, uint64_t n, uint64_t m, uint64_t
   return B200Q_OK;
 }
 
+// int8 output [batch][M][N] as a 3-D map with 32 x 32 boxes and the 32-byte swizzle of the
+// epilogue's staging buffers.
+int encode_out_1b(CUtensorMap* map, void* base, uint64_t n, uint64_t m, uint64_t batch) {
+  cuuint64_t dims[3] = {n, m, batch};
+  cuuint64_t strides[2] = {n, n * m};
+  cuuint32_t box[3] = {32, 32, 1};
+  cuuint32_t es[3] = {1, 1, 1};
+  CUresult r = g_encode_tiled(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, base, dims, strides, box, es,
+                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_32B,
+                              CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(B200Q_ERR_CUDA, "cuTensorMapEncodeTiled (int8 output) failed (%d)", (int)r);
+  return B200Q_OK;
+}
+
 int encode_im2col(CUtensorMap* map, const int8_t* x, const ConvGeom& g, int bk) {
   cuuint64_t dims[4] = {(cuuint64_t)g.c, (cuuint64_t)g.w, (cuuint64_t)g.h, (cuuint64_t)g.n};
   cuuint64_t strides[3] = {(cuuint64_t)g.c, (cuuint64_t)g.c * g.w, (cuuint64_t)g.c * g.w * g.h};
@@ -210,6 +224,12 @@ int pick_bn(int n, int mn_major_b) {
   return 256;
 }
 
+// int8 TMA-store epilogue switch (env B200Q_S8_TMA_STORE=0 turns it off, for A/B timing).
+const bool g_s8_tma_store = [] {
+  const char* v = getenv("B200Q_S8_TMA_STORE");
+  return !(v && v[0] == '0');
+}();
+
 int launch_tc(const DeviceState& st, const CUtensorMap& ma, const CUtensorMap& mb, TcArgs a, cudaStream_t stream) {
   // 4-byte outputs go through shared memory and TMA stores when the row pitch allows a tensor map.
   CUtensorMap mc = ma;  // unused placeholder when tma_store == 0
@@ -224,7 +244,20 @@ int launch_tc(const DeviceState& st, const CUtensorMap& ma, const CUtensorMap& m
   // Stage per-column bias / scale in shared memory when they fit (4096 columns = 32 KiB).
   a.stage_cols = (a.epi.out_kind != kOutS32 || a.epi.bias) && a.N <= 4096 ? (a.N + 31) / 32 * 32 : 0;
   a.default_clamp = a.epi.out_kind == kOutS8 && a.epi.zp == 0 && a.epi.lo == -128 && a.epi.hi == 127;
-  const int epi_bytes = a.stage_cols * 8 + (a.tma_store ? 1024 + kTcEpiWarps * 2 * kEpiStageBytes : 0);
+  // int8 outputs: TMA stores when the row pitch allows a map and every 32-column chunk can read
+  // its bias / scale (staged columns are zero-padded to a multiple of 32).  GEMMs with a reduction
+  // shorter than 128 keep direct stores: there the epilogue alone sets the pace and the staging
+  // round trip measured slower.
+  if (a.epi.out_kind == kOutS8 && g_s8_tma_store && a.num_kb * a.BK >= 128 && a.ldc == a.N && a.N % 16 == 0 &&
+      aligned16(a.out) &&
+      (a.stage_cols > 0 || a.N % 32 == 0) && a.vec_ok) {
+    const uint64_t rows = static_cast<uint64_t>(a.M);
+    int rc = encode_out_1b(&mc, a.out, static_cast<uint64_t>(a.N), rows, static_cast<uint64_t>(a.batch));
+    if (rc) return rc;
+    a.tma_store = 1;
+  }
+  const int stage_out = a.epi.out_kind == kOutS8 ? kEpiStageBytesS8 : kEpiStageBytes;
+  const int epi_bytes = a.stage_cols * 8 + (a.tma_store ? 1024 + kTcEpiWarps * 2 * stage_out : 0);
   int stages = (kSmemLimit - kSmemReserve - epi_bytes) / stage_bytes;
   if (stages > 8) stages = 8;
   if (stages < 2) return fail(B200Q_ERR_UNSUPPORTED, "tile does not fit shared memory");

@@ -48,10 +48,11 @@ struct TcArgs {
   int* err;
   int stage_cols;     // bias/scale columns copied to shared memory at start (0 = read from global)
   int default_clamp;  // int8 output with zp 0 and bounds [-128, 127]: saturating pack does the clamp
-  int tma_store;      // 4-byte outputs leave through shared memory + TMA tensor stores (map tmC)
+  int tma_store;      // outputs leave through shared memory + TMA tensor stores (map tmC)
 };
 
-constexpr int kEpiStageBytes = 32 * 128;  // one warp's 32 rows x 32 four-byte columns
+constexpr int kEpiStageBytes = 32 * 128;   // one warp's 32 rows x 32 four-byte columns
+constexpr int kEpiStageBytesS8 = 32 * 32;  // one warp's 32 rows x 32 int8 columns
 
 __device__ __forceinline__ uint32_t kmajor_layout(int bk) {
   return bk == 128 ? 2u : (bk == 64 ? 4u : 6u);  // SWIZZLE_128B / 64B / 32B
@@ -79,7 +80,7 @@ __device__ __forceinline__ uint32_t pack4_sat_s8(int a, int b, int c, int d) {
 // All array indices are compile-time constants after unrolling: nothing spills to local memory.
 template <int KIND>
 __device__ __forceinline__ void store_chunk(const TcArgs& a, const uint32_t (&v)[32], size_t off, int n, int valid,
-                                            const int32_t* bias, const float* scale) {
+                                            const int32_t* bias, const float* scale, bool has_bias) {
   const Epilogue& e = a.epi;
   if (valid == 32 && a.vec_ok) {
     const int4* bp = reinterpret_cast<const int4*>(bias + n);
@@ -89,7 +90,7 @@ __device__ __forceinline__ void store_chunk(const TcArgs& a, const uint32_t (&v)
     for (int q = 0; q < 8; ++q) {
       int t0 = static_cast<int>(v[4 * q + 0]), t1 = static_cast<int>(v[4 * q + 1]);
       int t2 = static_cast<int>(v[4 * q + 2]), t3 = static_cast<int>(v[4 * q + 3]);
-      if (bias) {
+      if (has_bias) {
         const int4 bb = bp[q];
         t0 = wrap_add(t0, bb.x); t1 = wrap_add(t1, bb.y); t2 = wrap_add(t2, bb.z); t3 = wrap_add(t3, bb.w);
       }
@@ -123,7 +124,7 @@ __device__ __forceinline__ void store_chunk(const TcArgs& a, const uint32_t (&v)
   for (int j = 0; j < 32; ++j) {
     if (j < valid) {
       int t = static_cast<int>(v[j]);
-      if (bias) t = wrap_add(t, bias[n + j]);
+      if (has_bias) t = wrap_add(t, bias[n + j]);
       if constexpr (KIND == kOutS32) {
         static_cast<int32_t*>(a.out)[off + j] = t;
       } else if constexpr (KIND == kOutF32) {
@@ -140,7 +141,8 @@ __device__ __forceinline__ void store_chunk(const TcArgs& a, const uint32_t (&v)
 // and stored by one TMA instruction, which also clips rows >= M and columns >= N.
 template <int KIND>
 __device__ __forceinline__ void stage_chunk_4b(const TcArgs& a, const uint32_t (&v)[32], int n, int lane,
-                                               uint8_t* sbuf, const int32_t* bias, const float* scale) {
+                                               uint8_t* sbuf, const int32_t* bias, const float* scale,
+                                               bool has_bias) {
   const bool full = n + 32 <= a.N;
 #pragma unroll
   for (int q = 0; q < 8; ++q) {
@@ -149,7 +151,7 @@ __device__ __forceinline__ void stage_chunk_4b(const TcArgs& a, const uint32_t (
     for (int i = 0; i < 4; ++i) {
       const int col = n + 4 * q + i;
       t[i] = static_cast<int>(v[4 * q + i]);
-      if (bias && (full || col < a.N)) t[i] = wrap_add(t[i], bias[col]);
+      if (has_bias && (full || col < a.N)) t[i] = wrap_add(t[i], bias[col]);
     }
     uint4 w;
     if constexpr (KIND == kOutS32) {
@@ -167,37 +169,77 @@ __device__ __forceinline__ void stage_chunk_4b(const TcArgs& a, const uint32_t (
   }
 }
 
+// int8 outputs through shared memory: the warp's 32 rows x 32 bytes are written into a
+// 32B-swizzled 1 KiB buffer (16-byte half h of row r at half h ^ ((r / 4) % 2), the layout of a
+// SWIZZLE_32B tensor map: conflict-free for one 16-byte store per lane) and leave with one TMA
+// store, which clips rows >= M and columns >= N.  The requantization is the one of store_chunk.
+__device__ __forceinline__ void stage_chunk_s8(const TcArgs& a, const uint32_t (&v)[32], int n, int lane,
+                                               uint8_t* sbuf, const int32_t* bias, const float* scale,
+                                               bool has_bias) {
+  const Epilogue& e = a.epi;
+  const int4* bp = reinterpret_cast<const int4*>(bias + n);
+  const float4* sp = reinterpret_cast<const float4*>(scale + n);
+  uint32_t packed[8];
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    int t0 = static_cast<int>(v[4 * q + 0]), t1 = static_cast<int>(v[4 * q + 1]);
+    int t2 = static_cast<int>(v[4 * q + 2]), t3 = static_cast<int>(v[4 * q + 3]);
+    if (has_bias) {
+      const int4 bb = bp[q];
+      t0 = wrap_add(t0, bb.x); t1 = wrap_add(t1, bb.y); t2 = wrap_add(t2, bb.z); t3 = wrap_add(t3, bb.w);
+    }
+    const float4 s4 = sp[q];
+    int r0 = __float2int_rn(__fmul_rn(__int2float_rn(t0), s4.x));
+    int r1 = __float2int_rn(__fmul_rn(__int2float_rn(t1), s4.y));
+    int r2 = __float2int_rn(__fmul_rn(__int2float_rn(t2), s4.z));
+    int r3 = __float2int_rn(__fmul_rn(__int2float_rn(t3), s4.w));
+    if (!a.default_clamp) {
+      const int lo = e.lo - e.zp, hi = e.hi - e.zp;
+      r0 = min(max(r0, lo), hi) + e.zp; r1 = min(max(r1, lo), hi) + e.zp;
+      r2 = min(max(r2, lo), hi) + e.zp; r3 = min(max(r3, lo), hi) + e.zp;
+    }
+    packed[q] = pack4_sat_s8(r0, r1, r2, r3);
+  }
+  const int sw = (lane >> 2) & 1;
+  *reinterpret_cast<uint4*>(sbuf + lane * 32 + (sw << 4)) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+  *reinterpret_cast<uint4*>(sbuf + lane * 32 + ((sw ^ 1) << 4)) =
+      make_uint4(packed[4], packed[5], packed[6], packed[7]);
+}
+
 // Epilogue role: 8 warps; warp w reads TMEM lanes 32*(w%4)..+31 (the hardware restricts a warp
 // to the lane quarter w%4) and the chunks of 32 columns with chunk % 2 == (w-2)/4.  The TMEM load
 // of the next chunk is issued before the current chunk is processed (two register buffers).
-template <int KIND>
+template <int KIND, bool TMA>
 __device__ __forceinline__ void emit_chunk(const TcArgs& a, const CUtensorMap* tmC, const uint32_t (&v)[32], int b,
                                            int m, int mrow0, size_t row_off, int n, int lane, uint8_t* sbufs,
-                                           int& sb, const int32_t* bias, const float* scale) {
+                                           int& sb, const int32_t* bias, const float* scale,
+                                           bool has_bias) {
   if (n >= a.N) return;
-  if constexpr (KIND != kOutS8) {
-    if (a.tma_store) {
-      uint8_t* buf = sbufs + sb * kEpiStageBytes;
-      if (lane == 0) bulk_wait_group_read<1>();  // the store that used this buffer has read it
-      __syncwarp();
-      stage_chunk_4b<KIND>(a, v, n, lane, buf, bias, scale);
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) {
-        tma_store_3d(tmC, smem_u32(buf), n, mrow0, b);
-        bulk_commit_group();
-      }
-      sb ^= 1;
-      return;
+  if constexpr (TMA) {
+    uint8_t* buf = sbufs + sb * (KIND == kOutS8 ? kEpiStageBytesS8 : kEpiStageBytes);
+    if (lane == 0) bulk_wait_group_read<1>();  // the store that used this buffer has read it
+    __syncwarp();
+    if constexpr (KIND == kOutS8)
+      stage_chunk_s8(a, v, n, lane, buf, bias, scale, has_bias);
+    else
+      stage_chunk_4b<KIND>(a, v, n, lane, buf, bias, scale, has_bias);
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      tma_store_3d(tmC, smem_u32(buf), n, mrow0, b);
+      bulk_commit_group();
     }
+    sb ^= 1;
+    return;
   }
-  if (m < a.M) store_chunk<KIND>(a, v, row_off + n, n, min(32, a.N - n), bias, scale);
+  if (m < a.M) store_chunk<KIND>(a, v, row_off + n, n, min(32, a.N - n), bias, scale, has_bias);
 }
 
-template <int KIND>
-__device__ __forceinline__ void epilogue_role(const TcArgs& a, const CUtensorMap* tmC, uint32_t tmem_base,
+template <int KIND, bool TMA>
+__device__ __forceinline__ void epilogue_role_t(const TcArgs& a, const CUtensorMap* tmC, uint32_t tmem_base,
                                               uint32_t accf0, uint32_t acce0, int warp, int lane,
-                                              const int32_t* bias, const float* scale, uint8_t* sbufs) {
+                                              const int32_t* bias, const float* scale, bool has_bias,
+                                              uint8_t* sbufs) {
   int sb = 0;
   const int q = warp & 3;
   const int half = (warp - 2) >> 2;
@@ -224,11 +266,11 @@ __device__ __forceinline__ void epilogue_role(const TcArgs& a, const CUtensorMap
       const int ca = half + 2 * i, cb = ca + 2;
       if (i + 1 < nmine) tmem_ld_32x32b_x32(tbase + cb * 32, vb);
       const int mrow0 = mt * kTcBM + q * 32;
-      emit_chunk<KIND>(a, tmC, va, b, m, mrow0, row_off, n0 + ca * 32, lane, sbufs, sb, bias, scale);
+      emit_chunk<KIND, TMA>(a, tmC, va, b, m, mrow0, row_off, n0 + ca * 32, lane, sbufs, sb, bias, scale, has_bias);
       tmem_ld_wait();
       if (i + 1 < nmine) {
         if (i + 2 < nmine) tmem_ld_32x32b_x32(tbase + (cb + 2) * 32, va);
-        emit_chunk<KIND>(a, tmC, vb, b, m, mrow0, row_off, n0 + cb * 32, lane, sbufs, sb, bias, scale);
+        emit_chunk<KIND, TMA>(a, tmC, vb, b, m, mrow0, row_off, n0 + cb * 32, lane, sbufs, sb, bias, scale, has_bias);
         tmem_ld_wait();
       }
     }
@@ -240,14 +282,27 @@ __device__ __forceinline__ void epilogue_role(const TcArgs& a, const CUtensorMap
       acc_ph ^= 1u;
     }
   }
-  if (KIND != kOutS8 && a.tma_store && lane == 0) bulk_wait_group_all();
+  if (TMA && lane == 0) bulk_wait_group_all();
+}
+
+template <int KIND>
+__device__ __forceinline__ void epilogue_role(const TcArgs& a, const CUtensorMap* tmC, uint32_t tmem_base,
+                                              uint32_t accf0, uint32_t acce0, int warp, int lane,
+                                              const int32_t* bias, const float* scale, bool has_bias,
+                                              uint8_t* sbufs) {
+  if (a.tma_store)
+    epilogue_role_t<KIND, true>(a, tmC, tmem_base, accf0, acce0, warp, lane, bias, scale, has_bias, sbufs);
+  else
+    epilogue_role_t<KIND, false>(a, tmC, tmem_base, accf0, acce0, warp, lane, bias, scale, has_bias, sbufs);
 }
 
 __global__ void __launch_bounds__(kTcThreads, 1)
     tc_gemm_s8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                       const __grid_constant__ CUtensorMap tmC, const TcArgs a) {
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // 1024-byte alignment by pointer arithmetic on the shared window (an integer round trip would
+  // turn every later access through these pointers into a generic load / store).
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   const uint32_t stage_a = kTcBM * a.BK;
   const uint32_t stage_b = a.BN * a.BK;
   uint8_t* sA = smem;
@@ -264,8 +319,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   int32_t* s_bias = reinterpret_cast<int32_t*>(bars + 2 * a.stages + 6);
   float* s_scale = reinterpret_cast<float*>(s_bias + a.stage_cols);
   // TMA-store staging: 2 x 4 KiB per epilogue warp, 1024-byte aligned, after the bias / scale copy
-  uint8_t* s_out = reinterpret_cast<uint8_t*>(
-      (reinterpret_cast<uintptr_t>(s_scale + a.stage_cols) + 1023) & ~uintptr_t(1023));
+  uint8_t* s_out = reinterpret_cast<uint8_t*>(s_scale + a.stage_cols);
+  s_out += (1024u - (smem_u32(s_out) & 1023u)) & 1023u;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -429,25 +484,34 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
   } else {
     // ------------------------------------------------------------- epilogue
-    const int32_t* bias = a.epi.bias;
-    const float* scale = a.epi.scale;
+    const bool has_bias = a.epi.bias != nullptr;
+    uint8_t* sbufs = s_out + (warp - 2) * 2 * (a.epi.out_kind == kOutS8 ? kEpiStageBytesS8 : kEpiStageBytes);
     if (a.stage_cols > 0) {
       // Copy the per-column bias / scale into shared memory once per CTA (epilogue warps only).
       for (int i = threadIdx.x - 64; i < a.stage_cols; i += kTcEpiWarps * 32) {
-        s_bias[i] = (a.epi.bias && i < a.N) ? __ldg(a.epi.bias + i) : 0;
+        s_bias[i] = (has_bias && i < a.N) ? __ldg(a.epi.bias + i) : 0;
         s_scale[i] = (a.epi.scale && i < a.N) ? __ldg(a.epi.scale + i) : 0.0f;
       }
       asm volatile("bar.sync 1, %0;" ::"n"(kTcEpiWarps * 32) : "memory");
-      bias = a.epi.bias ? s_bias : nullptr;
-      scale = s_scale;
+      // s_bias / s_scale derive from the shared-memory window here, so the per-chunk reads
+      // compile to shared-memory loads rather than generic ones.
+      if (a.epi.out_kind == kOutS8)
+        epilogue_role<kOutS8>(a, &tmC, tmem_base, accf0, acce0, warp, lane, s_bias, s_scale, has_bias, sbufs);
+      else if (a.epi.out_kind == kOutS32)
+        epilogue_role<kOutS32>(a, &tmC, tmem_base, accf0, acce0, warp, lane, s_bias, s_scale, has_bias, sbufs);
+      else
+        epilogue_role<kOutF32>(a, &tmC, tmem_base, accf0, acce0, warp, lane, s_bias, s_scale, has_bias, sbufs);
+    } else {
+      if (a.epi.out_kind == kOutS8)
+        epilogue_role<kOutS8>(a, &tmC, tmem_base, accf0, acce0, warp, lane, a.epi.bias, a.epi.scale, has_bias,
+                              sbufs);
+      else if (a.epi.out_kind == kOutS32)
+        epilogue_role<kOutS32>(a, &tmC, tmem_base, accf0, acce0, warp, lane, a.epi.bias, a.epi.scale, has_bias,
+                               sbufs);
+      else
+        epilogue_role<kOutF32>(a, &tmC, tmem_base, accf0, acce0, warp, lane, a.epi.bias, a.epi.scale, has_bias,
+                               sbufs);
     }
-    uint8_t* sbufs = s_out + (warp - 2) * 2 * kEpiStageBytes;
-    if (a.epi.out_kind == kOutS8)
-      epilogue_role<kOutS8>(a, &tmC, tmem_base, accf0, acce0, warp, lane, bias, scale, sbufs);
-    else if (a.epi.out_kind == kOutS32)
-      epilogue_role<kOutS32>(a, &tmC, tmem_base, accf0, acce0, warp, lane, bias, scale, sbufs);
-    else
-      epilogue_role<kOutF32>(a, &tmC, tmem_base, accf0, acce0, warp, lane, bias, scale, sbufs);
   }
 
   tc_fence_before();
