@@ -215,7 +215,7 @@ int encode_im2col(CUtensorMap* map, const int8_t* x, const ConvGeom& g, int bk) 
 
 // ------------------------------------------------------------- tcgen05 launch
 constexpr int kSmemLimit = 227 * 1024;
-constexpr int kSmemReserve = 1024 + 256;  // alignment slack + barriers / TMEM slot
+constexpr int kSmemReserve = 1024 + 512;  // alignment slack + barriers / TMEM slot
 
 int pick_bn(int n, int mn_major_b) {
   if (mn_major_b) return n <= 128 ? 128 : 256;
@@ -228,6 +228,12 @@ int pick_bn(int n, int mn_major_b) {
 const bool g_s8_tma_store = [] {
   const char* v = getenv("B200Q_S8_TMA_STORE");
   return !(v && v[0] == '0');
+}();
+
+const int g_nacc_max = [] {
+  const char* v = getenv("B200Q_NACC_MAX");
+  const int n = v ? atoi(v) : 8;
+  return n >= 8 ? 8 : n >= 4 ? 4 : 2;
 }();
 
 int launch_tc(const DeviceState& st, const CUtensorMap& ma, const CUtensorMap& mb, TcArgs a, cudaStream_t stream) {
@@ -267,7 +273,11 @@ int launch_tc(const DeviceState& st, const CUtensorMap& ma, const CUtensorMap& m
   const long long total = static_cast<long long>(a.batch) * a.m_tiles * a.n_tiles;
   if (total > 0x7FFFFFFFll) return fail(B200Q_ERR_UNSUPPORTED, "too many tiles");
   a.total_tiles = static_cast<int>(total);
-  a.tmem_cols = static_cast<uint32_t>(2 * a.BN);
+  // As many accumulator buffers as the 512 TMEM columns hold: short reductions finish a tile
+  // every few hundred cycles, and the MMA warp must not wait for the epilogue's turnaround.
+  a.nacc = g_nacc_max < 512 / a.BN ? g_nacc_max : 512 / a.BN;
+  if (a.nacc < 2) a.nacc = 2;
+  a.tmem_cols = static_cast<uint32_t>(a.nacc * a.BN);
   a.idesc = (2u << 4)                                   // D = s32
             | (1u << 7) | (1u << 10)                    // A, B signed int8
             | (static_cast<uint32_t>(a.a_major) << 15)  // A major
@@ -277,7 +287,10 @@ int launch_tc(const DeviceState& st, const CUtensorMap& ma, const CUtensorMap& m
   a.wait_limit = wait_limit();
   a.err = st.err;
   const int grid = a.total_tiles < st.sms ? a.total_tiles : st.sms;
-  const size_t smem = static_cast<size_t>(stages) * stage_bytes + kSmemReserve + epi_bytes;
+  size_t smem = static_cast<size_t>(stages) * stage_bytes + kSmemReserve + epi_bytes;
+  // One CTA per SM: the CTA allocates all 512 TMEM columns, so a second resident CTA of this
+  // grid would only wait for them.  Asking for more than half the shared memory rules it out.
+  if (smem < static_cast<size_t>(kSmemLimit / 2 + 1024)) smem = kSmemLimit / 2 + 1024;
   tc_gemm_s8_kernel<<<grid, kTcThreads, smem, stream>>>(ma, mb, mc, a);
   g_tc_launches.fetch_add(1, std::memory_order_relaxed);
   return check_launch("tc_gemm_s8_kernel launch");

@@ -44,6 +44,7 @@ struct TcArgs {
   int vec_ok;               // rows and bias/scale allow 16-byte vector stores
   uint32_t idesc;
   uint32_t tmem_cols;
+  int nacc;           // TMEM accumulator buffers (nacc x BN columns), 2..kTcMaxAcc
   long long wait_limit;
   int* err;
   int stage_cols;     // bias/scale columns copied to shared memory at start (0 = read from global)
@@ -51,6 +52,7 @@ struct TcArgs {
   int tma_store;      // outputs leave through shared memory + TMA tensor stores (map tmC)
 };
 
+constexpr int kTcMaxAcc = 8;
 constexpr int kEpiStageBytes = 32 * 128;   // one warp's 32 rows x 32 four-byte columns
 constexpr int kEpiStageBytesS8 = 32 * 32;  // one warp's 32 rows x 32 int8 columns
 
@@ -78,7 +80,7 @@ __device__ __forceinline__ uint32_t pack4_sat_s8(int a, int b, int c, int d) {
 // Fused epilogue for one row and 32 consecutive output columns [n, n + valid).
 // bias / scale point at shared memory (staged) or global memory; bias may be null.
 // All array indices are compile-time constants after unrolling: nothing spills to local memory.
-template <int KIND>
+template <int KIND, bool DCL>
 __device__ __forceinline__ void store_chunk(const TcArgs& a, const uint32_t (&v)[32], size_t off, int n, int valid,
                                             const int32_t* bias, const float* scale, bool has_bias) {
   const Epilogue& e = a.epi;
@@ -104,7 +106,7 @@ __device__ __forceinline__ void store_chunk(const TcArgs& a, const uint32_t (&v)
           reinterpret_cast<float4*>(static_cast<float*>(a.out) + off)[q] = make_float4(p0, p1, p2, p3);
         } else {
           int r0 = __float2int_rn(p0), r1 = __float2int_rn(p1), r2 = __float2int_rn(p2), r3 = __float2int_rn(p3);
-          if (!a.default_clamp) {
+          if constexpr (!DCL) {
             const int lo = e.lo - e.zp, hi = e.hi - e.zp;
             r0 = min(max(r0, lo), hi) + e.zp; r1 = min(max(r1, lo), hi) + e.zp;
             r2 = min(max(r2, lo), hi) + e.zp; r3 = min(max(r3, lo), hi) + e.zp;
@@ -173,6 +175,7 @@ __device__ __forceinline__ void stage_chunk_4b(const TcArgs& a, const uint32_t (
 // 32B-swizzled 1 KiB buffer (16-byte half h of row r at half h ^ ((r / 4) % 2), the layout of a
 // SWIZZLE_32B tensor map: conflict-free for one 16-byte store per lane) and leave with one TMA
 // store, which clips rows >= M and columns >= N.  The requantization is the one of store_chunk.
+template <bool DCL>
 __device__ __forceinline__ void stage_chunk_s8(const TcArgs& a, const uint32_t (&v)[32], int n, int lane,
                                                uint8_t* sbuf, const int32_t* bias, const float* scale,
                                                bool has_bias) {
@@ -193,7 +196,7 @@ __device__ __forceinline__ void stage_chunk_s8(const TcArgs& a, const uint32_t (
     int r1 = __float2int_rn(__fmul_rn(__int2float_rn(t1), s4.y));
     int r2 = __float2int_rn(__fmul_rn(__int2float_rn(t2), s4.z));
     int r3 = __float2int_rn(__fmul_rn(__int2float_rn(t3), s4.w));
-    if (!a.default_clamp) {
+    if constexpr (!DCL) {
       const int lo = e.lo - e.zp, hi = e.hi - e.zp;
       r0 = min(max(r0, lo), hi) + e.zp; r1 = min(max(r1, lo), hi) + e.zp;
       r2 = min(max(r2, lo), hi) + e.zp; r3 = min(max(r3, lo), hi) + e.zp;
@@ -209,7 +212,7 @@ __device__ __forceinline__ void stage_chunk_s8(const TcArgs& a, const uint32_t (
 // Epilogue role: 8 warps; warp w reads TMEM lanes 32*(w%4)..+31 (the hardware restricts a warp
 // to the lane quarter w%4) and the chunks of 32 columns with chunk % 2 == (w-2)/4.  The TMEM load
 // of the next chunk is issued before the current chunk is processed (two register buffers).
-template <int KIND, bool TMA>
+template <int KIND, bool TMA, bool DCL>
 __device__ __forceinline__ void emit_chunk(const TcArgs& a, const CUtensorMap* tmC, const uint32_t (&v)[32], int b,
                                            int m, int mrow0, size_t row_off, int n, int lane, uint8_t* sbufs,
                                            int& sb, const int32_t* bias, const float* scale,
@@ -220,7 +223,7 @@ __device__ __forceinline__ void emit_chunk(const TcArgs& a, const CUtensorMap* t
     if (lane == 0) bulk_wait_group_read<1>();  // the store that used this buffer has read it
     __syncwarp();
     if constexpr (KIND == kOutS8)
-      stage_chunk_s8(a, v, n, lane, buf, bias, scale, has_bias);
+      stage_chunk_s8<DCL>(a, v, n, lane, buf, bias, scale, has_bias);
     else
       stage_chunk_4b<KIND>(a, v, n, lane, buf, bias, scale, has_bias);
     fence_proxy_async_smem();
@@ -232,10 +235,10 @@ __device__ __forceinline__ void emit_chunk(const TcArgs& a, const CUtensorMap* t
     sb ^= 1;
     return;
   }
-  if (m < a.M) store_chunk<KIND>(a, v, row_off + n, n, min(32, a.N - n), bias, scale, has_bias);
+  if (m < a.M) store_chunk<KIND, DCL>(a, v, row_off + n, n, min(32, a.N - n), bias, scale, has_bias);
 }
 
-template <int KIND, bool TMA>
+template <int KIND, bool TMA, bool DCL>
 __device__ __forceinline__ void epilogue_role_t(const TcArgs& a, const CUtensorMap* tmC, uint32_t tmem_base,
                                               uint32_t accf0, uint32_t acce0, int warp, int lane,
                                               const int32_t* bias, const float* scale, bool has_bias,
@@ -266,18 +269,20 @@ __device__ __forceinline__ void epilogue_role_t(const TcArgs& a, const CUtensorM
       const int ca = half + 2 * i, cb = ca + 2;
       if (i + 1 < nmine) tmem_ld_32x32b_x32(tbase + cb * 32, vb);
       const int mrow0 = mt * kTcBM + q * 32;
-      emit_chunk<KIND, TMA>(a, tmC, va, b, m, mrow0, row_off, n0 + ca * 32, lane, sbufs, sb, bias, scale, has_bias);
+      emit_chunk<KIND, TMA, DCL>(a, tmC, va, b, m, mrow0, row_off, n0 + ca * 32, lane, sbufs, sb, bias, scale,
+                                 has_bias);
       tmem_ld_wait();
       if (i + 1 < nmine) {
         if (i + 2 < nmine) tmem_ld_32x32b_x32(tbase + (cb + 2) * 32, va);
-        emit_chunk<KIND, TMA>(a, tmC, vb, b, m, mrow0, row_off, n0 + cb * 32, lane, sbufs, sb, bias, scale, has_bias);
+        emit_chunk<KIND, TMA, DCL>(a, tmC, vb, b, m, mrow0, row_off, n0 + cb * 32, lane, sbufs, sb, bias, scale,
+                                   has_bias);
         tmem_ld_wait();
       }
     }
     tc_fence_before();
     __syncwarp();
     if (lane == 0) mbar_arrive(acce0 + 8 * buf);
-    if (++buf == 2) {
+    if (++buf == a.nacc) {
       buf = 0;
       acc_ph ^= 1u;
     }
@@ -290,10 +295,19 @@ __device__ __forceinline__ void epilogue_role(const TcArgs& a, const CUtensorMap
                                               uint32_t accf0, uint32_t acce0, int warp, int lane,
                                               const int32_t* bias, const float* scale, bool has_bias,
                                               uint8_t* sbufs) {
-  if (a.tma_store)
-    epilogue_role_t<KIND, true>(a, tmC, tmem_base, accf0, acce0, warp, lane, bias, scale, has_bias, sbufs);
-  else
-    epilogue_role_t<KIND, false>(a, tmC, tmem_base, accf0, acce0, warp, lane, bias, scale, has_bias, sbufs);
+  // The default int8 range [-128, 127] with zero point 0 is clamped by the saturating pack alone;
+  // compiling it as its own variant keeps the per-element branch out of the unrolled loop.
+  if (KIND == kOutS8 && a.default_clamp) {
+    if (a.tma_store)
+      epilogue_role_t<KIND, true, true>(a, tmC, tmem_base, accf0, acce0, warp, lane, bias, scale, has_bias, sbufs);
+    else
+      epilogue_role_t<KIND, false, true>(a, tmC, tmem_base, accf0, acce0, warp, lane, bias, scale, has_bias, sbufs);
+  } else {
+    if (a.tma_store)
+      epilogue_role_t<KIND, true, false>(a, tmC, tmem_base, accf0, acce0, warp, lane, bias, scale, has_bias, sbufs);
+    else
+      epilogue_role_t<KIND, false, false>(a, tmC, tmem_base, accf0, acce0, warp, lane, bias, scale, has_bias, sbufs);
+  }
 }
 
 __global__ void __launch_bounds__(kTcThreads, 1)
@@ -312,11 +326,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const uint32_t full0 = smem_u32(bars);
   const uint32_t empty0 = smem_u32(bars + a.stages);
   const uint32_t accf0 = smem_u32(bars + 2 * a.stages);
-  const uint32_t acce0 = smem_u32(bars + 2 * a.stages + 2);
-  const uint32_t drain = smem_u32(bars + 2 * a.stages + 4);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * a.stages + 5);
+  const uint32_t acce0 = smem_u32(bars + 2 * a.stages + kTcMaxAcc);
+  const uint32_t drain = smem_u32(bars + 2 * a.stages + 2 * kTcMaxAcc);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * a.stages + 2 * kTcMaxAcc + 1);
   // bias[stage_cols] then scale[stage_cols], 16-byte aligned, after the barriers
-  int32_t* s_bias = reinterpret_cast<int32_t*>(bars + 2 * a.stages + 6);
+  int32_t* s_bias = reinterpret_cast<int32_t*>(bars + 2 * a.stages + 2 * kTcMaxAcc + 2);
   float* s_scale = reinterpret_cast<float*>(s_bias + a.stage_cols);
   // TMA-store staging: 2 x 4 KiB per epilogue warp, 1024-byte aligned, after the bias / scale copy
   uint8_t* s_out = reinterpret_cast<uint8_t*>(s_scale + a.stage_cols);
@@ -330,7 +344,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       mbar_init(full0 + 8 * i, 1);
       mbar_init(empty0 + 8 * i, 1);
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < a.nacc; ++i) {
       mbar_init(accf0 + 8 * i, 1);
       mbar_init(acce0 + 8 * i, kTcEpiWarps);
     }
@@ -473,7 +487,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
         if (!ok) break;
         tc_commit_elect(accf0 + 8 * buf);
-        if (++buf == 2) {
+        if (++buf == a.nacc) {
           buf = 0;
           acc_ph ^= 1u;
         }
