@@ -230,6 +230,12 @@ const bool g_s8_tma_store = [] {
   return !(v && v[0] == '0');
 }();
 
+// Resident-B switch (env B200Q_B_RESIDENT=0 turns it off, for A/B timing).
+const bool g_b_resident = [] {
+  const char* v = getenv("B200Q_B_RESIDENT");
+  return !(v && v[0] == '0');
+}();
+
 const int g_nacc_max = [] {
   const char* v = getenv("B200Q_NACC_MAX");
   const int n = v ? atoi(v) : 8;
@@ -246,7 +252,12 @@ int launch_tc(const DeviceState& st, const CUtensorMap& ma, const CUtensorMap& m
     if (rc) return rc;
     a.tma_store = 1;
   }
-  const int stage_bytes = kTcBM * a.BK + a.BN * a.BK;
+  a.n_tiles = (a.N + a.BN - 1) / a.BN;
+  // Resident B for a single N tile whose K blocks fit in 64 KiB (narrow layers, 3x3 convs with
+  // few output channels): the weights are loaded once per CTA instead of once per 128-row tile.
+  const long long b_all = static_cast<long long>(a.num_kb) * a.BN * a.BK;
+  a.b_res = g_b_resident && a.n_tiles == 1 && !a.b_batched && a.b_major == 0 && b_all <= 64 * 1024;
+  const int stage_bytes = kTcBM * a.BK + (a.b_res ? 0 : a.BN * a.BK);
   // Stage per-column bias / scale in shared memory when they fit (4096 columns = 32 KiB).
   a.stage_cols = (a.epi.out_kind != kOutS32 || a.epi.bias) && a.N <= 4096 ? (a.N + 31) / 32 * 32 : 0;
   a.default_clamp = a.epi.out_kind == kOutS8 && a.epi.zp == 0 && a.epi.lo == -128 && a.epi.hi == 127;
@@ -264,12 +275,12 @@ int launch_tc(const DeviceState& st, const CUtensorMap& ma, const CUtensorMap& m
   }
   const int stage_out = a.epi.out_kind == kOutS8 ? kEpiStageBytesS8 : kEpiStageBytes;
   const int epi_bytes = a.stage_cols * 8 + (a.tma_store ? 1024 + kTcEpiWarps * 2 * stage_out : 0);
-  int stages = (kSmemLimit - kSmemReserve - epi_bytes) / stage_bytes;
+  const int b_res_bytes = a.b_res ? static_cast<int>(b_all) : 0;
+  int stages = (kSmemLimit - kSmemReserve - epi_bytes - b_res_bytes) / stage_bytes;
   if (stages > 8) stages = 8;
   if (stages < 2) return fail(B200Q_ERR_UNSUPPORTED, "tile does not fit shared memory");
   a.stages = stages;
   a.m_tiles = (a.M + kTcBM - 1) / kTcBM;
-  a.n_tiles = (a.N + a.BN - 1) / a.BN;
   const long long total = static_cast<long long>(a.batch) * a.m_tiles * a.n_tiles;
   if (total > 0x7FFFFFFFll) return fail(B200Q_ERR_UNSUPPORTED, "too many tiles");
   a.total_tiles = static_cast<int>(total);
@@ -287,7 +298,7 @@ int launch_tc(const DeviceState& st, const CUtensorMap& ma, const CUtensorMap& m
   a.wait_limit = wait_limit();
   a.err = st.err;
   const int grid = a.total_tiles < st.sms ? a.total_tiles : st.sms;
-  size_t smem = static_cast<size_t>(stages) * stage_bytes + kSmemReserve + epi_bytes;
+  size_t smem = static_cast<size_t>(stages) * stage_bytes + b_res_bytes + kSmemReserve + epi_bytes;
   // One CTA per SM: the CTA allocates all 512 TMEM columns, so a second resident CTA of this
   // grid would only wait for them.  Asking for more than half the shared memory rules it out.
   if (smem < static_cast<size_t>(kSmemLimit / 2 + 1024)) smem = kSmemLimit / 2 + 1024;

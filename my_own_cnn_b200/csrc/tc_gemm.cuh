@@ -50,6 +50,7 @@ struct TcArgs {
   int stage_cols;     // bias/scale columns copied to shared memory at start (0 = read from global)
   int default_clamp;  // int8 output with zp 0 and bounds [-128, 127]: saturating pack does the clamp
   int tma_store;      // outputs leave through shared memory + TMA tensor stores (map tmC)
+  int b_res;          // B resident: all num_kb K blocks of the single N tile loaded once per CTA
 };
 
 constexpr int kTcMaxAcc = 8;
@@ -319,18 +320,21 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   const uint32_t stage_a = kTcBM * a.BK;
   const uint32_t stage_b = a.BN * a.BK;
+  // Ring of stages: A (+ B unless B is resident).  A resident B holds num_kb blocks after the ring.
   uint8_t* sA = smem;
   uint8_t* sB = smem + a.stages * stage_a;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + a.stages * stage_b);
-  // bars: full[stages], empty[stages], acc_full[2], acc_empty[2], drain[1]
+  const uint32_t b_bytes = a.b_res ? a.num_kb * stage_b : a.stages * stage_b;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + b_bytes);
+  // bars: full[stages], empty[stages], acc_full[8], acc_empty[8], drain, b_full, TMEM slot
   const uint32_t full0 = smem_u32(bars);
   const uint32_t empty0 = smem_u32(bars + a.stages);
   const uint32_t accf0 = smem_u32(bars + 2 * a.stages);
   const uint32_t acce0 = smem_u32(bars + 2 * a.stages + kTcMaxAcc);
   const uint32_t drain = smem_u32(bars + 2 * a.stages + 2 * kTcMaxAcc);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * a.stages + 2 * kTcMaxAcc + 1);
+  const uint32_t b_full = smem_u32(bars + 2 * a.stages + 2 * kTcMaxAcc + 1);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * a.stages + 2 * kTcMaxAcc + 2);
   // bias[stage_cols] then scale[stage_cols], 16-byte aligned, after the barriers
-  int32_t* s_bias = reinterpret_cast<int32_t*>(bars + 2 * a.stages + 2 * kTcMaxAcc + 2);
+  int32_t* s_bias = reinterpret_cast<int32_t*>(bars + 2 * a.stages + 2 * kTcMaxAcc + 4);
   float* s_scale = reinterpret_cast<float*>(s_bias + a.stage_cols);
   // TMA-store staging: 2 x 4 KiB per epilogue warp, 1024-byte aligned, after the bias / scale copy
   uint8_t* s_out = reinterpret_cast<uint8_t*>(s_scale + a.stage_cols);
@@ -349,6 +353,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       mbar_init(acce0 + 8 * i, kTcEpiWarps);
     }
     mbar_init(drain, 1);
+    mbar_init(b_full, 1);
     fence_mbar_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
@@ -372,7 +377,25 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       uint32_t issued_mask = 0;  // stages that received a load
       uint32_t last_ph = 0;      // parity of the last load into each stage (bit per stage)
       bool ok = true;
-      const uint32_t tx = stage_a + stage_b;
+      const uint32_t tx = a.b_res ? stage_a : stage_a + stage_b;
+      // One B block (K block kb of N tile n0, batch bb) into shared memory at dB.
+      auto load_b = [&](uint32_t dB, uint32_t bar, int kb, int n0, int bb) {
+        if (a.conv_b) {
+          const int tap = a.mode == 1 ? kb / a.cchunks : 0;
+          const int cc = kb - tap * a.cchunks;
+          tma_load_3d(dB, &tmB, bar, cc * a.BK, tap, n0);
+        } else if (a.b_major == 0) {
+          tma_load_3d(dB, &tmB, bar, kb * a.BK, n0, bb);
+        } else {
+          for (int i = 0; i < a.BN / 128; ++i) tma_load_3d(dB + i * a.BK * 128, &tmB, bar, n0 + 128 * i, kb * a.BK, bb);
+        }
+      };
+      if (a.b_res && blockIdx.x < a.total_tiles) {
+        // The whole B of the single N tile, once: the weights of a narrow layer are re-read for
+        // every 128-row tile otherwise, and boxes that reach past N or C are slow to fill.
+        mbar_arrive_expect_tx(b_full, a.num_kb * stage_b);
+        for (int kb = 0; kb < a.num_kb; ++kb) load_b(smem_u32(sB + kb * stage_b), b_full, kb, 0, 0);
+      }
       for (int tile = blockIdx.x; tile < a.total_tiles && ok; tile += gridDim.x) {
         const int b = tile / tiles_per_batch;
         const int rem = tile - b * tiles_per_batch;
@@ -410,17 +433,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           } else {
             tma_load_3d(dA, &tmA, fb, m0, kb * a.BK, b);
           }
-          const int bb = a.b_batched ? b : 0;
-          if (a.conv_b) {
-            const int tap = a.mode == 1 ? kb / a.cchunks : 0;
-            const int cc = kb - tap * a.cchunks;
-            tma_load_3d(dB, &tmB, fb, cc * a.BK, tap, n0);
-          } else if (a.b_major == 0) {
-            tma_load_3d(dB, &tmB, fb, kb * a.BK, n0, bb);
-          } else {
-            for (int i = 0; i < a.BN / 128; ++i)
-              tma_load_3d(dB + i * a.BK * 128, &tmB, fb, n0 + 128 * i, kb * a.BK, bb);
-          }
+          if (!a.b_res) load_b(dB, fb, kb, n0, a.b_batched ? b : 0);
           issued_mask |= 1u << stage;
           last_ph = (last_ph & ~(1u << stage)) | (ph << stage);
           if (++stage == a.stages) {
@@ -434,6 +447,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         for (int i = 0; i < a.stages; ++i)
           if (issued_mask & (1u << i))
             mbar_wait_bounded(full0 + 8 * i, (last_ph >> i) & 1u, a.wait_limit, a.err, kDevErrTimeoutProducer);
+        if (a.b_res) mbar_wait_bounded(b_full, 0, a.wait_limit, a.err, kDevErrTimeoutProducer);
       }
     }
   } else if (warp == 1) {
@@ -458,6 +472,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       // (shared addresses stay below 256 KiB, so the add never carries out of the field).
       const uint64_t a_desc0 = make_smem_desc(smem_u32(sA), a_lbo, a_sbo, a_layout);
       const uint64_t b_desc0 = make_smem_desc(smem_u32(sB), b_lbo, b_sbo, b_layout);
+      if (a.b_res && blockIdx.x < a.total_tiles)
+        ok = __all_sync(0xFFFFFFFFu, mbar_wait_bounded(b_full, 0, a.wait_limit, a.err, kDevErrTimeoutMma));
       for (int tile = blockIdx.x; tile < a.total_tiles && ok; tile += gridDim.x) {
         if (!__all_sync(0xFFFFFFFFu,
                         mbar_wait_bounded(acce0 + 8 * buf, acc_ph ^ 1u, a.wait_limit, a.err, kDevErrTimeoutMma))) {
@@ -475,7 +491,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             break;
           }
           const uint64_t ad_s = a_desc0 + ((stage * stage_a) >> 4);
-          const uint64_t bd_s = b_desc0 + ((stage * stage_b) >> 4);
+          const uint64_t bd_s = b_desc0 + (((a.b_res ? kb : stage) * stage_b) >> 4);
           for (int j = 0; j < ksteps; ++j)
             tc_mma_i8_elect(d_tmem, ad_s + ((j * a_step) >> 4), bd_s + ((j * b_step) >> 4), a.idesc,
                             (kb | j) != 0 ? 1u : 0u);
