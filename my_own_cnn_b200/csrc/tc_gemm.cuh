@@ -78,6 +78,49 @@ __device__ __forceinline__ uint32_t pack4_sat_s8(int a, int b, int c, int d) {
   return out;
 }
 
+// Vector form of the fused epilogue: the first 4 * NQ columns of the chunk (NQ = 8: all 32,
+// NQ = 4: the first 16), 16-byte bias / scale reads and 16-byte stores.
+template <int KIND, bool DCL, int NQ>
+__device__ __forceinline__ void store_vec(const TcArgs& a, const uint32_t (&v)[32], size_t off, int n,
+                                          const int32_t* bias, const float* scale, bool has_bias) {
+  const Epilogue& e = a.epi;
+  const int4* bp = reinterpret_cast<const int4*>(bias + n);
+  const float4* sp = reinterpret_cast<const float4*>(scale + n);
+  uint32_t packed[8];
+#pragma unroll
+  for (int q = 0; q < NQ; ++q) {
+    int t0 = static_cast<int>(v[4 * q + 0]), t1 = static_cast<int>(v[4 * q + 1]);
+    int t2 = static_cast<int>(v[4 * q + 2]), t3 = static_cast<int>(v[4 * q + 3]);
+    if (has_bias) {
+      const int4 bb = bp[q];
+      t0 = wrap_add(t0, bb.x); t1 = wrap_add(t1, bb.y); t2 = wrap_add(t2, bb.z); t3 = wrap_add(t3, bb.w);
+    }
+    if constexpr (KIND == kOutS32) {
+      reinterpret_cast<int4*>(static_cast<int32_t*>(a.out) + off)[q] = make_int4(t0, t1, t2, t3);
+    } else {
+      const float4 s4 = sp[q];
+      const float p0 = __fmul_rn(__int2float_rn(t0), s4.x), p1 = __fmul_rn(__int2float_rn(t1), s4.y);
+      const float p2 = __fmul_rn(__int2float_rn(t2), s4.z), p3 = __fmul_rn(__int2float_rn(t3), s4.w);
+      if constexpr (KIND == kOutF32) {
+        reinterpret_cast<float4*>(static_cast<float*>(a.out) + off)[q] = make_float4(p0, p1, p2, p3);
+      } else {
+        int r0 = __float2int_rn(p0), r1 = __float2int_rn(p1), r2 = __float2int_rn(p2), r3 = __float2int_rn(p3);
+        if constexpr (!DCL) {
+          const int lo = e.lo - e.zp, hi = e.hi - e.zp;
+          r0 = min(max(r0, lo), hi) + e.zp; r1 = min(max(r1, lo), hi) + e.zp;
+          r2 = min(max(r2, lo), hi) + e.zp; r3 = min(max(r3, lo), hi) + e.zp;
+        }
+        packed[q] = pack4_sat_s8(r0, r1, r2, r3);
+      }
+    }
+  }
+  if constexpr (KIND == kOutS8) {
+    int4* o = reinterpret_cast<int4*>(static_cast<int8_t*>(a.out) + off);
+    o[0] = make_int4(packed[0], packed[1], packed[2], packed[3]);
+    if constexpr (NQ == 8) o[1] = make_int4(packed[4], packed[5], packed[6], packed[7]);
+  }
+}
+
 // Fused epilogue for one row and 32 consecutive output columns [n, n + valid).
 // bias / scale point at shared memory (staged) or global memory; bias may be null.
 // All array indices are compile-time constants after unrolling: nothing spills to local memory.
@@ -85,43 +128,15 @@ template <int KIND, bool DCL>
 __device__ __forceinline__ void store_chunk(const TcArgs& a, const uint32_t (&v)[32], size_t off, int n, int valid,
                                             const int32_t* bias, const float* scale, bool has_bias) {
   const Epilogue& e = a.epi;
-  if (valid == 32 && a.vec_ok) {
-    const int4* bp = reinterpret_cast<const int4*>(bias + n);
-    const float4* sp = reinterpret_cast<const float4*>(scale + n);
-    uint32_t packed[8];
-#pragma unroll
-    for (int q = 0; q < 8; ++q) {
-      int t0 = static_cast<int>(v[4 * q + 0]), t1 = static_cast<int>(v[4 * q + 1]);
-      int t2 = static_cast<int>(v[4 * q + 2]), t3 = static_cast<int>(v[4 * q + 3]);
-      if (has_bias) {
-        const int4 bb = bp[q];
-        t0 = wrap_add(t0, bb.x); t1 = wrap_add(t1, bb.y); t2 = wrap_add(t2, bb.z); t3 = wrap_add(t3, bb.w);
-      }
-      if constexpr (KIND == kOutS32) {
-        reinterpret_cast<int4*>(static_cast<int32_t*>(a.out) + off)[q] = make_int4(t0, t1, t2, t3);
-      } else {
-        const float4 s4 = sp[q];
-        const float p0 = __fmul_rn(__int2float_rn(t0), s4.x), p1 = __fmul_rn(__int2float_rn(t1), s4.y);
-        const float p2 = __fmul_rn(__int2float_rn(t2), s4.z), p3 = __fmul_rn(__int2float_rn(t3), s4.w);
-        if constexpr (KIND == kOutF32) {
-          reinterpret_cast<float4*>(static_cast<float*>(a.out) + off)[q] = make_float4(p0, p1, p2, p3);
-        } else {
-          int r0 = __float2int_rn(p0), r1 = __float2int_rn(p1), r2 = __float2int_rn(p2), r3 = __float2int_rn(p3);
-          if constexpr (!DCL) {
-            const int lo = e.lo - e.zp, hi = e.hi - e.zp;
-            r0 = min(max(r0, lo), hi) + e.zp; r1 = min(max(r1, lo), hi) + e.zp;
-            r2 = min(max(r2, lo), hi) + e.zp; r3 = min(max(r3, lo), hi) + e.zp;
-          }
-          packed[q] = pack4_sat_s8(r0, r1, r2, r3);
-        }
-      }
+  if (a.vec_ok) {
+    if (valid == 32) {
+      store_vec<KIND, DCL, 8>(a, v, off, n, bias, scale, has_bias);
+      return;
     }
-    if constexpr (KIND == kOutS8) {
-      int4* o = reinterpret_cast<int4*>(static_cast<int8_t*>(a.out) + off);
-      o[0] = make_int4(packed[0], packed[1], packed[2], packed[3]);
-      o[1] = make_int4(packed[4], packed[5], packed[6], packed[7]);
+    if (valid == 16) {  // the 16-column tail of N = 16, 48, 80, ...
+      store_vec<KIND, DCL, 4>(a, v, off, n, bias, scale, has_bias);
+      return;
     }
-    return;
   }
 #pragma unroll
   for (int j = 0; j < 32; ++j) {
@@ -211,8 +226,9 @@ __device__ __forceinline__ void stage_chunk_s8(const TcArgs& a, const uint32_t (
 }
 
 // Epilogue role: 8 warps; warp w reads TMEM lanes 32*(w%4)..+31 (the hardware restricts a warp
-// to the lane quarter w%4) and the chunks of 32 columns with chunk % 2 == (w-2)/4.  The TMEM load
-// of the next chunk is issued before the current chunk is processed (two register buffers).
+// to the lane quarter w%4) and, in the j-th tile of its CTA, the chunks of 32 columns with
+// chunk % 2 == ((w-2)/4 + j) % 2.  The TMEM load of the next chunk is issued before the current
+// chunk is processed (two register buffers).
 template <int KIND, bool TMA, bool DCL>
 __device__ __forceinline__ void emit_chunk(const TcArgs& a, const CUtensorMap* tmC, const uint32_t (&v)[32], int b,
                                            int m, int mrow0, size_t row_off, int n, int lane, uint8_t* sbufs,
@@ -249,25 +265,29 @@ __device__ __forceinline__ void epilogue_role_t(const TcArgs& a, const CUtensorM
   const int half = (warp - 2) >> 2;
   const int row = q * 32 + lane;
   const int tiles_per_batch = a.m_tiles * a.n_tiles;
-  const int nmine = (a.BN / 32 - half + 1) / 2;  // chunks half, half+2, ...
   int buf = 0;
   uint32_t acc_ph = 0;
-  for (int tile = blockIdx.x; tile < a.total_tiles; tile += gridDim.x) {
+  int sel = half;  // this warp's chunks in the current tile: sel, sel + 2, ...
+  for (int tile = blockIdx.x; tile < a.total_tiles; tile += gridDim.x, sel ^= 1) {
     const int b = tile / tiles_per_batch;
     const int rem = tile - b * tiles_per_batch;
     const int mt = rem / a.n_tiles;
     const int nt = rem - mt * a.n_tiles;
     const int m = mt * kTcBM + row;
     const int n0 = nt * a.BN;
+    // Chunks holding columns < N; the two warps of a lane quarter swap parities every tile, so an
+    // odd chunk count (N <= 32, N = 96, ...) is shared evenly over two tiles.
+    const int nvalid = (min(a.BN, a.N - n0) + 31) >> 5;
+    const int nmine = (nvalid - sel + 1) >> 1;
     if (!mbar_wait_bounded(accf0 + 8 * buf, acc_ph, a.wait_limit, a.err, kDevErrTimeoutEpilogue)) break;
     tc_fence_after();
     const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(buf * a.BN);
     const size_t row_off = static_cast<size_t>(b) * a.batch_stride + static_cast<size_t>(m) * a.ldc;
     uint32_t va[32], vb[32];
-    tmem_ld_32x32b_x32(tbase + half * 32, va);
+    if (nmine > 0) tmem_ld_32x32b_x32(tbase + sel * 32, va);
     tmem_ld_wait();
     for (int i = 0; i < nmine; i += 2) {
-      const int ca = half + 2 * i, cb = ca + 2;
+      const int ca = sel + 2 * i, cb = ca + 2;
       if (i + 1 < nmine) tmem_ld_32x32b_x32(tbase + cb * 32, vb);
       const int mrow0 = mt * kTcBM + q * 32;
       emit_chunk<KIND, TMA, DCL>(a, tmC, va, b, m, mrow0, row_off, n0 + ca * 32, lane, sbufs, sb, bias, scale,
