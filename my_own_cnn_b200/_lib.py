@@ -30,6 +30,7 @@ PATH_NAMES = {
     5: "cuda-core-qi32",
     6: "cuda-core-bmm-i32",
     7: "tcgen05-packed",
+    8: "tcgen05-tiled-2sm",
 }
 
 

@@ -94,6 +94,8 @@ int device_state(DeviceState** out) {
     if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(g_dev_err)");
     e = cudaFuncSetAttribute(tc_gemm_s8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(tc_gemm_s8_kernel)");
+    e = cudaFuncSetAttribute(tc_gemm_s8_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(tc_gemm_s8_pair_kernel)");
     if (!g_encode_tiled) {
       cudaDriverEntryPointQueryResult q;
       void* fn = nullptr;
@@ -236,11 +238,30 @@ const bool g_b_resident = [] {
   return !(v && v[0] == '0');
 }();
 
+// 2-SM tiles switch (env B200Q_PAIR=0 turns them off, for A/B timing).
+const bool g_pair = [] {
+  const char* v = getenv("B200Q_PAIR");
+  return !(v && v[0] == '0');
+}();
+
 const int g_nacc_max = [] {
   const char* v = getenv("B200Q_NACC_MAX");
   const int n = v ? atoi(v) : 8;
   return n >= 8 ? 8 : n >= 4 ? 4 : 2;
 }();
+
+// 2-SM tiles for large tiled GEMMs with more than one 256-column N tile: K-major operands, no
+// channel-padding weight map, enough 256-row tiles to give every SM pair work.  Measured faster
+// for reductions of 2048 and more or 4-byte outputs (config 4b +16 %); equal or slower for int8
+// outputs of shorter reductions, where both CTAs' epilogues gate every accumulator buffer.  The
+// caller encodes the B map with BN / 2 rows per box when this holds.
+bool want_pair(const DeviceState& st, const TcArgs& a) {
+  if (!g_pair || a.mode != 0 || a.a_major != 0 || a.b_major != 0 || a.conv_b || a.BN != 256) return false;
+  if (a.num_kb * a.BK < 2048 && a.epi.out_kind == kOutS8) return false;
+  const long long n_tiles = (a.N + a.BN - 1) / a.BN;
+  const long long pair_tiles = static_cast<long long>(a.batch) * ((a.M + 2 * kTcBM - 1) / (2 * kTcBM)) * n_tiles;
+  return n_tiles >= 2 && pair_tiles >= st.sms;
+}
 
 int launch_tc(const DeviceState& st, const CUtensorMap& ma, const CUtensorMap& mb, TcArgs a, cudaStream_t stream) {
   // 4-byte outputs go through shared memory and TMA stores when the row pitch allows a tensor map.
@@ -256,8 +277,9 @@ int launch_tc(const DeviceState& st, const CUtensorMap& ma, const CUtensorMap& m
   // Resident B for a single N tile whose K blocks fit in 64 KiB (narrow layers, 3x3 convs with
   // few output channels): the weights are loaded once per CTA instead of once per 128-row tile.
   const long long b_all = static_cast<long long>(a.num_kb) * a.BN * a.BK;
-  a.b_res = g_b_resident && a.n_tiles == 1 && !a.b_batched && a.b_major == 0 && b_all <= 64 * 1024;
-  const int stage_bytes = kTcBM * a.BK + (a.b_res ? 0 : a.BN * a.BK);
+  a.b_res = !a.pair && g_b_resident && a.n_tiles == 1 && !a.b_batched && a.b_major == 0 && b_all <= 64 * 1024;
+  const int b_rows = a.pair ? a.BN / 2 : a.BN;  // B rows per stage held by this CTA
+  const int stage_bytes = kTcBM * a.BK + (a.b_res ? 0 : b_rows * a.BK);
   // Stage per-column bias / scale in shared memory when they fit (4096 columns = 32 KiB).
   a.stage_cols = (a.epi.out_kind != kOutS32 || a.epi.bias) && a.N <= 4096 ? (a.N + 31) / 32 * 32 : 0;
   a.default_clamp = a.epi.out_kind == kOutS8 && a.epi.zp == 0 && a.epi.lo == -128 && a.epi.hi == 127;
@@ -280,7 +302,8 @@ int launch_tc(const DeviceState& st, const CUtensorMap& ma, const CUtensorMap& m
   if (stages > 8) stages = 8;
   if (stages < 2) return fail(B200Q_ERR_UNSUPPORTED, "tile does not fit shared memory");
   a.stages = stages;
-  a.m_tiles = (a.M + kTcBM - 1) / kTcBM;
+  const int tile_m = a.pair ? 2 * kTcBM : kTcBM;
+  a.m_tiles = (a.M + tile_m - 1) / tile_m;
   const long long total = static_cast<long long>(a.batch) * a.m_tiles * a.n_tiles;
   if (total > 0x7FFFFFFFll) return fail(B200Q_ERR_UNSUPPORTED, "too many tiles");
   a.total_tiles = static_cast<int>(total);
@@ -294,14 +317,20 @@ int launch_tc(const DeviceState& st, const CUtensorMap& ma, const CUtensorMap& m
             | (static_cast<uint32_t>(a.a_major) << 15)  // A major
             | (static_cast<uint32_t>(a.b_major) << 16)  // B major
             | (static_cast<uint32_t>(a.BN >> 3) << 17)  // N
-            | (static_cast<uint32_t>(kTcBM >> 4) << 24);  // M
+            | (static_cast<uint32_t>(tile_m >> 4) << 24);  // M (256 for the pair MMA)
   a.wait_limit = wait_limit();
   a.err = st.err;
-  const int grid = a.total_tiles < st.sms ? a.total_tiles : st.sms;
+  int grid = a.total_tiles < st.sms ? a.total_tiles : st.sms;
+  if (a.pair) grid = 2 * (a.total_tiles < st.sms / 2 ? a.total_tiles : st.sms / 2);
   size_t smem = static_cast<size_t>(stages) * stage_bytes + b_res_bytes + kSmemReserve + epi_bytes;
   // One CTA per SM: the CTA allocates all 512 TMEM columns, so a second resident CTA of this
   // grid would only wait for them.  Asking for more than half the shared memory rules it out.
   if (smem < static_cast<size_t>(kSmemLimit / 2 + 1024)) smem = kSmemLimit / 2 + 1024;
+  if (a.pair) {
+    tc_gemm_s8_pair_kernel<<<grid, kTcThreads, smem, stream>>>(ma, mb, mc, a);
+    g_tc_launches.fetch_add(1, std::memory_order_relaxed);
+    return check_launch("tc_gemm_s8_pair_kernel launch");
+  }
   tc_gemm_s8_kernel<<<grid, kTcThreads, smem, stream>>>(ma, mb, mc, a);
   g_tc_launches.fetch_add(1, std::memory_order_relaxed);
   return check_launch("tc_gemm_s8_kernel launch");
@@ -425,7 +454,9 @@ int run_packed_conv(const DeviceState& st, const int8_t* x, const int8_t* w, voi
   CUtensorMap ma, mb;
   rc = encode_tiled_3d(&ma, a_buf, static_cast<uint64_t>(kp), static_cast<uint64_t>(rows), 1, a.BK, kTcBM, a.BK);
   if (rc) return rc;
-  rc = encode_tiled_3d(&mb, w_buf, static_cast<uint64_t>(kp), static_cast<uint64_t>(g.k), 1, a.BK, a.BN, a.BK);
+  a.pair = want_pair(st, a);
+  rc = encode_tiled_3d(&mb, w_buf, static_cast<uint64_t>(kp), static_cast<uint64_t>(g.k), 1, a.BK,
+                       a.pair ? a.BN / 2 : a.BN, a.BK);
   if (rc) return rc;
   return launch_tc(st, ma, mb, a, stream);
 }
@@ -579,18 +610,22 @@ int b200q_conv2d_s8(const int8_t* d_x, const int8_t* d_w, const int32_t* d_bias,
     a.conv_b = c % a.BK != 0;  // 3-D weight map only when the last K block needs zero fill
     CUtensorMap ma, mb;
     const int kdim = r * s * c;
+    a.mode = is_1x1_plain ? 0 : 1;
+    a.num_kb = is_1x1_plain ? a.cchunks : r * s * a.cchunks;
+    a.pair = want_pair(*st, a);
     if (a.conv_b)  // weights as {C, R*S, K}: a box of BK channels x 1 tap x BN output channels
       rc = encode_tiled_3d(&mb, d_w, static_cast<uint64_t>(c), static_cast<uint64_t>(r * s),
                            static_cast<uint64_t>(k), a.BK, 1, a.BK, a.BN);
-    else  // weights as the K-major matrix [K][R*S*C]
-      rc = encode_tiled_3d(&mb, d_w, static_cast<uint64_t>(kdim), static_cast<uint64_t>(k), 1, a.BK, a.BN, a.BK);
+    else  // weights as the K-major matrix [K][R*S*C] (half the N tile per box for 2-SM tiles)
+      rc = encode_tiled_3d(&mb, d_w, static_cast<uint64_t>(kdim), static_cast<uint64_t>(k), 1, a.BK,
+                           a.pair ? a.BN / 2 : a.BN, a.BK);
     if (rc) return rc;
     if (is_1x1_plain) {
       a.mode = 0;
       a.num_kb = a.cchunks;
       rc = encode_tiled_3d(&ma, d_x, static_cast<uint64_t>(c), static_cast<uint64_t>(M), 1, a.BK, kTcBM, a.BK);
       if (rc) return rc;
-      g_last_path = 2;
+      g_last_path = a.pair ? 8 : 2;
     } else {
       a.mode = 1;
       a.num_kb = r * s * a.cchunks;
@@ -681,12 +716,13 @@ int b200q_bmm_s8(const int8_t* A, const int8_t* B, const int32_t* d_bias, const 
     else
       rc = encode_tiled_3d(&ma, A, (uint64_t)M, (uint64_t)K, (uint64_t)batch, kTcBM, a.BK, 128);
     if (rc) return rc;
+    a.pair = want_pair(*st, a);
     if (tb)
-      rc = encode_tiled_3d(&mb, B, (uint64_t)K, (uint64_t)N, (uint64_t)batch, a.BK, a.BN, 128);
+      rc = encode_tiled_3d(&mb, B, (uint64_t)K, (uint64_t)N, (uint64_t)batch, a.BK, a.pair ? a.BN / 2 : a.BN, 128);
     else
       rc = encode_tiled_3d(&mb, B, (uint64_t)N, (uint64_t)K, (uint64_t)batch, 128, a.BK, 128);
     if (rc) return rc;
-    g_last_path = 2;
+    g_last_path = a.pair ? 8 : 2;
     return launch_tc(*st, ma, mb, a, cs);
   }
   for (int b0 = 0; b0 < batch; b0 += 65535) {

@@ -51,6 +51,7 @@ struct TcArgs {
   int default_clamp;  // int8 output with zp 0 and bounds [-128, 127]: saturating pack does the clamp
   int tma_store;      // outputs leave through shared memory + TMA tensor stores (map tmC)
   int b_res;          // B resident: all num_kb K blocks of the single N tile loaded once per CTA
+  int pair;           // 2-SM tiles (tc_gemm_s8_pair_kernel): 256-row tiles, B box of BN / 2 rows
 };
 
 constexpr int kTcMaxAcc = 8;
@@ -255,7 +256,9 @@ __device__ __forceinline__ void emit_chunk(const TcArgs& a, const CUtensorMap* t
   if (m < a.M) store_chunk<KIND, DCL>(a, v, row_off + n, n, min(32, a.N - n), bias, scale, has_bias);
 }
 
-template <int KIND, bool TMA, bool DCL>
+// PAIR: the CTA is one half of a 2-SM pair (tiles of 2 x 128 rows; this CTA's TMEM holds rows
+// rank * 128 .. + 127 of each tile; the accumulator-empty barrier lives in the leader CTA).
+template <int KIND, bool TMA, bool DCL, bool PAIR>
 __device__ __forceinline__ void epilogue_role_t(const TcArgs& a, const CUtensorMap* tmC, uint32_t tmem_base,
                                               uint32_t accf0, uint32_t acce0, int warp, int lane,
                                               const int32_t* bias, const float* scale, bool has_bias,
@@ -263,17 +266,21 @@ __device__ __forceinline__ void epilogue_role_t(const TcArgs& a, const CUtensorM
   int sb = 0;
   const int q = warp & 3;
   const int half = (warp - 2) >> 2;
-  const int row = q * 32 + lane;
+  const int rank = PAIR ? static_cast<int>(cluster_ctarank()) : 0;
+  const int unit = PAIR ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+  const int nunits = PAIR ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
+  constexpr int TM = PAIR ? 2 * kTcBM : kTcBM;
+  const int row = rank * kTcBM + q * 32 + lane;
   const int tiles_per_batch = a.m_tiles * a.n_tiles;
   int buf = 0;
   uint32_t acc_ph = 0;
   int sel = half;  // this warp's chunks in the current tile: sel, sel + 2, ...
-  for (int tile = blockIdx.x; tile < a.total_tiles; tile += gridDim.x, sel ^= 1) {
+  for (int tile = unit; tile < a.total_tiles; tile += nunits, sel ^= 1) {
     const int b = tile / tiles_per_batch;
     const int rem = tile - b * tiles_per_batch;
     const int mt = rem / a.n_tiles;
     const int nt = rem - mt * a.n_tiles;
-    const int m = mt * kTcBM + row;
+    const int m = mt * TM + row;
     const int n0 = nt * a.BN;
     // Chunks holding columns < N; the two warps of a lane quarter swap parities every tile, so an
     // odd chunk count (N <= 32, N = 96, ...) is shared evenly over two tiles.
@@ -289,7 +296,7 @@ __device__ __forceinline__ void epilogue_role_t(const TcArgs& a, const CUtensorM
     for (int i = 0; i < nmine; i += 2) {
       const int ca = sel + 2 * i, cb = ca + 2;
       if (i + 1 < nmine) tmem_ld_32x32b_x32(tbase + cb * 32, vb);
-      const int mrow0 = mt * kTcBM + q * 32;
+      const int mrow0 = mt * TM + rank * kTcBM + q * 32;
       emit_chunk<KIND, TMA, DCL>(a, tmC, va, b, m, mrow0, row_off, n0 + ca * 32, lane, sbufs, sb, bias, scale,
                                  has_bias);
       tmem_ld_wait();
@@ -302,7 +309,12 @@ __device__ __forceinline__ void epilogue_role_t(const TcArgs& a, const CUtensorM
     }
     tc_fence_before();
     __syncwarp();
-    if (lane == 0) mbar_arrive(acce0 + 8 * buf);
+    if (lane == 0) {
+      if constexpr (PAIR)
+        mbar_arrive_cluster(mapa_shared(acce0 + 8 * buf, 0));
+      else
+        mbar_arrive(acce0 + 8 * buf);
+    }
     if (++buf == a.nacc) {
       buf = 0;
       acc_ph ^= 1u;
@@ -311,7 +323,7 @@ __device__ __forceinline__ void epilogue_role_t(const TcArgs& a, const CUtensorM
   if (TMA && lane == 0) bulk_wait_group_all();
 }
 
-template <int KIND>
+template <int KIND, bool PAIR = false>
 __device__ __forceinline__ void epilogue_role(const TcArgs& a, const CUtensorMap* tmC, uint32_t tmem_base,
                                               uint32_t accf0, uint32_t acce0, int warp, int lane,
                                               const int32_t* bias, const float* scale, bool has_bias,
@@ -320,14 +332,49 @@ __device__ __forceinline__ void epilogue_role(const TcArgs& a, const CUtensorMap
   // compiling it as its own variant keeps the per-element branch out of the unrolled loop.
   if (KIND == kOutS8 && a.default_clamp) {
     if (a.tma_store)
-      epilogue_role_t<KIND, true, true>(a, tmC, tmem_base, accf0, acce0, warp, lane, bias, scale, has_bias, sbufs);
+      epilogue_role_t<KIND, true, true, PAIR>(a, tmC, tmem_base, accf0, acce0, warp, lane, bias, scale, has_bias, sbufs);
     else
-      epilogue_role_t<KIND, false, true>(a, tmC, tmem_base, accf0, acce0, warp, lane, bias, scale, has_bias, sbufs);
+      epilogue_role_t<KIND, false, true, PAIR>(a, tmC, tmem_base, accf0, acce0, warp, lane, bias, scale, has_bias, sbufs);
   } else {
     if (a.tma_store)
-      epilogue_role_t<KIND, true, false>(a, tmC, tmem_base, accf0, acce0, warp, lane, bias, scale, has_bias, sbufs);
+      epilogue_role_t<KIND, true, false, PAIR>(a, tmC, tmem_base, accf0, acce0, warp, lane, bias, scale, has_bias, sbufs);
     else
-      epilogue_role_t<KIND, false, false>(a, tmC, tmem_base, accf0, acce0, warp, lane, bias, scale, has_bias, sbufs);
+      epilogue_role_t<KIND, false, false, PAIR>(a, tmC, tmem_base, accf0, acce0, warp, lane, bias, scale, has_bias, sbufs);
+  }
+}
+
+// Epilogue warps: stage bias / scale in shared memory when they fit, then drain the accumulators.
+template <bool PAIR>
+__device__ __forceinline__ void run_epilogue(const TcArgs& a, const CUtensorMap* tmC, uint32_t tmem_base,
+                                             uint32_t accf0, uint32_t acce0, int warp, int lane, int32_t* s_bias,
+                                             float* s_scale, uint8_t* s_out) {
+  const bool has_bias = a.epi.bias != nullptr;
+  uint8_t* sbufs = s_out + (warp - 2) * 2 * (a.epi.out_kind == kOutS8 ? kEpiStageBytesS8 : kEpiStageBytes);
+  if (a.stage_cols > 0) {
+    // Copy the per-column bias / scale into shared memory once per CTA (epilogue warps only).
+    for (int i = threadIdx.x - 64; i < a.stage_cols; i += kTcEpiWarps * 32) {
+      s_bias[i] = (has_bias && i < a.N) ? __ldg(a.epi.bias + i) : 0;
+      s_scale[i] = (a.epi.scale && i < a.N) ? __ldg(a.epi.scale + i) : 0.0f;
+    }
+    asm volatile("bar.sync 1, %0;" ::"n"(kTcEpiWarps * 32) : "memory");
+    // s_bias / s_scale derive from the shared-memory window here, so the per-chunk reads
+    // compile to shared-memory loads rather than generic ones.
+    if (a.epi.out_kind == kOutS8)
+      epilogue_role<kOutS8, PAIR>(a, tmC, tmem_base, accf0, acce0, warp, lane, s_bias, s_scale, has_bias, sbufs);
+    else if (a.epi.out_kind == kOutS32)
+      epilogue_role<kOutS32, PAIR>(a, tmC, tmem_base, accf0, acce0, warp, lane, s_bias, s_scale, has_bias, sbufs);
+    else
+      epilogue_role<kOutF32, PAIR>(a, tmC, tmem_base, accf0, acce0, warp, lane, s_bias, s_scale, has_bias, sbufs);
+  } else {
+    if (a.epi.out_kind == kOutS8)
+      epilogue_role<kOutS8, PAIR>(a, tmC, tmem_base, accf0, acce0, warp, lane, a.epi.bias, a.epi.scale, has_bias,
+                                  sbufs);
+    else if (a.epi.out_kind == kOutS32)
+      epilogue_role<kOutS32, PAIR>(a, tmC, tmem_base, accf0, acce0, warp, lane, a.epi.bias, a.epi.scale, has_bias,
+                                   sbufs);
+    else
+      epilogue_role<kOutF32, PAIR>(a, tmC, tmem_base, accf0, acce0, warp, lane, a.epi.bias, a.epi.scale, has_bias,
+                                   sbufs);
   }
 }
 
@@ -534,34 +581,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
   } else {
     // ------------------------------------------------------------- epilogue
-    const bool has_bias = a.epi.bias != nullptr;
-    uint8_t* sbufs = s_out + (warp - 2) * 2 * (a.epi.out_kind == kOutS8 ? kEpiStageBytesS8 : kEpiStageBytes);
-    if (a.stage_cols > 0) {
-      // Copy the per-column bias / scale into shared memory once per CTA (epilogue warps only).
-      for (int i = threadIdx.x - 64; i < a.stage_cols; i += kTcEpiWarps * 32) {
-        s_bias[i] = (has_bias && i < a.N) ? __ldg(a.epi.bias + i) : 0;
-        s_scale[i] = (a.epi.scale && i < a.N) ? __ldg(a.epi.scale + i) : 0.0f;
-      }
-      asm volatile("bar.sync 1, %0;" ::"n"(kTcEpiWarps * 32) : "memory");
-      // s_bias / s_scale derive from the shared-memory window here, so the per-chunk reads
-      // compile to shared-memory loads rather than generic ones.
-      if (a.epi.out_kind == kOutS8)
-        epilogue_role<kOutS8>(a, &tmC, tmem_base, accf0, acce0, warp, lane, s_bias, s_scale, has_bias, sbufs);
-      else if (a.epi.out_kind == kOutS32)
-        epilogue_role<kOutS32>(a, &tmC, tmem_base, accf0, acce0, warp, lane, s_bias, s_scale, has_bias, sbufs);
-      else
-        epilogue_role<kOutF32>(a, &tmC, tmem_base, accf0, acce0, warp, lane, s_bias, s_scale, has_bias, sbufs);
-    } else {
-      if (a.epi.out_kind == kOutS8)
-        epilogue_role<kOutS8>(a, &tmC, tmem_base, accf0, acce0, warp, lane, a.epi.bias, a.epi.scale, has_bias,
-                              sbufs);
-      else if (a.epi.out_kind == kOutS32)
-        epilogue_role<kOutS32>(a, &tmC, tmem_base, accf0, acce0, warp, lane, a.epi.bias, a.epi.scale, has_bias,
-                               sbufs);
-      else
-        epilogue_role<kOutF32>(a, &tmC, tmem_base, accf0, acce0, warp, lane, a.epi.bias, a.epi.scale, has_bias,
-                               sbufs);
-    }
+    run_epilogue<false>(a, &tmC, tmem_base, accf0, acce0, warp, lane, s_bias, s_scale, s_out);
   }
 
   tc_fence_before();
@@ -569,6 +589,166 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, a.tmem_cols);
+  }
+}
+
+// 2-SM variant for large tiled GEMMs (mode 0, K-major A and B, BN = 256): a cluster of two CTAs
+// computes a 256 x 256 tile with M = 256 tcgen05 MMAs issued by the leader (rank 0).  Each CTA
+// loads its own 128 rows of A and 128 rows of B (half the B bytes per SM of the one-CTA tile);
+// both loads count on the leader's full barrier; the leader's commits arrive on the empty and
+// accumulator-full barriers of both CTAs; the peer's epilogue warps release accumulators on the
+// leader's barrier.  No TMA multicast.
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
+    tc_gemm_s8_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                           const __grid_constant__ CUtensorMap tmC, const TcArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  const uint32_t stage_a = kTcBM * a.BK;
+  const uint32_t stage_b = (a.BN / 2) * a.BK;
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + a.stages * stage_a;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + a.stages * stage_b);
+  const uint32_t full0 = smem_u32(bars);
+  const uint32_t empty0 = smem_u32(bars + a.stages);
+  const uint32_t accf0 = smem_u32(bars + 2 * a.stages);
+  const uint32_t acce0 = smem_u32(bars + 2 * a.stages + kTcMaxAcc);
+  const uint32_t drain = smem_u32(bars + 2 * a.stages + 2 * kTcMaxAcc);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * a.stages + 2 * kTcMaxAcc + 2);
+  int32_t* s_bias = reinterpret_cast<int32_t*>(bars + 2 * a.stages + 2 * kTcMaxAcc + 4);
+  float* s_scale = reinterpret_cast<float*>(s_bias + a.stage_cols);
+  uint8_t* s_out = reinterpret_cast<uint8_t*>(s_scale + a.stage_cols);
+  s_out += (1024u - (smem_u32(s_out) & 1023u)) & 1023u;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int rank = static_cast<int>(cluster_ctarank());
+  const int unit = static_cast<int>(blockIdx.x >> 1);
+  const int nunits = static_cast<int>(gridDim.x >> 1);
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < a.stages; ++i) {
+      mbar_init(full0 + 8 * i, 2);  // one arrive.expect_tx per CTA of the pair
+      mbar_init(empty0 + 8 * i, 1);
+    }
+    for (int i = 0; i < a.nacc; ++i) {
+      mbar_init(accf0 + 8 * i, 1);
+      mbar_init(acce0 + 8 * i, 2 * kTcEpiWarps);  // epilogue warps of both CTAs
+    }
+    mbar_init(drain, 1);
+    fence_mbar_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(smem_u32(tmem_slot), a.tmem_cols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // barriers of both CTAs initialised before any remote arrive
+  tc_fence_after();
+  const uint32_t tmem_base = __shfl_sync(0xFFFFFFFFu, *tmem_slot, 0);
+  const int tiles_per_batch = a.m_tiles * a.n_tiles;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ producer (both CTAs)
+      int stage = 0;
+      uint32_t ph = 0;
+      const uint32_t tx = stage_a + stage_b;
+      const uint32_t full_leader = mapa_shared(full0, 0);
+      for (int tile = unit; tile < a.total_tiles; tile += nunits) {
+        const int b = tile / tiles_per_batch;
+        const int rem = tile - b * tiles_per_batch;
+        const int mt = rem / a.n_tiles;
+        const int nt = rem - mt * a.n_tiles;
+        const int m0 = mt * 2 * kTcBM + rank * kTcBM;
+        const int nb0 = nt * a.BN + rank * (a.BN / 2);
+        const int bb = a.b_batched ? b : 0;
+        bool ok = true;
+        for (int kb = 0; kb < a.num_kb; ++kb) {
+          if (!mbar_wait_bounded(empty0 + 8 * stage, ph ^ 1u, a.wait_limit, a.err, kDevErrTimeoutProducer)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb = full_leader + 8 * stage;
+          // Relaxed: the bytes are ordered by the TMA's own complete_tx; a release at cluster scope
+          // here cost half the throughput.
+          if (rank == 0)
+            mbar_arrive_expect_tx(full0 + 8 * stage, tx);
+          else
+            mbar_arrive_expect_tx_cluster_relaxed(fb, tx);
+          tma_load_3d_pair(smem_u32(sA + stage * stage_a), &tmA, fb, kb * a.BK, m0, b);
+          tma_load_3d_pair(smem_u32(sB + stage * stage_b), &tmB, fb, kb * a.BK, nb0, bb);
+          if (++stage == a.stages) {
+            stage = 0;
+            ph ^= 1u;
+          }
+        }
+        if (!ok) break;
+      }
+    }
+  } else if (warp == 1) {
+    if (rank == 0) {
+      // ----------------------------------------------------------------- MMA (leader only)
+      int stage = 0;
+      uint32_t ph = 0;
+      int buf = 0;
+      uint32_t acc_ph = 0;
+      bool ok = true;
+      const uint32_t layout = kmajor_layout(a.BK);
+      const uint64_t a_desc0 = make_smem_desc(smem_u32(sA), 16u, 8u * a.BK, layout);
+      const uint64_t b_desc0 = make_smem_desc(smem_u32(sB), 16u, 8u * a.BK, layout);
+      const int ksteps = a.BK / 32;
+      for (int tile = unit; tile < a.total_tiles && ok; tile += nunits) {
+        if (!__all_sync(0xFFFFFFFFu,
+                        mbar_wait_bounded(acce0 + 8 * buf, acc_ph ^ 1u, a.wait_limit, a.err, kDevErrTimeoutMma))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * a.BN);
+        for (int kb = 0; kb < a.num_kb; ++kb) {
+          if (!__all_sync(0xFFFFFFFFu,
+                          mbar_wait_bounded(full0 + 8 * stage, ph, a.wait_limit, a.err, kDevErrTimeoutMma))) {
+            ok = false;
+            break;
+          }
+          const uint64_t ad_s = a_desc0 + ((stage * stage_a) >> 4);
+          const uint64_t bd_s = b_desc0 + ((stage * stage_b) >> 4);
+          if (ksteps == 4) {
+            tc_mma_i8_pair_kblock4(d_tmem, ad_s, bd_s, a.idesc, kb != 0 ? 1u : 0u);
+          } else {
+            for (int j = 0; j < ksteps; ++j)
+              tc_mma_i8_pair_elect(d_tmem, ad_s + 2 * j, bd_s + 2 * j, a.idesc, (kb | j) != 0 ? 1u : 0u);
+          }
+          tc_commit_pair_elect(empty0 + 8 * stage);
+          if (++stage == a.stages) {
+            stage = 0;
+            ph ^= 1u;
+          }
+        }
+        if (!ok) break;
+        tc_commit_pair_elect(accf0 + 8 * buf);
+        if (++buf == a.nacc) {
+          buf = 0;
+          acc_ph ^= 1u;
+        }
+      }
+      tc_commit_pair_elect(drain);
+      mbar_wait_bounded(drain, 0, a.wait_limit, a.err, kDevErrTimeoutMma);
+    }
+  } else {
+    // ------------------------------------------------------------- epilogue (both CTAs)
+    run_epilogue<true>(a, &tmC, tmem_base, accf0, acce0, warp, lane, s_bias, s_scale, s_out);
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // no remote arrive or MMA into this CTA's TMEM after this point
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, a.tmem_cols);
   }
 }
 

@@ -305,6 +305,34 @@ def test_config4_pointwise_full_batch_sampled_images(cuda_lib):
         np.testing.assert_array_equal(y[img:img + 1].cpu().numpy(), oracle.requant_s8(acc, bh, scale_h))
 
 
+def test_pair_tiles_exact_on_long_reduction(cuda_lib):
+    """2-SM tiles (cluster of two CTAs, M = 256 MMAs): config 4b geometry with a batch whose row
+    count is not a multiple of 256; int32 accumulators compared in full with an exact float64
+    product, int8 outputs of sampled images with the oracle."""
+    b2q = _b2q()
+    from my_own_cnn_b200 import synth
+
+    n, h, w, c, k = 100, 14, 14, 2048, 512
+    x = synth.fill_s8_uniform(torch.empty((n, h, w, c), dtype=torch.int8, device="cuda"), 42, 411)
+    wt = synth.fill_s8_uniform(torch.empty((k, 1, 1, c), dtype=torch.int8, device="cuda"), 42, 412)
+    acc = b2q.conv2d_s8(x, wt, None, None, b2q.Conv2DParams(0, 0), b2q.Epilogue.int32())
+    torch.cuda.synchronize()
+    assert b2q.last_path() == "tcgen05-tiled-2sm"
+    ref = (x.reshape(-1, c).double() @ wt.reshape(k, c).double().T).to(torch.int64)
+    assert torch.equal(acc.reshape(-1, k).to(torch.int64), ref)
+    bias = synth.fill_i32_uniform(torch.empty(k, dtype=torch.int32, device="cuda"), 42, 413, -2**15, 2**15)
+    scale_h = synth.scales_f32(k, 42, 414)
+    y = b2q.conv2d_s8(x, wt, bias, torch.from_numpy(scale_h).cuda(), b2q.Conv2DParams(0, 0), b2q.Epilogue.int8())
+    torch.cuda.synchronize()
+    assert b2q.last_path() == "tcgen05-tiled-2sm"
+    wh = synth.s8_uniform_host(42, 412, -127, 127, 0, k * c).reshape(k, 1, 1, c)
+    bh = synth.i32_uniform_host(42, 413, -2**15, 2**15, 0, k)
+    for img in (0, 51, 99):
+        xh = synth.s8_uniform_host(42, 411, -127, 127, img * h * w * c, h * w * c).reshape(1, h, w, c)
+        a = oracle.conv_s8(oracle.conv_args(1, h, w, c, 1, 1, k, 0, 0), xh, wh)
+        np.testing.assert_array_equal(y[img:img + 1].cpu().numpy(), oracle.requant_s8(a, bh, scale_h))
+
+
 # ------------------------------------------------------------------ failure path
 
 def test_bounded_wait_timeout_reports_and_context_survives(cuda_lib):
