@@ -335,6 +335,107 @@ __global__ void __launch_bounds__(256) im2col_pack_s8_kernel(const int8_t* __res
   }
 }
 
+// Depthwise 3x3 with dilation 1, PX horizontally adjacent output pixels per thread (stride_w =
+// SW): the 3 x ((PX - 1) * SW + 3) input words the pixels share are loaded once (stride 1, PX = 4:
+// 18 loads for 4 pixels instead of 36), unconditionally when the window is inside the image.  The
+// per-pixel arithmetic is the one of dw_conv_s8_kernel.
+template <int KIND, int SW, int PX>
+__global__ void __launch_bounds__(256) dw_conv_s8_px_kernel(const int8_t* __restrict__ x, const int8_t* __restrict__ w,
+                                                            void* __restrict__ y, ConvGeom g, Epilogue e) {
+  constexpr int NC = (PX - 1) * SW + 3;
+  const int groups8 = g.c >> 3;
+  const int lanes_per_block = blockDim.x / groups8;
+  const int cg = threadIdx.x % groups8;
+  const int pl = threadIdx.x / groups8;
+  if (pl >= lanes_per_block) return;
+  const int c0 = cg * 8;
+  uint32_t wq[8][2], w8[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int8_t* wp = w + static_cast<size_t>(c0 + j) * 9;
+    uint32_t v[9];
+#pragma unroll
+    for (int t = 0; t < 9; ++t) v[t] = static_cast<uint8_t>(__ldg(wp + t));
+    wq[j][0] = v[0] | (v[1] << 8) | (v[2] << 16) | (v[3] << 24);
+    wq[j][1] = v[4] | (v[5] << 8) | (v[6] << 16) | (v[7] << 24);
+    w8[j] = v[8] << (8 * (j & 3));
+  }
+  int32_t bsum[8];
+  float sc[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    bsum[j] = e.bias ? __ldg(e.bias + c0 + j) : 0;
+    sc[j] = e.scale ? __ldg(e.scale + c0 + j) : 0.0f;
+  }
+  const int wgroups = (g.wo + PX - 1) / PX;
+  const int nitems = g.n * g.ho * wgroups;  // < 2^31 (checked by the caller)
+  const int row_pitch = g.w * g.c;
+  for (int it = blockIdx.x * lanes_per_block + pl; it < nitems; it += gridDim.x * lanes_per_block) {
+    const int wgi = it % wgroups;
+    const int t2 = it / wgroups;
+    const int ho = t2 % g.ho;
+    const int n = t2 / g.ho;
+    const int wo0 = wgi * PX;
+    const int h0 = ho * g.stride_h - g.pad_h, w0 = wo0 * SW - g.pad_w;
+    const int8_t* base = x + (static_cast<size_t>(n) * g.h * g.w) * g.c + c0;
+    uint2 v[3][NC];
+    if (h0 >= 0 && h0 + 2 < g.h && w0 >= 0 && w0 + NC - 1 < g.w) {
+#pragma unroll
+      for (int r = 0; r < 3; ++r)
+#pragma unroll
+        for (int cc = 0; cc < NC; ++cc)
+          v[r][cc] = __ldg(reinterpret_cast<const uint2*>(base + (h0 + r) * row_pitch + (w0 + cc) * g.c));
+    } else {
+#pragma unroll
+      for (int r = 0; r < 3; ++r)
+#pragma unroll
+        for (int cc = 0; cc < NC; ++cc) {
+          const int hi = h0 + r, wi = w0 + cc;
+          v[r][cc] = (hi >= 0 && hi < g.h && wi >= 0 && wi < g.w)
+                         ? __ldg(reinterpret_cast<const uint2*>(base + hi * row_pitch + wi * g.c))
+                         : make_uint2(0u, 0u);
+        }
+    }
+#pragma unroll
+    for (int p = 0; p < PX; ++p) {
+      if (wo0 + p >= g.wo) break;
+      uint32_t xl[9], xh[9];
+#pragma unroll
+      for (int t = 0; t < 9; ++t) {
+        xl[t] = v[t / 3][p * SW + t % 3].x;
+        xh[t] = v[t / 3][p * SW + t % 3].y;
+      }
+      int acc[8];
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        const uint32_t* xs = half ? xh : xl;
+        uint32_t c[4], d[4];
+        transpose4x4_bytes(xs[0], xs[1], xs[2], xs[3], c[0], c[1], c[2], c[3]);
+        transpose4x4_bytes(xs[4], xs[5], xs[6], xs[7], d[0], d[1], d[2], d[3]);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int ch = half * 4 + j;
+          int a = __dp4a(static_cast<int>(c[j]), static_cast<int>(wq[ch][0]), 0);
+          a = __dp4a(static_cast<int>(d[j]), static_cast<int>(wq[ch][1]), a);
+          acc[ch] = __dp4a(static_cast<int>(xs[8]), static_cast<int>(w8[ch]), a);
+        }
+      }
+      const size_t o = (static_cast<size_t>(t2) * g.wo + wo0 + p) * g.c + c0;
+      if constexpr (KIND == kOutS8) {
+        int q[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) q[j] = requant_one(wrap_add(acc[j], bsum[j]), sc[j], e);
+        const uint32_t lo = __byte_perm(__byte_perm(q[0], q[1], 0x0040), __byte_perm(q[2], q[3], 0x0040), 0x5410);
+        const uint32_t hi = __byte_perm(__byte_perm(q[4], q[5], 0x0040), __byte_perm(q[6], q[7], 0x0040), 0x5410);
+        *reinterpret_cast<uint2*>(static_cast<int8_t*>(y) + o) = make_uint2(lo, hi);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) epilogue_store(e, y, o + j, acc[j], c0 + j);
+      }
+    }
+  }
+}
+
 // Weights [k][R*S*C] -> [k][kp] with zero columns past R*S*C.
 __global__ void weight_pad_s8_kernel(const int8_t* __restrict__ w, int8_t* __restrict__ wp, int k, int rsc, int kp) {
   const size_t total = static_cast<size_t>(k) * kp;
