@@ -667,17 +667,17 @@ int b200q_conv2d_s8(const int8_t* d_x, const int8_t* d_w, const int32_t* d_bias,
     g_last_path = 4;
     if (g_dw_px && g.dil_h == 1 && g.dil_w == 1 && (g.stride_w == 1 || g.stride_w == 2)) {
       // Several adjacent output pixels per thread share their input words.
-      const int px = g.stride_w == 1 ? 4 : 2;
+      const int px = g.stride_w == 1 ? 8 : 2;
       const long long items = static_cast<long long>(g.n) * g.ho * ((g.wo + px - 1) / px);
       const long long blocks = (items + lanes - 1) / lanes;
       const int grid = static_cast<int>(blocks < st->sms * 8ll ? blocks : st->sms * 8ll);
       if (g.stride_w == 1) {
         if (e.out_kind == kOutS8)
-          dw_conv_s8_px_kernel<kOutS8, 1, 4><<<grid, 256, 0, cs>>>(d_x, d_w, d_y, g, e);
+          dw_conv_s8_px_kernel<kOutS8, 1, 8><<<grid, 256, 0, cs>>>(d_x, d_w, d_y, g, e);
         else if (e.out_kind == kOutS32)
-          dw_conv_s8_px_kernel<kOutS32, 1, 4><<<grid, 256, 0, cs>>>(d_x, d_w, d_y, g, e);
+          dw_conv_s8_px_kernel<kOutS32, 1, 8><<<grid, 256, 0, cs>>>(d_x, d_w, d_y, g, e);
         else
-          dw_conv_s8_px_kernel<kOutF32, 1, 4><<<grid, 256, 0, cs>>>(d_x, d_w, d_y, g, e);
+          dw_conv_s8_px_kernel<kOutF32, 1, 8><<<grid, 256, 0, cs>>>(d_x, d_w, d_y, g, e);
       } else {
         if (e.out_kind == kOutS8)
           dw_conv_s8_px_kernel<kOutS8, 2, 2><<<grid, 256, 0, cs>>>(d_x, d_w, d_y, g, e);

@@ -336,8 +336,8 @@ __global__ void __launch_bounds__(256) im2col_pack_s8_kernel(const int8_t* __res
 }
 
 // Depthwise 3x3 with dilation 1, PX horizontally adjacent output pixels per thread (stride_w =
-// SW): the 3 x ((PX - 1) * SW + 3) input words the pixels share are loaded once (stride 1, PX = 4:
-// 18 loads for 4 pixels instead of 36), unconditionally when the window is inside the image.  The
+// SW): the 3 x ((PX - 1) * SW + 3) input words the pixels share are loaded once (stride 1, PX = 8:
+// 30 loads for 8 pixels instead of 72), unconditionally when the window is inside the image.  The
 // per-pixel arithmetic is the one of dw_conv_s8_kernel.
 template <int KIND, int SW, int PX>
 __global__ void __launch_bounds__(256) dw_conv_s8_px_kernel(const int8_t* __restrict__ x, const int8_t* __restrict__ w,

@@ -163,7 +163,7 @@ def test_conv_s8_tcgen05_pointwise(cuda_lib, shape):
 
 @pytest.mark.parametrize("shape,groups,expect", [
     ((2, 20, 20, 48, 3, 3, 48, 1, 2, 1), 48, "cuda-core-depthwise"),   # depthwise s2
-    ((1, 17, 19, 96, 3, 3, 96, 1, 1, 1), 96, "cuda-core-depthwise"),   # W tail of the 4-pixel groups
+    ((1, 17, 19, 96, 3, 3, 96, 1, 1, 1), 96, "cuda-core-depthwise"),   # W tail of the 8-pixel groups
     ((2, 9, 10, 8, 3, 3, 8, 1, 2, 1), 8, "cuda-core-depthwise"),        # C = 8, s2, 2-pixel groups
     ((3, 7, 7, 960, 3, 3, 960, 1, 1, 1), 960, "cuda-core-depthwise"),   # MobileNetV2 7x7 stage
     ((1, 11, 13, 16, 3, 3, 16, 2, 1, 2), 16, "cuda-core-depthwise"),    # dilation 2: one pixel/thread
