@@ -110,6 +110,24 @@ int b200q_conv2d_s8(const int8_t* d_x, const int8_t* d_w, const int32_t* d_bias,
                     const float* d_scale, void* d_y, int n, int h, int w, int c, int r, int s,
                     int k, const b200q_conv_params* p, const b200q_epilogue* epi, void* stream);
 
+/* b200q_conv2d_s8 with a residual add fused into the int8 epilogue (the shortcut of a ResNet /
+ * MobileNetV2 block; no reference counterpart):
+ *   p = fp32(acc + bias[k]) * scale[k] + fp32(res[pixel][k]) * res_scale   (IEEE steps, no fma)
+ *   q = clamp(rint(p), lo - zp, hi - zp) + zp
+ * d_res: int8 NHWC with the output's shape, 16-byte aligned for the tensor-core paths.  int8 outputs
+ * only (B200Q_ERR_INVALID_ARG otherwise). */
+int b200q_conv2d_s8_add(const int8_t* d_x, const int8_t* d_w, const int32_t* d_bias, const float* d_scale,
+                        const int8_t* d_res, float res_scale, int8_t* d_y, int n, int h, int w, int c, int r,
+                        int s, int k, const b200q_conv_params* p, const b200q_epilogue* epi, void* stream);
+
+/* int8 NHWC max pool (R x S window, stride, zero-free padding: padded positions take no part).
+ * Output [n, (h + 2*pad_h - r)/stride_h + 1, (w + 2*pad_w - s)/stride_w + 1, c]. */
+int b200q_maxpool_s8(const int8_t* d_x, int8_t* d_y, int n, int h, int w, int c, int r, int s, int stride_h,
+                     int stride_w, int pad_h, int pad_w, void* stream);
+
+/* int8 NHWC global average pool -> [n][c]: q = clamp(rint(fp32(sum) / fp32(h*w)), -128, 127). */
+int b200q_global_avgpool_s8(const int8_t* d_x, int8_t* d_y, int n, int h, int w, int c, void* stream);
+
 /* int8 batched GEMM, layouts as bmm.h:9-29, int32 accumulation, per-column epilogue.
  * d_bias: [N] int32 or NULL; d_col_scale: [N] fp32 (required for S8 / F32 outputs). */
 int b200q_bmm_s8(const int8_t* A, const int8_t* B, const int32_t* d_bias, const float* d_col_scale,

@@ -204,6 +204,35 @@ def conv2d_s8_into(y, x, w, bias, scale, n, h, wd, c, r, s, k, p: Conv2DParams, 
                                           ctypes.byref(cp), ctypes.byref(ce), _stream(stream)))
 
 
+def conv2d_s8_add_into(y, x, w, bias, scale, res, res_scale: float, n, h, wd, c, r, s, k, p: Conv2DParams,
+                       epi: Epilogue, stream=None) -> None:
+    """conv2d_s8_into with a residual add fused into the int8 epilogue (b200q_conv2d_s8_add):
+    p = fp32(acc + bias) * scale + fp32(res) * res_scale, rounded and clamped like Epilogue.int8."""
+    ce = epi.to_c()
+    cp = p.to_c()
+    _lib.check(_lib.lib().b200q_conv2d_s8_add(_ptr(x), _ptr(w), _ptr(bias), _ptr(scale), _ptr(res),
+                                              ctypes.c_float(res_scale), _ptr(y), n, h, wd, c, r, s, k,
+                                              ctypes.byref(cp), ctypes.byref(ce), _stream(stream)))
+
+
+def conv2d_s8_add(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None, scale: torch.Tensor,
+                  res: torch.Tensor, res_scale: float, p: Conv2DParams, epi: Epilogue,
+                  out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+    """int8 conv + residual: res is int8 with the output's shape [n, ho, wo, k]."""
+    if x.dtype != torch.int8 or w.dtype != torch.int8 or res.dtype != torch.int8:
+        raise TypeError("conv2d_s8_add takes int8 activations, weights and residual")
+    n, h, wd, c = x.shape
+    k, r, s, _ = w.shape
+    ho, wo = conv_out_shape(h, wd, c, r, s, k, p)
+    if tuple(res.shape) != (n, ho, wo, k):
+        raise RuntimeError(f"residual shape {tuple(res.shape)} != output shape {(n, ho, wo, k)}")
+    if out is None:
+        out = torch.empty((n, ho, wo, k), dtype=torch.int8, device=x.device)
+    conv2d_s8_add_into(out, x.contiguous(), w.contiguous(), bias, scale, res.contiguous(), res_scale, n, h, wd, c,
+                       r, s, k, p, epi, stream)
+    return out
+
+
 def conv2d_s8(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None, scale: torch.Tensor | None,
               p: Conv2DParams, epi: Epilogue, out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
     """x: int8 [n,h,w,c]; w: int8 [k,r,s,c/groups]; bias int32 [k] or None; scale fp32 [k]."""

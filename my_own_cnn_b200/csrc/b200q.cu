@@ -148,6 +148,8 @@ int make_epilogue(const b200q_epilogue* epi, const int32_t* bias, const float* s
   out->hi = epi->clamp_hi;
   out->bias = bias;
   out->scale = scale;
+  out->res = nullptr;
+  out->res_scale = 0.0f;
   return B200Q_OK;
 }
 
@@ -562,9 +564,10 @@ int b200q_bmm_matmul_i32(const int32_t* A, const int32_t* B, int32_t* C, int bat
   return B200Q_OK;
 }
 
-int b200q_conv2d_s8(const int8_t* d_x, const int8_t* d_w, const int32_t* d_bias, const float* d_scale, void* d_y,
-                    int n, int h, int w, int c, int r, int s, int k, const b200q_conv_params* p,
-                    const b200q_epilogue* epi, void* stream) {
+// Dispatch of the int8 conv (shared by the plain and the residual-add entry points).
+static int conv2d_s8_impl(const int8_t* d_x, const int8_t* d_w, const int32_t* d_bias, const float* d_scale,
+                   const int8_t* d_res, float res_scale, void* d_y, int n, int h, int w, int c, int r, int s, int k,
+                   const b200q_conv_params* p, const b200q_epilogue* epi, void* stream) {
   ConvGeom g;
   int rc = conv_geom(n, h, w, c, r, s, k, p, 1, 1, &g);
   if (rc) return rc;
@@ -572,6 +575,11 @@ int b200q_conv2d_s8(const int8_t* d_x, const int8_t* d_w, const int32_t* d_bias,
   Epilogue e;
   rc = make_epilogue(epi, d_bias, d_scale, &e);
   if (rc) return rc;
+  if (d_res) {
+    if (e.out_kind != kOutS8) return fail(B200Q_ERR_INVALID_ARG, "a residual add needs int8 outputs");
+    e.res = d_res;
+    e.res_scale = res_scale;
+  }
   DeviceState* st = nullptr;
   rc = device_state(&st);
   if (rc) return rc;
@@ -579,7 +587,7 @@ int b200q_conv2d_s8(const int8_t* d_x, const int8_t* d_w, const int32_t* d_bias,
   const long long M = static_cast<long long>(n) * g.ho * g.wo;
   const size_t x_bytes = static_cast<size_t>(n) * h * w * c;
   const bool vec_ptrs = aligned16(d_x) && aligned16(d_w) && aligned16(d_y) && (!d_bias || aligned16(d_bias)) &&
-                        (!d_scale || aligned16(d_scale));
+                        (!d_scale || aligned16(d_scale)) && (!d_res || aligned16(d_res));
   const bool is_1x1_plain = r == 1 && s == 1 && g.stride_h == 1 && g.stride_w == 1 && g.pad_h == 0 && g.pad_w == 0;
   const bool corners_ok = g.pad_w <= 127 && g.pad_h <= 127 && g.pad_w - (s - 1) * g.dil_w >= -128 &&
                           g.pad_h - (r - 1) * g.dil_h >= -128 && (s - 1) * g.dil_w <= 255 && (r - 1) * g.dil_h <= 255 &&
@@ -651,7 +659,8 @@ int b200q_conv2d_s8(const int8_t* d_x, const int8_t* d_w, const int32_t* d_bias,
   // Also taken by groups == 1 convs the im2col TMA cannot read (activations < 128 KiB, corner limits).
   if (g_policy.load() == 0 && g.groups == 1 && (c % 16 != 0 ? M >= 4096 : M >= 64) && M < (1ll << 31) &&
       kp_packed <= 16384 &&
-      aligned16(d_y) && (!d_bias || aligned16(d_bias)) && (!d_scale || aligned16(d_scale))) {
+      aligned16(d_y) && (!d_bias || aligned16(d_bias)) && (!d_scale || aligned16(d_scale)) &&
+      (!d_res || aligned16(d_res))) {
     void* ws = nullptr;
     rc = get_workspace(packed_scratch_bytes(M, k, kp_packed), cs, &ws);
     if (rc) return rc;
@@ -659,7 +668,7 @@ int b200q_conv2d_s8(const int8_t* d_x, const int8_t* d_w, const int32_t* d_bias,
     return run_packed_conv(*st, d_x, d_w, d_y, g, e, static_cast<int8_t*>(ws), cs);
   }
   const size_t total = static_cast<size_t>(M) * k;
-  if (g.groups == c && k == c && c % 8 == 0 && c <= 8 * 256 && r == 3 && s == 3 && M < (1ll << 31) &&
+  if (!d_res && g.groups == c && k == c && c % 8 == 0 && c <= 8 * 256 && r == 3 && s == 3 && M < (1ll << 31) &&
       aligned16(d_x) &&
       aligned16(d_y)) {
     const int groups8 = c / 8;
@@ -704,6 +713,19 @@ int b200q_conv2d_s8(const int8_t* d_x, const int8_t* d_w, const int32_t* d_bias,
   conv_s8_generic_kernel<<<grid_for(total, 256, st->sms), 256, 0, cs>>>(d_x, d_w, d_y, g, e, dp4a);
   g_last_path = 3;
   return check_launch("conv_s8_generic_kernel launch");
+}
+
+int b200q_conv2d_s8(const int8_t* d_x, const int8_t* d_w, const int32_t* d_bias, const float* d_scale, void* d_y,
+                    int n, int h, int w, int c, int r, int s, int k, const b200q_conv_params* p,
+                    const b200q_epilogue* epi, void* stream) {
+  return conv2d_s8_impl(d_x, d_w, d_bias, d_scale, nullptr, 0.0f, d_y, n, h, w, c, r, s, k, p, epi, stream);
+}
+
+int b200q_conv2d_s8_add(const int8_t* d_x, const int8_t* d_w, const int32_t* d_bias, const float* d_scale,
+                        const int8_t* d_res, float res_scale, int8_t* d_y, int n, int h, int w, int c, int r, int s,
+                        int k, const b200q_conv_params* p, const b200q_epilogue* epi, void* stream) {
+  if (!d_res) return fail(B200Q_ERR_INVALID_ARG, "residual pointer is null");
+  return conv2d_s8_impl(d_x, d_w, d_bias, d_scale, d_res, res_scale, d_y, n, h, w, c, r, s, k, p, epi, stream);
 }
 
 int b200q_bmm_s8(const int8_t* A, const int8_t* B, const int32_t* d_bias, const float* d_col_scale, void* C,
@@ -773,6 +795,44 @@ int b200q_bmm_s8(const int8_t* A, const int8_t* B, const int32_t* d_bias, const 
 // Packed low-channel conv with fixed scratch: see include/b200q.h.  Same arithmetic and kernels as
 // the packed path of b200q_conv2d_s8, but the im2col matrix and padded weights go to the static
 // array above instead of a workspace, and nothing is allocated.
+int b200q_maxpool_s8(const int8_t* d_x, int8_t* d_y, int n, int h, int w, int c, int r, int s, int stride_h,
+                     int stride_w, int pad_h, int pad_w, void* stream) {
+  if (n < 0 || h <= 0 || w <= 0 || c <= 0 || r <= 0 || s <= 0) return fail(B200Q_ERR_INVALID_ARG, "bad pool shape");
+  if (stride_h <= 0 || stride_w <= 0) return fail(B200Q_ERR_INVALID_ARG, "stride must be > 0");
+  if (pad_h < 0 || pad_w < 0 || pad_h >= r || pad_w >= s)
+    return fail(B200Q_ERR_INVALID_ARG, "padding must be >= 0 and smaller than the window");
+  if (!d_x || !d_y) return fail(B200Q_ERR_INVALID_ARG, "null tensor pointer");
+  ConvGeom g{};
+  g.n = n; g.h = h; g.w = w; g.c = c; g.r = r; g.s = s; g.k = c;
+  g.ho = (h + 2 * pad_h - r) / stride_h + 1;
+  g.wo = (w + 2 * pad_w - s) / stride_w + 1;
+  g.pad_h = pad_h; g.pad_w = pad_w; g.stride_h = stride_h; g.stride_w = stride_w; g.dil_h = 1; g.dil_w = 1;
+  g.groups = c; g.cg = 1; g.kg = 1; g.by = 1; g.bx = 1; g.bho = g.ho; g.bwo = g.wo;
+  if (g.ho <= 0 || g.wo <= 0) return fail(B200Q_ERR_INVALID_ARG, "pool window larger than the padded input");
+  if (n == 0) return B200Q_OK;
+  if (c % 16 == 0 && !(aligned16(d_x) && aligned16(d_y)))
+    return fail(B200Q_ERR_INVALID_ARG, "C %% 16 == 0 pools need 16-byte aligned tensors");
+  DeviceState* st = nullptr;
+  int rc = device_state(&st);
+  if (rc) return rc;
+  const size_t items = static_cast<size_t>(n) * g.ho * g.wo * (c % 16 == 0 ? c / 16 : c);
+  maxpool_s8_kernel<<<grid_for(items, 256, st->sms), 256, 0, as_stream(stream)>>>(d_x, d_y, g);
+  return check_launch("maxpool_s8_kernel launch");
+}
+
+int b200q_global_avgpool_s8(const int8_t* d_x, int8_t* d_y, int n, int h, int w, int c, void* stream) {
+  if (n < 0 || h <= 0 || w <= 0 || c <= 0) return fail(B200Q_ERR_INVALID_ARG, "bad pool shape");
+  if (static_cast<long long>(h) * w > (1 << 23)) return fail(B200Q_ERR_UNSUPPORTED, "pool window too large");
+  if (!d_x || !d_y) return fail(B200Q_ERR_INVALID_ARG, "null tensor pointer");
+  if (n == 0) return B200Q_OK;
+  DeviceState* st = nullptr;
+  int rc = device_state(&st);
+  if (rc) return rc;
+  const size_t warps = static_cast<size_t>(n) * ((c + 31) / 32);
+  global_avgpool_s8_kernel<<<grid_for(warps * 32, 256, st->sms), 256, 0, as_stream(stream)>>>(d_x, d_y, n, h * w, c);
+  return check_launch("global_avgpool_s8_kernel launch");
+}
+
 int b200q_conv2d_s8_packed_noalloc(const int8_t* d_x, const int8_t* d_w, const int32_t* d_bias, const float* d_scale,
                                    void* d_y, int n, int h, int w, int c, int r, int s, int k,
                                    const b200q_conv_params* p, const b200q_epilogue* epi, void* stream) {

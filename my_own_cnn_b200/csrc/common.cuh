@@ -21,6 +21,8 @@ struct Epilogue {
   int hi;
   const int32_t* bias;  // may be null
   const float* scale;   // required for S8 / F32
+  const int8_t* res;    // int8 residual with the output's layout (S8 outputs only), or null
+  float res_scale;
 };
 
 // Requantize one int32 value (bias already added, wrapping):
@@ -31,6 +33,20 @@ struct Epilogue {
 __device__ __forceinline__ int requant_one(int32_t t, float sc, const Epilogue& e) {
   const int r = __float2int_rn(__fmul_rn(__int2float_rn(t), sc));
   return min(max(r, e.lo - e.zp), e.hi - e.zp) + e.zp;
+}
+
+// Requantize with a fused residual add (int8 residual code rv, its scale rs):
+//   p = fl(fl(t) * scale) + fl(rv * rs)   (three IEEE round-to-nearest-even operations, no fma)
+//   q = clamp(rint_sat(p), lo - zp, hi - zp) + zp
+__device__ __forceinline__ int requant_res(int32_t t, float sc, int rv, float rs, const Epilogue& e) {
+  const float p = __fadd_rn(__fmul_rn(__int2float_rn(t), sc), __fmul_rn(__int2float_rn(rv), rs));
+  const int r = __float2int_rn(p);
+  return min(max(r, e.lo - e.zp), e.hi - e.zp) + e.zp;
+}
+
+// Signed byte i (0..3) of a packed word.
+__device__ __forceinline__ int sbyte(uint32_t w, int i) {
+  return static_cast<int>(static_cast<int32_t>(w << (24 - 8 * i)) >> 24);
 }
 
 __device__ __forceinline__ int32_t wrap_add(int32_t a, int32_t b) {
@@ -44,6 +60,9 @@ __device__ __forceinline__ void epilogue_store(const Epilogue& e, void* out, siz
     static_cast<int32_t*>(out)[idx] = t;
   } else if (e.out_kind == kOutF32) {
     static_cast<float*>(out)[idx] = __fmul_rn(__int2float_rn(t), __ldg(e.scale + col));
+  } else if (e.res) {
+    static_cast<int8_t*>(out)[idx] =
+        static_cast<int8_t>(requant_res(t, __ldg(e.scale + col), __ldg(e.res + idx), e.res_scale, e));
   } else {
     static_cast<int8_t*>(out)[idx] = static_cast<int8_t>(requant_one(t, __ldg(e.scale + col), e));
   }

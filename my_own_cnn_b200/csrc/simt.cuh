@@ -436,6 +436,75 @@ __global__ void __launch_bounds__(256) dw_conv_s8_px_kernel(const int8_t* __rest
   }
 }
 
+// Max pool, NHWC int8: one thread = one output pixel x 16 channels (C % 16 == 0) using 4-lane
+// signed byte max, or one output element otherwise.  Padded positions take no part (a window that
+// lies entirely in the padding gives -128).
+__global__ void maxpool_s8_kernel(const int8_t* __restrict__ x, int8_t* __restrict__ y, ConvGeom g) {
+  const bool vec = g.c % 16 == 0;
+  const int cv = vec ? g.c / 16 : g.c;
+  const long long total = static_cast<long long>(g.n) * g.ho * g.wo * cv;
+  for (long long idx = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; idx < total;
+       idx += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int cc = static_cast<int>(idx % cv);
+    const long long pix = idx / cv;
+    const int wo = static_cast<int>(pix % g.wo);
+    const long long t = pix / g.wo;
+    const int ho = static_cast<int>(t % g.ho);
+    const int n = static_cast<int>(t / g.ho);
+    const int8_t* base = x + static_cast<size_t>(n) * g.h * g.w * g.c;
+    if (vec) {
+      uint4 m = make_uint4(0x80808080u, 0x80808080u, 0x80808080u, 0x80808080u);
+      for (int i = 0; i < g.r; ++i) {
+        const int hi = ho * g.stride_h - g.pad_h + i;
+        if (hi < 0 || hi >= g.h) continue;
+        for (int j = 0; j < g.s; ++j) {
+          const int wi = wo * g.stride_w - g.pad_w + j;
+          if (wi < 0 || wi >= g.w) continue;
+          const uint4 v = __ldg(reinterpret_cast<const uint4*>(base + (static_cast<size_t>(hi) * g.w + wi) * g.c) + cc);
+          m.x = __vmaxs4(m.x, v.x); m.y = __vmaxs4(m.y, v.y); m.z = __vmaxs4(m.z, v.z); m.w = __vmaxs4(m.w, v.w);
+        }
+      }
+      reinterpret_cast<uint4*>(y + pix * g.c)[cc] = m;
+    } else {
+      int m = -128;
+      for (int i = 0; i < g.r; ++i) {
+        const int hi = ho * g.stride_h - g.pad_h + i;
+        if (hi < 0 || hi >= g.h) continue;
+        for (int j = 0; j < g.s; ++j) {
+          const int wi = wo * g.stride_w - g.pad_w + j;
+          if (wi < 0 || wi >= g.w) continue;
+          m = max(m, static_cast<int>(base[(static_cast<size_t>(hi) * g.w + wi) * g.c + cc]));
+        }
+      }
+      y[pix * g.c + cc] = static_cast<int8_t>(m);
+    }
+  }
+}
+
+// Global average pool, NHWC int8 -> [n][c]: one warp per (image, 32-channel group); lanes stride
+// over the pixels with exact int32 sums, then q = clamp(rint_sat(sum / (h*w)), -128, 127) with one
+// IEEE division.
+__global__ void global_avgpool_s8_kernel(const int8_t* __restrict__ x, int8_t* __restrict__ y, int n, int hw,
+                                         int c) {
+  const int warps = blockDim.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int cgroups = (c + 31) / 32;
+  const long long items = static_cast<long long>(n) * cgroups;
+  const float cnt = static_cast<float>(hw);
+  for (long long it = blockIdx.x * static_cast<long long>(warps) + (threadIdx.x >> 5); it < items;
+       it += static_cast<long long>(gridDim.x) * warps) {
+    const int b = static_cast<int>(it / cgroups);
+    const int ch = static_cast<int>(it % cgroups) * 32 + lane;
+    if (ch >= c) continue;
+    const int8_t* p = x + static_cast<size_t>(b) * hw * c + ch;
+    int32_t sum = 0;
+    for (int i = 0; i < hw; ++i) sum += p[static_cast<size_t>(i) * c];
+    int q = __float2int_rn(__fdiv_rn(static_cast<float>(sum), cnt));
+    q = min(max(q, -128), 127);
+    y[static_cast<size_t>(b) * c + ch] = static_cast<int8_t>(q);
+  }
+}
+
 // Weights [k][R*S*C] -> [k][kp] with zero columns past R*S*C.
 __global__ void weight_pad_s8_kernel(const int8_t* __restrict__ w, int8_t* __restrict__ wp, int k, int rsc, int kp) {
   const size_t total = static_cast<size_t>(k) * kp;

@@ -81,13 +81,22 @@ __device__ __forceinline__ uint32_t pack4_sat_s8(int a, int b, int c, int d) {
 
 // Vector form of the fused epilogue: the first 4 * NQ columns of the chunk (NQ = 8: all 32,
 // NQ = 4: the first 16), 16-byte bias / scale reads and 16-byte stores.
-template <int KIND, bool DCL, int NQ>
+template <int KIND, bool DCL, int NQ, bool RES>
 __device__ __forceinline__ void store_vec(const TcArgs& a, const uint32_t (&v)[32], size_t off, int n,
                                           const int32_t* bias, const float* scale, bool has_bias) {
   const Epilogue& e = a.epi;
   const int4* bp = reinterpret_cast<const int4*>(bias + n);
   const float4* sp = reinterpret_cast<const float4*>(scale + n);
   uint32_t packed[8];
+  uint32_t rw[8];  // residual bytes of this row's columns (RES only)
+  if constexpr (RES) {
+    const uint4 r0 = *reinterpret_cast<const uint4*>(e.res + off);
+    rw[0] = r0.x; rw[1] = r0.y; rw[2] = r0.z; rw[3] = r0.w;
+    if constexpr (NQ == 8) {
+      const uint4 r1 = *reinterpret_cast<const uint4*>(e.res + off + 16);
+      rw[4] = r1.x; rw[5] = r1.y; rw[6] = r1.z; rw[7] = r1.w;
+    }
+  }
 #pragma unroll
   for (int q = 0; q < NQ; ++q) {
     int t0 = static_cast<int>(v[4 * q + 0]), t1 = static_cast<int>(v[4 * q + 1]);
@@ -105,7 +114,14 @@ __device__ __forceinline__ void store_vec(const TcArgs& a, const uint32_t (&v)[3
       if constexpr (KIND == kOutF32) {
         reinterpret_cast<float4*>(static_cast<float*>(a.out) + off)[q] = make_float4(p0, p1, p2, p3);
       } else {
-        int r0 = __float2int_rn(p0), r1 = __float2int_rn(p1), r2 = __float2int_rn(p2), r3 = __float2int_rn(p3);
+        float f0 = p0, f1 = p1, f2 = p2, f3 = p3;
+        if constexpr (RES) {
+          f0 = __fadd_rn(f0, __fmul_rn(__int2float_rn(sbyte(rw[q], 0)), e.res_scale));
+          f1 = __fadd_rn(f1, __fmul_rn(__int2float_rn(sbyte(rw[q], 1)), e.res_scale));
+          f2 = __fadd_rn(f2, __fmul_rn(__int2float_rn(sbyte(rw[q], 2)), e.res_scale));
+          f3 = __fadd_rn(f3, __fmul_rn(__int2float_rn(sbyte(rw[q], 3)), e.res_scale));
+        }
+        int r0 = __float2int_rn(f0), r1 = __float2int_rn(f1), r2 = __float2int_rn(f2), r3 = __float2int_rn(f3);
         if constexpr (!DCL) {
           const int lo = e.lo - e.zp, hi = e.hi - e.zp;
           r0 = min(max(r0, lo), hi) + e.zp; r1 = min(max(r1, lo), hi) + e.zp;
@@ -125,17 +141,17 @@ __device__ __forceinline__ void store_vec(const TcArgs& a, const uint32_t (&v)[3
 // Fused epilogue for one row and 32 consecutive output columns [n, n + valid).
 // bias / scale point at shared memory (staged) or global memory; bias may be null.
 // All array indices are compile-time constants after unrolling: nothing spills to local memory.
-template <int KIND, bool DCL>
+template <int KIND, bool DCL, bool RES>
 __device__ __forceinline__ void store_chunk(const TcArgs& a, const uint32_t (&v)[32], size_t off, int n, int valid,
                                             const int32_t* bias, const float* scale, bool has_bias) {
   const Epilogue& e = a.epi;
   if (a.vec_ok) {
     if (valid == 32) {
-      store_vec<KIND, DCL, 8>(a, v, off, n, bias, scale, has_bias);
+      store_vec<KIND, DCL, 8, RES>(a, v, off, n, bias, scale, has_bias);
       return;
     }
     if (valid == 16) {  // the 16-column tail of N = 16, 48, 80, ...
-      store_vec<KIND, DCL, 4>(a, v, off, n, bias, scale, has_bias);
+      store_vec<KIND, DCL, 4, RES>(a, v, off, n, bias, scale, has_bias);
       return;
     }
   }
@@ -148,6 +164,9 @@ __device__ __forceinline__ void store_chunk(const TcArgs& a, const uint32_t (&v)
         static_cast<int32_t*>(a.out)[off + j] = t;
       } else if constexpr (KIND == kOutF32) {
         static_cast<float*>(a.out)[off + j] = __fmul_rn(__int2float_rn(t), scale[n + j]);
+      } else if constexpr (RES) {
+        static_cast<int8_t*>(a.out)[off + j] =
+            static_cast<int8_t>(requant_res(t, scale[n + j], e.res[off + j], e.res_scale, e));
       } else {
         static_cast<int8_t*>(a.out)[off + j] = static_cast<int8_t>(requant_one(t, scale[n + j], e));
       }
@@ -192,14 +211,26 @@ __device__ __forceinline__ void stage_chunk_4b(const TcArgs& a, const uint32_t (
 // 32B-swizzled 1 KiB buffer (16-byte half h of row r at half h ^ ((r / 4) % 2), the layout of a
 // SWIZZLE_32B tensor map: conflict-free for one 16-byte store per lane) and leave with one TMA
 // store, which clips rows >= M and columns >= N.  The requantization is the one of store_chunk.
-template <bool DCL>
+template <bool DCL, bool RES>
 __device__ __forceinline__ void stage_chunk_s8(const TcArgs& a, const uint32_t (&v)[32], int n, int lane,
                                                uint8_t* sbuf, const int32_t* bias, const float* scale,
-                                               bool has_bias) {
+                                               bool has_bias, const int8_t* rrow) {
   const Epilogue& e = a.epi;
   const int4* bp = reinterpret_cast<const int4*>(bias + n);
   const float4* sp = reinterpret_cast<const float4*>(scale + n);
   uint32_t packed[8];
+  uint32_t rw[8] = {0, 0, 0, 0, 0, 0, 0, 0};  // residual bytes of the row (RES; rows past M read none)
+  if constexpr (RES) {
+    if (rrow) {
+      const bool full = n + 32 <= a.N;
+      const uint4 r0 = *reinterpret_cast<const uint4*>(rrow);
+      rw[0] = r0.x; rw[1] = r0.y; rw[2] = r0.z; rw[3] = r0.w;
+      if (full || n + 16 < a.N) {
+        const uint4 r1 = *reinterpret_cast<const uint4*>(rrow + 16);
+        rw[4] = r1.x; rw[5] = r1.y; rw[6] = r1.z; rw[7] = r1.w;
+      }
+    }
+  }
 #pragma unroll
   for (int q = 0; q < 8; ++q) {
     int t0 = static_cast<int>(v[4 * q + 0]), t1 = static_cast<int>(v[4 * q + 1]);
@@ -209,10 +240,15 @@ __device__ __forceinline__ void stage_chunk_s8(const TcArgs& a, const uint32_t (
       t0 = wrap_add(t0, bb.x); t1 = wrap_add(t1, bb.y); t2 = wrap_add(t2, bb.z); t3 = wrap_add(t3, bb.w);
     }
     const float4 s4 = sp[q];
-    int r0 = __float2int_rn(__fmul_rn(__int2float_rn(t0), s4.x));
-    int r1 = __float2int_rn(__fmul_rn(__int2float_rn(t1), s4.y));
-    int r2 = __float2int_rn(__fmul_rn(__int2float_rn(t2), s4.z));
-    int r3 = __float2int_rn(__fmul_rn(__int2float_rn(t3), s4.w));
+    float f0 = __fmul_rn(__int2float_rn(t0), s4.x), f1 = __fmul_rn(__int2float_rn(t1), s4.y);
+    float f2 = __fmul_rn(__int2float_rn(t2), s4.z), f3 = __fmul_rn(__int2float_rn(t3), s4.w);
+    if constexpr (RES) {
+      f0 = __fadd_rn(f0, __fmul_rn(__int2float_rn(sbyte(rw[q], 0)), e.res_scale));
+      f1 = __fadd_rn(f1, __fmul_rn(__int2float_rn(sbyte(rw[q], 1)), e.res_scale));
+      f2 = __fadd_rn(f2, __fmul_rn(__int2float_rn(sbyte(rw[q], 2)), e.res_scale));
+      f3 = __fadd_rn(f3, __fmul_rn(__int2float_rn(sbyte(rw[q], 3)), e.res_scale));
+    }
+    int r0 = __float2int_rn(f0), r1 = __float2int_rn(f1), r2 = __float2int_rn(f2), r3 = __float2int_rn(f3);
     if constexpr (!DCL) {
       const int lo = e.lo - e.zp, hi = e.hi - e.zp;
       r0 = min(max(r0, lo), hi) + e.zp; r1 = min(max(r1, lo), hi) + e.zp;
@@ -230,7 +266,7 @@ __device__ __forceinline__ void stage_chunk_s8(const TcArgs& a, const uint32_t (
 // to the lane quarter w%4) and, in the j-th tile of its CTA, the chunks of 32 columns with
 // chunk % 2 == ((w-2)/4 + j) % 2.  The TMEM load of the next chunk is issued before the current
 // chunk is processed (two register buffers).
-template <int KIND, bool TMA, bool DCL>
+template <int KIND, bool TMA, bool DCL, bool RES>
 __device__ __forceinline__ void emit_chunk(const TcArgs& a, const CUtensorMap* tmC, const uint32_t (&v)[32], int b,
                                            int m, int mrow0, size_t row_off, int n, int lane, uint8_t* sbufs,
                                            int& sb, const int32_t* bias, const float* scale,
@@ -241,7 +277,8 @@ __device__ __forceinline__ void emit_chunk(const TcArgs& a, const CUtensorMap* t
     if (lane == 0) bulk_wait_group_read<1>();  // the store that used this buffer has read it
     __syncwarp();
     if constexpr (KIND == kOutS8)
-      stage_chunk_s8<DCL>(a, v, n, lane, buf, bias, scale, has_bias);
+      stage_chunk_s8<DCL, RES>(a, v, n, lane, buf, bias, scale, has_bias,
+                               RES && m < a.M ? a.epi.res + row_off + n : nullptr);
     else
       stage_chunk_4b<KIND>(a, v, n, lane, buf, bias, scale, has_bias);
     fence_proxy_async_smem();
@@ -253,12 +290,12 @@ __device__ __forceinline__ void emit_chunk(const TcArgs& a, const CUtensorMap* t
     sb ^= 1;
     return;
   }
-  if (m < a.M) store_chunk<KIND, DCL>(a, v, row_off + n, n, min(32, a.N - n), bias, scale, has_bias);
+  if (m < a.M) store_chunk<KIND, DCL, RES>(a, v, row_off + n, n, min(32, a.N - n), bias, scale, has_bias);
 }
 
 // PAIR: the CTA is one half of a 2-SM pair (tiles of 2 x 128 rows; this CTA's TMEM holds rows
 // rank * 128 .. + 127 of each tile; the accumulator-empty barrier lives in the leader CTA).
-template <int KIND, bool TMA, bool DCL, bool PAIR>
+template <int KIND, bool TMA, bool DCL, bool PAIR, bool RES>
 __device__ __forceinline__ void epilogue_role_t(const TcArgs& a, const CUtensorMap* tmC, uint32_t tmem_base,
                                               uint32_t accf0, uint32_t acce0, int warp, int lane,
                                               const int32_t* bias, const float* scale, bool has_bias,
@@ -297,12 +334,12 @@ __device__ __forceinline__ void epilogue_role_t(const TcArgs& a, const CUtensorM
       const int ca = sel + 2 * i, cb = ca + 2;
       if (i + 1 < nmine) tmem_ld_32x32b_x32(tbase + cb * 32, vb);
       const int mrow0 = mt * TM + rank * kTcBM + q * 32;
-      emit_chunk<KIND, TMA, DCL>(a, tmC, va, b, m, mrow0, row_off, n0 + ca * 32, lane, sbufs, sb, bias, scale,
+      emit_chunk<KIND, TMA, DCL, RES>(a, tmC, va, b, m, mrow0, row_off, n0 + ca * 32, lane, sbufs, sb, bias, scale,
                                  has_bias);
       tmem_ld_wait();
       if (i + 1 < nmine) {
         if (i + 2 < nmine) tmem_ld_32x32b_x32(tbase + (cb + 2) * 32, va);
-        emit_chunk<KIND, TMA, DCL>(a, tmC, vb, b, m, mrow0, row_off, n0 + cb * 32, lane, sbufs, sb, bias, scale,
+        emit_chunk<KIND, TMA, DCL, RES>(a, tmC, vb, b, m, mrow0, row_off, n0 + cb * 32, lane, sbufs, sb, bias, scale,
                                    has_bias);
         tmem_ld_wait();
       }
@@ -329,17 +366,29 @@ __device__ __forceinline__ void epilogue_role(const TcArgs& a, const CUtensorMap
                                               const int32_t* bias, const float* scale, bool has_bias,
                                               uint8_t* sbufs) {
   // The default int8 range [-128, 127] with zero point 0 is clamped by the saturating pack alone;
-  // compiling it as its own variant keeps the per-element branch out of the unrolled loop.
-  if (KIND == kOutS8 && a.default_clamp) {
+  // compiling it as its own variant keeps the per-element branch out of the unrolled loop.  A fused
+  // residual add (int8 outputs only) is a variant of its own too.
+  if (KIND == kOutS8 && a.epi.res) {
     if (a.tma_store)
-      epilogue_role_t<KIND, true, true, PAIR>(a, tmC, tmem_base, accf0, acce0, warp, lane, bias, scale, has_bias, sbufs);
+      epilogue_role_t<KIND, true, false, PAIR, true>(a, tmC, tmem_base, accf0, acce0, warp, lane, bias, scale,
+                                                     has_bias, sbufs);
     else
-      epilogue_role_t<KIND, false, true, PAIR>(a, tmC, tmem_base, accf0, acce0, warp, lane, bias, scale, has_bias, sbufs);
+      epilogue_role_t<KIND, false, false, PAIR, true>(a, tmC, tmem_base, accf0, acce0, warp, lane, bias, scale,
+                                                      has_bias, sbufs);
+  } else if (KIND == kOutS8 && a.default_clamp) {
+    if (a.tma_store)
+      epilogue_role_t<KIND, true, true, PAIR, false>(a, tmC, tmem_base, accf0, acce0, warp, lane, bias, scale,
+                                                     has_bias, sbufs);
+    else
+      epilogue_role_t<KIND, false, true, PAIR, false>(a, tmC, tmem_base, accf0, acce0, warp, lane, bias, scale,
+                                                      has_bias, sbufs);
   } else {
     if (a.tma_store)
-      epilogue_role_t<KIND, true, false, PAIR>(a, tmC, tmem_base, accf0, acce0, warp, lane, bias, scale, has_bias, sbufs);
+      epilogue_role_t<KIND, true, false, PAIR, false>(a, tmC, tmem_base, accf0, acce0, warp, lane, bias, scale,
+                                                      has_bias, sbufs);
     else
-      epilogue_role_t<KIND, false, false, PAIR>(a, tmC, tmem_base, accf0, acce0, warp, lane, bias, scale, has_bias, sbufs);
+      epilogue_role_t<KIND, false, false, PAIR, false>(a, tmC, tmem_base, accf0, acce0, warp, lane, bias, scale,
+                                                       has_bias, sbufs);
   }
 }
 

@@ -18,7 +18,9 @@
  *       p = f * scale[k]             (one fp32 multiply, no contraction)
  *       r = rint_sat(p)              (round half to even, saturated to int32, NaN -> 0)
  *       q = clamp(r, lo - zp, hi - zp) + zp
- *     and the dequantized fp32 output  y = (float)(acc + bias[k]) * scale[k].
+ *     and the dequantized fp32 output  y = (float)(acc + bias[k]) * scale[k];
+ *     with a fused residual add, p gains + (float)res * res_scale before rounding;
+ *   - int8 max pool and global average pool (new; the int8 network stacks between convs).
  *   - a counter-based splitmix64 generator that the CUDA library implements
  *     identically, so any slice of a synthetic tensor can be regenerated here.
  *
@@ -219,6 +221,61 @@ void orc_requant_s8(const int32_t* acc, size_t rows, int k, const int32_t* bias,
       if (r < lo - zp) r = lo - zp;
       if (r > hi - zp) r = hi - zp;
       out[i * k + j] = (int8_t)(r + zp);
+    }
+}
+
+/* Requantize with a fused residual add (the int8 residual res has the accumulators' layout):
+ *   p = (float)(acc + bias) * scale[k] + (float)res * res_scale   (each step one IEEE operation)
+ *   q = clamp(rint_sat(p), lo - zp, hi - zp) + zp */
+void orc_requant_res_s8(const int32_t* acc, size_t rows, int k, const int32_t* bias, const float* scale,
+                        const int8_t* res, float res_scale, int zp, int lo, int hi, int8_t* out) {
+  for (size_t i = 0; i < rows; ++i)
+    for (int j = 0; j < k; ++j) {
+      const uint32_t t = (uint32_t)acc[i * k + j] + (uint32_t)(bias ? bias[j] : 0);
+      const float pr = (float)(int32_t)t * scale[j];
+      const float rr = (float)res[i * k + j] * res_scale;
+      const float p = pr + rr;
+      int32_t r = rint_sat(p);
+      if (r < lo - zp) r = lo - zp;
+      if (r > hi - zp) r = hi - zp;
+      out[i * k + j] = (int8_t)(r + zp);
+    }
+}
+
+/* Max pool, NHWC int8, R x S window, stride / padding; padded positions take no part. */
+int orc_maxpool_s8(const int8_t* x, int8_t* y, int n, int h, int w, int c, int r, int s, int stride_h,
+                   int stride_w, int pad_h, int pad_w) {
+  const int ho = (h + 2 * pad_h - r) / stride_h + 1, wo = (w + 2 * pad_w - s) / stride_w + 1;
+  if (ho <= 0 || wo <= 0) return ORC_EINVAL;
+  for (int b = 0; b < n; ++b)
+    for (int oh = 0; oh < ho; ++oh)
+      for (int ow = 0; ow < wo; ++ow)
+        for (int ch = 0; ch < c; ++ch) {
+          int m = -128;
+          for (int i = 0; i < r; ++i)
+            for (int j = 0; j < s; ++j) {
+              const int ih = oh * stride_h - pad_h + i, iw = ow * stride_w - pad_w + j;
+              if (ih < 0 || ih >= h || iw < 0 || iw >= w) continue;
+              const int v = x[(((size_t)b * h + ih) * w + iw) * c + ch];
+              if (v > m) m = v;
+            }
+          y[(((size_t)b * ho + oh) * wo + ow) * c + ch] = (int8_t)m;
+        }
+  return ORC_OK;
+}
+
+/* Global average pool, NHWC int8 -> [n][c]: q = clamp(rint_sat((float)sum / (float)(h*w)), -128, 127)
+ * (sum exact in int32; one IEEE division). */
+void orc_global_avgpool_s8(const int8_t* x, int8_t* y, int n, int h, int w, int c) {
+  const float cnt = (float)(h * w);
+  for (int b = 0; b < n; ++b)
+    for (int ch = 0; ch < c; ++ch) {
+      int32_t sum = 0;
+      for (int i = 0; i < h * w; ++i) sum += x[((size_t)b * h * w + i) * c + ch];
+      int32_t q = rint_sat((float)sum / cnt);
+      if (q < -128) q = -128;
+      if (q > 127) q = 127;
+      y[(size_t)b * c + ch] = (int8_t)q;
     }
 }
 

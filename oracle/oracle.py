@@ -52,6 +52,9 @@ def lib():
         L.orc_requant_s8.argtypes = [vp, c_size_t, c_int, vp, vp, c_int, c_int, c_int, vp]
         L.orc_requant_s8.restype = None
         L.orc_dequant_f32.argtypes = [vp, c_size_t, c_int, vp, vp, vp]
+        L.orc_requant_res_s8.argtypes = [vp, c_size_t, c_int, vp, vp, vp, c_float, c_int, c_int, c_int, vp]
+        L.orc_maxpool_s8.argtypes = [vp, vp] + [c_int] * 10
+        L.orc_global_avgpool_s8.argtypes = [vp, vp] + [c_int] * 4
         L.orc_dequant_f32.restype = None
         L.orc_bmm_i32.argtypes = [vp, vp, vp] + [c_int] * 6
         L.orc_bmm_i32.restype = None
@@ -153,6 +156,38 @@ def requant_s8(acc: np.ndarray, bias, scale: np.ndarray, zp: int = 0, lo: int = 
     out = np.empty(acc.shape, dtype=np.int8)
     lib().orc_requant_s8(_p(acc), rows, k, None if b is None else _p(b), _p(sc), zp, lo, hi, _p(out))
     return out
+
+
+def requant_res_s8(acc: np.ndarray, bias, scale: np.ndarray, res: np.ndarray, res_scale: float, zp: int = 0,
+                   lo: int = -128, hi: int = 127) -> np.ndarray:
+    acc = np.ascontiguousarray(acc, dtype=np.int32)
+    k = acc.shape[-1]
+    sc = np.ascontiguousarray(scale, dtype=np.float32)
+    rs = np.ascontiguousarray(res, dtype=np.int8)
+    assert rs.size == acc.size
+    b = None if bias is None else np.ascontiguousarray(bias, dtype=np.int32)
+    out = np.empty(acc.shape, dtype=np.int8)
+    lib().orc_requant_res_s8(_p(acc), acc.size // k, k, None if b is None else _p(b), _p(sc), _p(rs),
+                             float(res_scale), zp, lo, hi, _p(out))
+    return out
+
+
+def maxpool_s8(x: np.ndarray, r: int, s: int, stride_h: int, stride_w: int, pad_h: int, pad_w: int) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.int8)
+    n, h, w, c = x.shape
+    ho, wo = (h + 2 * pad_h - r) // stride_h + 1, (w + 2 * pad_w - s) // stride_w + 1
+    y = np.empty((n, ho, wo, c), dtype=np.int8)
+    if lib().orc_maxpool_s8(_p(x), _p(y), n, h, w, c, r, s, stride_h, stride_w, pad_h, pad_w):
+        raise RuntimeError("invalid pool shape")
+    return y
+
+
+def global_avgpool_s8(x: np.ndarray) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.int8)
+    n, h, w, c = x.shape
+    y = np.empty((n, c), dtype=np.int8)
+    lib().orc_global_avgpool_s8(_p(x), _p(y), n, h, w, c)
+    return y
 
 
 def dequant_f32(acc: np.ndarray, bias, scale: np.ndarray) -> np.ndarray:

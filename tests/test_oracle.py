@@ -143,3 +143,40 @@ def test_uniform_distribution_moments():
     v = oracle.fill_s8_uniform(42, 1, -127, 127, 0, 200000).astype(np.float64)
     assert abs(v.mean()) < 0.5
     assert abs(v.std() - np.sqrt((255**2 - 1) / 12)) < 0.5
+
+
+def test_residual_requant_oracle():
+    """Residual add: p = fl(fl(t) * s) + fl(res * rs) in fp32, then the int8 requant rules.
+    res = 0 reduces to the plain requant; a numpy restatement with float32 steps agrees."""
+    rng = np.random.default_rng(11)
+    acc = rng.integers(-2**20, 2**20, size=(37, 24), dtype=np.int64).astype(np.int32)
+    bias = rng.integers(-2**15, 2**15, size=24, dtype=np.int64).astype(np.int32)
+    scale = rng.uniform(1e-4, 1e-3, size=24).astype(np.float32)
+    zero = np.zeros(acc.shape, dtype=np.int8)
+    np.testing.assert_array_equal(oracle.requant_res_s8(acc, bias, scale, zero, 0.7),
+                                  oracle.requant_s8(acc, bias, scale))
+    res = rng.integers(-128, 128, size=acc.shape, dtype=np.int64).astype(np.int8)
+    rs = np.float32(0.37)
+    for lo, hi in [(-128, 127), (0, 127), (0, 96)]:
+        got = oracle.requant_res_s8(acc, bias, scale, res, float(rs), 0, lo, hi)
+        t = (acc.astype(np.int64) + bias).astype(np.int32)
+        p = (t.astype(np.float32) * scale).astype(np.float32) + (res.astype(np.float32) * rs).astype(np.float32)
+        want = np.clip(np.rint(p.astype(np.float32)), lo, hi).astype(np.int8)
+        np.testing.assert_array_equal(got, want)
+
+
+def test_pool_oracles_against_numpy():
+    rng = np.random.default_rng(12)
+    x = rng.integers(-128, 128, size=(2, 9, 11, 24), dtype=np.int64).astype(np.int8)
+    y = oracle.maxpool_s8(x, 3, 3, 2, 2, 1, 1)
+    assert y.shape == (2, 5, 6, 24)
+    xp = np.pad(x.astype(np.int32), ((0, 0), (1, 1), (1, 1), (0, 0)), constant_values=-1000)
+    want = np.full(y.shape, -1000, dtype=np.int32)
+    for i in range(3):
+        for j in range(3):
+            want = np.maximum(want, xp[:, i:i + 9:2, j:j + 11:2, :][:, :5, :6, :])
+    np.testing.assert_array_equal(y, want.astype(np.int8))
+    a = oracle.global_avgpool_s8(x)
+    s = x.astype(np.int32).sum(axis=(1, 2))
+    want = np.clip(np.rint(s.astype(np.float32) / np.float32(99)), -128, 127).astype(np.int8)
+    np.testing.assert_array_equal(a, want)
