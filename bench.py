@@ -445,6 +445,72 @@ def run_net(args, rank: int, world: int, local_rank: int) -> dict | None:
     return out
 
 
+def run_chain(args, rank: int, world: int, local_rank: int) -> dict | None:
+    """Configs 3 / 5 as chained networks: one step = the whole int8 forward of the per-GPU batch
+    (stem, max pool, every conv fed by the previous layer, residual adds fused into the conv
+    epilogues, global average pool), input resident in HBM."""
+    import torch
+
+    import my_own_cnn_b200 as b2q
+    from my_own_cnn_b200 import _lib, nets, synth
+    from my_own_cnn_b200.shard import checksum, gather_tensors, max_over_ranks
+
+    net = args.config.replace("-chain", "")
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    stream = torch.cuda.current_stream()
+    batch = args.batch or NET_BATCH[net]
+    model = nets.ChainedNet(net, SEED, dev)
+    x = torch.empty((batch, 224, 224, 3), dtype=torch.int8, device=dev)
+    act = torch.from_numpy(nets.act_table()).to(dev)
+    synth.fill_s8_table(x, SEED + rank, 1, act)  # each rank its own seeded images
+    flush = torch.empty(256 << 20, dtype=torch.int8, device=dev)
+    for _ in range(args.warmup):
+        y = model.forward(x)
+    torch.cuda.synchronize()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    sampler = ClockSampler()
+    if rank == 0:
+        sampler.start()
+    launches0 = b2q.tc_launch_count()
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    for st in range(args.steps):
+        flush.fill_(st & 0x7F)
+        evs[st][0].record(stream)
+        y = model.forward(x)
+        evs[st][1].record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    clocks = sampler.stop() if rank == 0 else None
+    launches = b2q.tc_launch_count() - launches0
+    if _lib.lib().b200q_device_error() != 0:
+        raise RuntimeError(_lib.lib().b200q_last_error().decode())
+    step_ms = sum(a.elapsed_time(b) for a, b in evs) / args.steps
+    (step_ms,) = max_over_ranks([step_ms], device=dev)
+    checksums = [g.tolist() for g in gather_tensors(checksum(y))]
+    if rank != 0:
+        return None
+    peaks = load_peaks()
+    ops = sum(sp.ops_per_image() for sp in model.specs) * batch
+    return {
+        "metric": METRIC, "value": round(world * batch / (step_ms * 1e-3), 1), "unit": "images/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_ms, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "s8xs8->s32",
+        "data": "synthetic (seeded splitmix64 input images; seeded random-init int8 weights)",
+        "config": {"workload": f"{net} int8 forward, chained (stem, max pool, convs with fused residual adds, "
+                               f"global average pool), per-GPU batch {batch}",
+                   "global_batch": batch * world, "per_gpu_batch": batch, "parallelism": f"dp{world} (batch shards)",
+                   "l2": "flushed between timed steps (256 MiB write outside the events)"},
+        "tops_per_gpu": round(ops / (step_ms * 1e-3) / 1e12, 1),
+        "frac_of_int8_peak": round(ops / (step_ms * 1e-3) / 1e12 / (2.0 * peaks["bf16_tflops"]), 4),
+        "gpu_launches": int(launches), "clocks": clocks,
+        "verify": {"pooled_feature_checksum_per_rank": checksums},
+    }
+
+
 def run_bmm(args, rank: int, world: int, local_rank: int) -> dict | None:
     """Config 2: batch 64 of 1024^3 int8 NN GEMMs per GPU, int32 accumulators and the per-column
     requantized int8 variant (two launches per step)."""
@@ -506,7 +572,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--chunk", type=int, default=64, help="images per chunk of the e2e pipeline")
-    ap.add_argument("--config", default="pointwise", choices=["pointwise", "resnet50", "mobilenetv2", "bmm"],
+    ap.add_argument("--config", default="pointwise",
+                    choices=["pointwise", "resnet50", "mobilenetv2", "resnet50-chain", "mobilenetv2-chain", "bmm"],
                     help="pointwise (BASELINE config 4, the default bench line); the others report configs 3 / 5 / 2")
     ap.add_argument("--batch", type=int, default=0, help="per-GPU batch for the network configs (0 = BASELINE)")
     args = ap.parse_args()
@@ -530,6 +597,8 @@ def main():
         dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
     if args.config in NET_BATCH:
         out = run_net(args, rank, world, local_rank)
+    elif args.config.endswith("-chain"):
+        out = run_chain(args, rank, world, local_rank)
     elif args.config == "bmm":
         out = run_bmm(args, rank, world, local_rank)
     else:

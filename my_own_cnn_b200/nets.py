@@ -23,7 +23,8 @@ import numpy as np
 import torch
 
 from . import synth
-from .conv import Conv2DParams, Epilogue, conv2d_s8_into, conv_out_shape
+from .conv import Conv2DParams, Epilogue, conv2d_s8_add_into, conv2d_s8_into, conv_out_shape
+from .pool import global_avgpool_s8, maxpool_s8
 
 Q6 = 96
 
@@ -150,3 +151,119 @@ def host_layer_tensors(sp: LayerSpec, i: int, seed: int, img0: int, nimg: int):
     b = synth.i32_uniform_host(seed, 100 * i + 3, -2**15, 2**15, 0, sp.k)
     s = synth.scales_f32(sp.k, seed, 100 * i + 4)
     return x, w, b, s
+
+
+# ---------------------------------------------------------------------------------------------
+# Chained networks: every layer of the table fed by the previous one, with the residual adds fused
+# into the conv epilogues, ResNet-50's 3x3/2 max pool after the stem and a global average pool at
+# the end.  Weights, biases and scales are the seeded per-layer tensors of NetData (same ids).
+
+RES_SCALE = 0.5  # scale of the shortcut branch in the fused residual add (synthetic network)
+
+
+@dataclass(frozen=True)
+class ChainOp:
+    kind: str          # "conv", "maxpool", "avgpool"
+    layer: int = -1    # index into the spec list (conv)
+    src: int = 0       # input buffer id
+    dst: int = 0       # output buffer id
+    res: int = -1      # residual buffer id (conv with fused add), -1 = none
+
+
+def chain_plan(name: str) -> list[ChainOp]:
+    """Data flow of the chained network over buffer ids (0 = network input)."""
+    specs = NETS[name]()
+    ops: list[ChainOp] = []
+    nxt = 1
+    if name == "resnet50":
+        ops.append(ChainOp("conv", 0, 0, nxt)); nxt += 1
+        ops.append(ChainOp("maxpool", -1, nxt - 1, nxt)); cur = nxt; nxt += 1
+        i = 1
+        while i < len(specs):
+            conv1, conv2, conv3 = i, i + 1, i + 2
+            proj = i + 3 if i + 3 < len(specs) and specs[i + 3].name.endswith(".proj") else -1
+            ops.append(ChainOp("conv", conv1, cur, nxt)); b1 = nxt; nxt += 1
+            ops.append(ChainOp("conv", conv2, b1, nxt)); b2 = nxt; nxt += 1
+            short = cur
+            if proj >= 0:
+                ops.append(ChainOp("conv", proj, cur, nxt)); short = nxt; nxt += 1
+            ops.append(ChainOp("conv", conv3, b2, nxt, res=short)); cur = nxt; nxt += 1
+            i += 4 if proj >= 0 else 3
+    elif name == "mobilenetv2":
+        ops.append(ChainOp("conv", 0, 0, nxt)); cur = nxt; nxt += 1
+        i = 1
+        while i < len(specs) - 1:
+            blk_in = cur
+            if specs[i].name.endswith(".expand"):
+                ops.append(ChainOp("conv", i, cur, nxt)); cur = nxt; nxt += 1; i += 1
+            dw = specs[i]
+            ops.append(ChainOp("conv", i, cur, nxt)); cur = nxt; nxt += 1; i += 1
+            proj = specs[i]
+            cin = specs[i - 1].c if not specs[i - 2].name.endswith(".expand") else specs[i - 2].c
+            residual = dw.stride == 1 and proj.k == cin
+            ops.append(ChainOp("conv", i, cur, nxt, res=blk_in if residual else -1)); cur = nxt; nxt += 1; i += 1
+        ops.append(ChainOp("conv", len(specs) - 1, cur, nxt)); cur = nxt; nxt += 1
+    else:
+        raise ValueError(name)
+    ops.append(ChainOp("avgpool", -1, cur, nxt))
+    return ops
+
+
+class ChainedNet:
+    """A whole int8 network on one device.  forward(x) runs every op of chain_plan on the stream;
+    intermediate buffers are allocated once per batch size and reused."""
+
+    def __init__(self, name: str, seed: int, device):
+        self.name, self.seed, self.device = name, seed, torch.device(device)
+        self.specs = NETS[name]()
+        self.plan = chain_plan(name)
+        wtab = torch.from_numpy(weight_table()).to(self.device)
+        self.weights = []
+        for i, sp in enumerate(self.specs):
+            w = synth.fill_s8_table(torch.empty((sp.k, sp.r, sp.r, sp.c // sp.groups), dtype=torch.int8,
+                                                device=self.device), seed, 100 * i + 2, wtab)
+            b = synth.fill_i32_uniform(torch.empty(sp.k, dtype=torch.int32, device=self.device), seed, 100 * i + 3,
+                                       -2**15, 2**15)
+            s = torch.from_numpy(synth.scales_f32(sp.k, seed, 100 * i + 4)).to(self.device)
+            self.weights.append((w, b, s))
+        self._bufs: dict[int, dict[int, torch.Tensor]] = {}
+
+    def _buffers(self, n: int, x: torch.Tensor) -> dict[int, torch.Tensor]:
+        if n not in self._bufs:
+            shapes = {0: tuple(x.shape[1:])}
+            bufs = {}
+            for op in self.plan:
+                h, w, c = shapes[op.src]
+                if op.kind == "conv":
+                    sp = self.specs[op.layer]
+                    ho, wo = sp.out_hw()
+                    shapes[op.dst] = (ho, wo, sp.k)
+                elif op.kind == "maxpool":
+                    shapes[op.dst] = ((h + 2 - 3) // 2 + 1, (w + 2 - 3) // 2 + 1, c)
+                else:
+                    shapes[op.dst] = (1, 1, c)
+                bufs[op.dst] = torch.empty((n,) + shapes[op.dst], dtype=torch.int8, device=self.device)
+            self._bufs[n] = bufs
+        return self._bufs[n]
+
+    def forward(self, x: torch.Tensor, stream=None) -> torch.Tensor:
+        """x: int8 [n, 224, 224, 3] on the device -> pooled int8 features [n, C_last]."""
+        n = x.shape[0]
+        bufs = self._buffers(n, x)
+        bufs[0] = x
+        for op in self.plan:
+            src, dst = bufs[op.src], bufs[op.dst]
+            if op.kind == "conv":
+                sp = self.specs[op.layer]
+                w, b, s = self.weights[op.layer]
+                if op.res >= 0:
+                    conv2d_s8_add_into(dst, src, w, b, s, bufs[op.res], RES_SCALE, n, sp.h, sp.w, sp.c, sp.r, sp.r,
+                                       sp.k, sp.params(), sp.epilogue(), stream)
+                else:
+                    conv2d_s8_into(dst, src, w, b, s, n, sp.h, sp.w, sp.c, sp.r, sp.r, sp.k, sp.params(),
+                                   sp.epilogue(), stream)
+            elif op.kind == "maxpool":
+                maxpool_s8(src, 3, 3, 2, 1, out=dst, stream=stream)
+            else:
+                global_avgpool_s8(src, out=dst.view(n, -1), stream=stream)
+        return bufs[self.plan[-1].dst].view(n, -1)
