@@ -495,6 +495,9 @@ def run_chain(args, rank: int, world: int, local_rank: int) -> dict | None:
         return None
     peaks = load_peaks()
     ops = sum(sp.ops_per_image() for sp in model.specs) * batch
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        cpu = chain_cpu_baseline(model, args.cpu_seconds)
     return {
         "metric": METRIC, "value": round(world * batch / (step_ms * 1e-3), 1), "unit": "images/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_ms, 4), "higher_is_better": True,
@@ -508,7 +511,48 @@ def run_chain(args, rank: int, world: int, local_rank: int) -> dict | None:
         "frac_of_int8_peak": round(ops / (step_ms * 1e-3) / 1e12 / (2.0 * peaks["bf16_tflops"]), 4),
         "gpu_launches": int(launches), "clocks": clocks,
         "verify": {"pooled_feature_checksum_per_rank": checksums},
+        **({"cpu_baseline": cpu} if cpu else {}),
     }
+
+
+def chain_cpu_baseline(model, budget_s: float) -> dict:
+    """The same chained forward on the host cores: the C oracle's threaded int8 conv plus its
+    requant / residual / pool restatements, on a bounded sample of images."""
+    from my_own_cnn_b200 import nets, synth
+    from oracle import oracle
+
+    threads = oracle.cpu_threads()
+
+    def forward(img0: int, nimg: int):
+        bufs = {0: synth.s8_table_host(SEED, 1, nets.act_table(), img0 * 224 * 224 * 3,
+                                       nimg * 224 * 224 * 3).reshape(nimg, 224, 224, 3)}
+        for op in model.plan:
+            src = bufs[op.src]
+            if op.kind == "conv":
+                sp = model.specs[op.layer]
+                w, b, s = (t.cpu().numpy() for t in model.weights[op.layer])
+                a = oracle.conv_args(nimg, sp.h, sp.w, sp.c, sp.r, sp.r, sp.k, sp.pad, sp.pad, sp.stride, sp.stride,
+                                     groups=sp.groups)
+                acc = oracle.conv_s8(a, src, w, threads=threads)
+                lo, hi = (-128, 127) if sp.linear else ((0, nets.Q6) if sp.relu6 else (0, 127))
+                bufs[op.dst] = (oracle.requant_res_s8(acc, b, s, bufs[op.res], nets.RES_SCALE, 0, lo, hi)
+                                if op.res >= 0 else oracle.requant_s8(acc, b, s, 0, lo, hi))
+            elif op.kind == "maxpool":
+                bufs[op.dst] = oracle.maxpool_s8(src, 3, 3, 2, 2, 1, 1)
+            else:
+                bufs[op.dst] = oracle.global_avgpool_s8(src)
+
+    t0 = time.perf_counter()
+    forward(0, 1)
+    t_one = time.perf_counter() - t0
+    images = int(max(1, min(64, budget_s / max(t_one, 1e-3))))
+    t0 = time.perf_counter()
+    forward(0, images)
+    dt = time.perf_counter() - t0
+    return {"value": round(images / dt, 3), "unit": "images/s", "cores": threads, "kind": "port",
+            "sample": f"{images} images through the whole chained {model.name} forward; C oracle conv "
+                      f"(threaded over output pixels) + requant / residual / pool restatements",
+            "seconds": round(dt, 2)}
 
 
 def run_bmm(args, rank: int, world: int, local_rank: int) -> dict | None:
