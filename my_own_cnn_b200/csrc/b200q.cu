@@ -252,6 +252,12 @@ const bool g_dw_px = [] {
   return !(v && v[0] == '0');
 }();
 
+// Word-wise pack switch (env B200Q_PACK_WORDS=0 keeps the byte-wise pack, for A/B timing).
+const bool g_pack_words = [] {
+  const char* v = getenv("B200Q_PACK_WORDS");
+  return !(v && v[0] == '0');
+}();
+
 const int g_nacc_max = [] {
   const char* v = getenv("B200Q_NACC_MAX");
   const int n = v ? atoi(v) : 8;
@@ -434,13 +440,21 @@ int run_packed_conv(const DeviceState& st, const int8_t* x, const int8_t* w, voi
   const int kp = (rsc + 31) / 32 * 32;
   int8_t* a_buf = scratch;
   int8_t* w_buf = scratch + round256(static_cast<size_t>(rows) * kp);
-  int tile_rows = 16384 / kp;
-  if (tile_rows > 64) tile_rows = 64;
-  if (tile_rows < 1) tile_rows = 1;
-  const long long blocks_needed = (rows + tile_rows - 1) / tile_rows;
-  const int pack_grid = static_cast<int>(blocks_needed < st.sms * 16ll ? blocks_needed : st.sms * 16ll);
-  im2col_pack_s8_kernel<<<pack_grid, 256, static_cast<size_t>(tile_rows) * kp, stream>>>(x, a_buf, g, kp, rows,
-                                                                                        tile_rows);
+  // Short packed rows (kp <= 64: 1x1 convs with C % 16 != 0, the 3x3 C = 3 stem) pack faster one
+  // thread per row; long rows (the 7x7 stem, kp = 160) faster through the shared-memory tile.
+  if (g_pack_words && g.dil_w == 1 && kp <= 64) {
+    const size_t x_bytes = static_cast<size_t>(g.n) * g.h * g.w * g.c;
+    im2col_pack_words_kernel<<<grid_for(static_cast<size_t>(rows), 256, st.sms), 256, 0, stream>>>(x, a_buf, g, kp,
+                                                                                                  rows, x_bytes);
+  } else {
+    int tile_rows = 16384 / kp;
+    if (tile_rows > 64) tile_rows = 64;
+    if (tile_rows < 1) tile_rows = 1;
+    const long long blocks_needed = (rows + tile_rows - 1) / tile_rows;
+    const int pack_grid = static_cast<int>(blocks_needed < st.sms * 16ll ? blocks_needed : st.sms * 16ll);
+    im2col_pack_s8_kernel<<<pack_grid, 256, static_cast<size_t>(tile_rows) * kp, stream>>>(x, a_buf, g, kp, rows,
+                                                                                          tile_rows);
+  }
   int rc = check_launch("im2col_pack_s8_kernel launch");
   if (rc) return rc;
   weight_pad_s8_kernel<<<grid_for(static_cast<size_t>(g.k) * kp, 256, st.sms), 256, 0, stream>>>(w, w_buf, g.k, rsc,

@@ -505,6 +505,72 @@ __global__ void global_avgpool_s8_kernel(const int8_t* __restrict__ x, int8_t* _
   }
 }
 
+// Packed rows word by word (dilation 1, short rows): row m's packed bytes are R segments of L = S*C contiguous
+// input bytes (filter row rr starts at input (hi0 + rr, wi0)), written back to back and followed by
+// zeros up to kp.  One thread per row; each output word is two aligned input words and a funnel
+// shift when its 4 bytes lie in one segment, bytes otherwise (the few words that straddle two
+// segments, and rows whose window leaves the image).  16-byte stores of 4 assembled words.
+__global__ void __launch_bounds__(256) im2col_pack_words_kernel(const int8_t* __restrict__ x,
+                                                                int8_t* __restrict__ a, ConvGeom g, int kp,
+                                                                long long total_rows, size_t x_bytes) {
+  // Aligned word pairs are read only where both words lie inside x.
+  const uintptr_t x_end = reinterpret_cast<uintptr_t>(x) + x_bytes;
+  const int L = g.s * g.c;
+  const int rsc = g.r * L;
+  for (long long m = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; m < total_rows;
+       m += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int wo = static_cast<int>(m % g.wo);
+    const long long t = m / g.wo;
+    const int ho = static_cast<int>(t % g.ho);
+    const int n = static_cast<int>(t / g.ho);
+    const int hi0 = ho * g.stride_h - g.pad_h, wi0 = wo * g.stride_w - g.pad_w;
+    const bool inside = hi0 >= 0 && hi0 + g.r <= g.h && wi0 >= 0 && wi0 + g.s <= g.w;
+    const int8_t* img = x + static_cast<size_t>(n) * g.h * g.w * g.c;
+    uint4* out = reinterpret_cast<uint4*>(a + m * kp);
+    int rr = 0, off = 0;  // segment and offset of output byte 4q
+    for (int v = 0; v < kp / 16; ++v) {
+      uint32_t wd[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int j = (v * 4 + q) * 4;
+        uint32_t word = 0;
+        const uintptr_t src =
+            reinterpret_cast<uintptr_t>(img + (static_cast<size_t>(hi0 + rr) * g.w + wi0) * g.c + off);
+        if (j + 4 <= rsc && off + 4 <= L && inside && (src & ~uintptr_t(3)) + 8 <= x_end) {
+          const uint32_t* w0 = reinterpret_cast<const uint32_t*>(src & ~uintptr_t(3));
+          const uint32_t sh = static_cast<uint32_t>(src & 3) * 8;
+          const uint32_t lo = __ldg(w0);
+          const uint32_t hi = sh ? __ldg(w0 + 1) : 0u;
+          word = __funnelshift_r(lo, hi, sh);
+        } else {
+          int r2 = rr, o2 = off;
+#pragma unroll
+          for (int b = 0; b < 4; ++b) {
+            if (j + b < rsc) {
+              const int ss = o2 / g.c, c = o2 - ss * g.c;
+              const int hi = hi0 + r2, wi = wi0 + ss;
+              if (hi >= 0 && hi < g.h && wi >= 0 && wi < g.w)
+                word |= static_cast<uint32_t>(static_cast<uint8_t>(img[(static_cast<size_t>(hi) * g.w + wi) * g.c + c]))
+                        << (8 * b);
+            }
+            if (++o2 == L) {
+              o2 = 0;
+              ++r2;
+            }
+          }
+        }
+        wd[q] = word;
+        off += 4;
+        while (off >= L) {
+          off -= L;
+          ++rr;
+        }
+      }
+      out[v] = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+    }
+  }
+}
+
 // Weights [k][R*S*C] -> [k][kp] with zero columns past R*S*C.
 __global__ void weight_pad_s8_kernel(const int8_t* __restrict__ w, int8_t* __restrict__ wp, int k, int rsc, int kp) {
   const size_t total = static_cast<size_t>(k) * kp;
