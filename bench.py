@@ -238,7 +238,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
                 "path": f"my_own_cnn_b200.stack.ConvStack.run_host (C ABI b200q_conv2d_s8), pinned host buffers, {args.chunk}-image chunks, H2D/compute/D2H overlapped"},
         "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(int8_peak_tops, 1),
                      "unit": "TOP/s", "frac": round(achieved / int8_peak_tops, 4), "traffic": traffic,
-                     "kernel": "tc_gemm_s8_kernel",
+                     "kernel": "tc_gemm_s8_kernel (layer 1) + tc_gemm_s8_pair_kernel (layer 2)",
                      "peak_source": f"2 x bf16_tflops ({peaks['source']}) = dense int8 peak"},
         "gpu_launches": int(launches),
         "clocks": clocks,
