@@ -113,3 +113,45 @@ def test_product_package_does_not_import_oracle():
     for f in (ROOT / "my_own_cnn_b200").rglob("*"):
         if f.suffix in (".py", ".cu", ".cuh", ".cpp", ".h") and f.name != "build.py":
             assert not pat.search(f.read_text()), f
+
+
+@pytest.mark.parametrize("net,convs,residuals", [("resnet50", 53, 16), ("mobilenetv2", 52, 10)])
+def test_chained_network_plans(net, convs, residuals):
+    """The chained forward uses every conv of the layer table once, feeds each conv a buffer of its
+    input shape, and adds a shortcut of the conv's output shape (host logic only)."""
+    from my_own_cnn_b200 import nets
+
+    specs = nets.NETS[net]()
+    plan = nets.chain_plan(net)
+    assert sorted(op.layer for op in plan if op.kind == "conv") == list(range(convs))
+    assert sum(op.res >= 0 for op in plan) == residuals
+    assert plan[-1].kind == "avgpool"
+    shapes = {0: (224, 224, 3)}
+    for op in plan:
+        h, w, c = shapes[op.src]
+        if op.kind == "conv":
+            sp = specs[op.layer]
+            assert (h, w, c) == (sp.h, sp.w, sp.c), sp.name
+            ho, wo = sp.out_hw()
+            shapes[op.dst] = (ho, wo, sp.k)
+            if op.res >= 0:
+                assert shapes[op.res] == shapes[op.dst], sp.name
+        elif op.kind == "maxpool":
+            shapes[op.dst] = ((h + 2 - 3) // 2 + 1, (w + 2 - 3) // 2 + 1, c)
+        else:
+            shapes[op.dst] = (1, 1, c)
+    assert shapes[plan[-1].dst] == (1, 1, 2048 if net == "resnet50" else 1280)
+
+
+def test_new_entry_points_validate_arguments():
+    """Pool and residual entry points reject bad shapes with a status, before touching a GPU."""
+    L = _lib.lib()
+    assert L.b200q_maxpool_s8(None, None, 1, 8, 8, 16, 3, 3, 0, 2, 1, 1, None) == 1
+    assert b"stride" in L.b200q_last_error()
+    assert L.b200q_maxpool_s8(None, None, 1, 2, 2, 16, 5, 5, 1, 1, 4, 4, None) == 1
+    assert L.b200q_global_avgpool_s8(None, None, 1, 0, 8, 16, None) == 1
+    cp = _lib.CConvParams(0, 0, 1, 1, 1, 1, 1)
+    ce = _lib.CEpilogue(1, 0, -128, 127)
+    assert L.b200q_conv2d_s8_add(None, None, None, None, None, 1.0, None, 1, 8, 8, 16, 1, 1, 16,
+                                 ctypes.byref(cp), ctypes.byref(ce), None) == 1
+    assert b"residual" in L.b200q_last_error()
