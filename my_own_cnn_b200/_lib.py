@@ -31,6 +31,7 @@ PATH_NAMES = {
     6: "cuda-core-bmm-i32",
     7: "tcgen05-packed",
     8: "tcgen05-tiled-2sm",
+    9: "tcgen05-rowtile",
 }
 
 

@@ -201,6 +201,20 @@ int encode_out_1b(CUtensorMap* map, void* base, uint64_t n, uint64_t m, uint64_t
   return B200Q_OK;
 }
 
+// Row-tile window map over x [N][H][W][C]: dims {16 B, W, H, C/16, N}, box {16, P, T + 3, C/16, 1},
+// no swizzle: one box lands as [C/16][T+3 rows][P columns][16 B].
+int encode_rowtile(CUtensorMap* map, const int8_t* x, const ConvGeom& g, int P, int T) {
+  cuuint64_t dims[5] = {16, (cuuint64_t)g.w, (cuuint64_t)g.h, (cuuint64_t)(g.c / 16), (cuuint64_t)g.n};
+  cuuint64_t strides[4] = {(cuuint64_t)g.c, (cuuint64_t)g.c * g.w, 16, (cuuint64_t)g.c * g.w * g.h};
+  cuuint32_t box[5] = {16, (cuuint32_t)P, (cuuint32_t)(T + 3), (cuuint32_t)(g.c / 16), 1};
+  cuuint32_t es[5] = {1, 1, 1, 1, 1};
+  CUresult r = g_encode_tiled(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 5, const_cast<int8_t*>(x), dims, strides, box, es,
+                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(B200Q_ERR_CUDA, "cuTensorMapEncodeTiled (row-tile window) failed (%d)", (int)r);
+  return B200Q_OK;
+}
+
 int encode_im2col(CUtensorMap* map, const int8_t* x, const ConvGeom& g, int bk) {
   cuuint64_t dims[4] = {(cuuint64_t)g.c, (cuuint64_t)g.w, (cuuint64_t)g.h, (cuuint64_t)g.n};
   cuuint64_t strides[3] = {(cuuint64_t)g.c, (cuuint64_t)g.c * g.w, (cuuint64_t)g.c * g.w * g.h};
@@ -258,6 +272,12 @@ const bool g_pack_words = [] {
   return !(v && v[0] == '0');
 }();
 
+// Row-tile switch (env B200Q_ROWTILE=0 keeps 3x3 convs on the im2col mode, for A/B timing).
+const bool g_rowtile = [] {
+  const char* v = getenv("B200Q_ROWTILE");
+  return !(v && v[0] == '0');
+}();
+
 const int g_nacc_max = [] {
   const char* v = getenv("B200Q_NACC_MAX");
   const int n = v ? atoi(v) : 8;
@@ -281,7 +301,7 @@ int launch_tc(const DeviceState& st, const CUtensorMap& ma, const CUtensorMap& m
   // 4-byte outputs go through shared memory and TMA stores when the row pitch allows a tensor map.
   CUtensorMap mc = ma;  // unused placeholder when tma_store == 0
   a.tma_store = 0;
-  if (a.epi.out_kind != kOutS8 && a.ldc == a.N && a.N % 4 == 0 && aligned16(a.out)) {
+  if (a.mode != 2 && a.epi.out_kind != kOutS8 && a.ldc == a.N && a.N % 4 == 0 && aligned16(a.out)) {
     const uint64_t rows = a.batch_stride ? static_cast<uint64_t>(a.M) : static_cast<uint64_t>(a.M);
     int rc = encode_out_4b(&mc, a.out, static_cast<uint64_t>(a.N), rows, static_cast<uint64_t>(a.batch));
     if (rc) return rc;
@@ -291,9 +311,10 @@ int launch_tc(const DeviceState& st, const CUtensorMap& ma, const CUtensorMap& m
   // Resident B for a single N tile whose K blocks fit in 64 KiB (narrow layers, 3x3 convs with
   // few output channels): the weights are loaded once per CTA instead of once per 128-row tile.
   const long long b_all = static_cast<long long>(a.num_kb) * a.BN * a.BK;
-  a.b_res = !a.pair && g_b_resident && a.n_tiles == 1 && !a.b_batched && a.b_major == 0 && b_all <= 64 * 1024;
+  a.b_res = a.mode == 2 || (!a.pair && g_b_resident && a.n_tiles == 1 && !a.b_batched && a.b_major == 0 &&
+                            b_all <= 64 * 1024);
   const int b_rows = a.pair ? a.BN / 2 : a.BN;  // B rows per stage held by this CTA
-  const int stage_bytes = kTcBM * a.BK + (a.b_res ? 0 : b_rows * a.BK);
+  const int stage_bytes = (a.mode == 2 ? a.rt_stage : kTcBM * a.BK) + (a.b_res ? 0 : b_rows * a.BK);
   // Stage per-column bias / scale in shared memory when they fit (4096 columns = 32 KiB).
   a.stage_cols = (a.epi.out_kind != kOutS32 || a.epi.bias) && a.N <= 4096 ? (a.N + 31) / 32 * 32 : 0;
   a.default_clamp = a.epi.out_kind == kOutS8 && a.epi.zp == 0 && a.epi.lo == -128 && a.epi.hi == 127;
@@ -301,7 +322,8 @@ int launch_tc(const DeviceState& st, const CUtensorMap& ma, const CUtensorMap& m
   // its bias / scale (staged columns are zero-padded to a multiple of 32).  GEMMs with a reduction
   // shorter than 128 keep direct stores: there the epilogue alone sets the pace and the staging
   // round trip measured slower.
-  if (a.epi.out_kind == kOutS8 && g_s8_tma_store && a.num_kb * a.BK >= 128 && a.ldc == a.N && a.N % 16 == 0 &&
+  if (a.mode != 2 && a.epi.out_kind == kOutS8 && g_s8_tma_store && a.num_kb * a.BK >= 128 && a.ldc == a.N &&
+      a.N % 16 == 0 &&
       aligned16(a.out) &&
       (a.stage_cols > 0 || a.N % 32 == 0) && a.vec_ok) {
     const uint64_t rows = static_cast<uint64_t>(a.M);
@@ -317,7 +339,7 @@ int launch_tc(const DeviceState& st, const CUtensorMap& ma, const CUtensorMap& m
   if (stages < 2) return fail(B200Q_ERR_UNSUPPORTED, "tile does not fit shared memory");
   a.stages = stages;
   const int tile_m = a.pair ? 2 * kTcBM : kTcBM;
-  a.m_tiles = (a.M + tile_m - 1) / tile_m;
+  a.m_tiles = a.mode == 2 ? a.n_img * ((a.Ho + a.rt_T - 1) / a.rt_T) : (a.M + tile_m - 1) / tile_m;
   const long long total = static_cast<long long>(a.batch) * a.m_tiles * a.n_tiles;
   if (total > 0x7FFFFFFFll) return fail(B200Q_ERR_UNSUPPORTED, "too many tiles");
   a.total_tiles = static_cast<int>(total);
@@ -610,6 +632,46 @@ static int conv2d_s8_impl(const int8_t* d_x, const int8_t* d_w, const int32_t* d
   // at least 128 KiB (a driver limitation on small im2col maps).
   const bool tc_ok = g_policy.load() == 0 && g.groups == 1 && c % 16 == 0 && vec_ptrs &&
                      M < (1ll << 31) && (is_1x1_plain || (corners_ok && x_bytes >= (128u << 10)));
+  // Row tiles for 3x3 / stride 1 / pad 1 convs whose weights stay resident: one window load per
+  // tile serves all nine taps (the im2col mode loads the window nine times, one row per pixel).
+  const int rt_P = g.wo + 1;
+  const int rt_bn = pick_bn(k, 0);
+  const bool rowtile_ok = g_rowtile && g_policy.load() == 0 && g.groups == 1 && r == 3 && s == 3 &&
+                          g.stride_h == 1 && g.stride_w == 1 && g.pad_h == 1 && g.pad_w == 1 && g.dil_h == 1 &&
+                          g.dil_w == 1 && (c == 32 || c == 64 || c == 128) && k <= 256 && rt_P <= 128 &&
+                          9ll * c * rt_bn <= 72 * 1024 && vec_ptrs && M < (1ll << 31);
+  if (rowtile_ok) {
+    TcArgs a{};
+    a.mode = 2;
+    a.BK = c;
+    a.cchunks = 1;
+    a.num_kb = 9;
+    a.BN = rt_bn;
+    a.M = static_cast<int>(M);
+    a.N = k;
+    a.batch = 1;
+    a.epi = e;
+    a.out = d_y;
+    a.ldc = k;
+    a.vec_ok = k % 16 == 0;
+    a.Ho = g.ho; a.Wo = g.wo; a.S = 3;
+    a.n_img = n;
+    a.rt_P = rt_P;
+    a.rt_T = 128 / rt_P;
+    // T + 3 window rows: the right-border tap of the last output row reads index (T + 2) * P, the
+    // zero column of one more row (without it that read would reach the next channel plane).
+    a.rt_plane = (a.rt_T + 3) * rt_P * 16;
+    a.rt_box = a.rt_plane * (c / 16);
+    // tap offsets read up to 2P + 2 pixels past a tile's 128 rows: slack after the last plane
+    a.rt_stage = (a.rt_box + (2 * rt_P + 2 + 128) * 16 + 1023) / 1024 * 1024;
+    CUtensorMap ma, mb;
+    rc = encode_tiled_3d(&mb, d_w, static_cast<uint64_t>(9 * c), static_cast<uint64_t>(k), 1, a.BK, a.BN, a.BK);
+    if (rc) return rc;
+    rc = encode_rowtile(&ma, d_x, g, a.rt_P, a.rt_T);
+    if (rc) return rc;
+    g_last_path = 9;
+    return launch_tc(*st, ma, mb, a, cs);
+  }
   if (tc_ok) {
     TcArgs a{};
     // K block per stage: the largest of 128/64/32 bytes whose channel padding (zero-filled by TMA

@@ -52,6 +52,14 @@ struct TcArgs {
   int tma_store;      // outputs leave through shared memory + TMA tensor stores (map tmC)
   int b_res;          // B resident: all num_kb K blocks of the single N tile loaded once per CTA
   int pair;           // 2-SM tiles (tc_gemm_s8_pair_kernel): 256-row tiles, B box of BN / 2 rows
+  // mode 2 (row tiles, 3x3 stride-1 convs): a tile is rt_T output rows of one image at row pitch
+  // rt_P = Wo + 1; its input window (rt_T + 3 rows x rt_P columns x C, column 0 the zero padding)
+  // arrives as one TMA box laid out [C / 16][pixel][16 B] (plane stride rt_plane bytes) and serves
+  // all nine taps.
+  int rt_P, rt_T, rt_plane;
+  int rt_box;    // bytes of one window box (rt_plane * C / 16)
+  int n_img;     // images (row tiles enumerate image x block of output rows)
+  int rt_stage;  // ring stage size for row tiles (window + read-past slack, 1024-aligned)
 };
 
 constexpr int kTcMaxAcc = 8;
@@ -317,8 +325,20 @@ __device__ __forceinline__ void epilogue_role_t(const TcArgs& a, const CUtensorM
     const int rem = tile - b * tiles_per_batch;
     const int mt = rem / a.n_tiles;
     const int nt = rem - mt * a.n_tiles;
-    const int m = mt * TM + row;
+    int m = mt * TM + row;
     const int n0 = nt * a.BN;
+    size_t rt_off = 0;
+    if (!PAIR && a.mode == 2) {
+      // Row tile: TMEM row -> (tile row i, column wo) at pitch P; pitch padding and rows past the
+      // tile or the image are not stored.
+      const int rblocks = (a.Ho + a.rt_T - 1) / a.rt_T;
+      const int img = mt / rblocks;
+      const int ho0 = (mt - img * rblocks) * a.rt_T;
+      const int i = row / a.rt_P, wo = row - i * a.rt_P;
+      const bool valid = i < a.rt_T && ho0 + i < a.Ho && wo < a.Wo;
+      m = valid ? 0 : a.M;
+      rt_off = (static_cast<size_t>(img * a.Ho + ho0 + i) * a.Wo + wo) * a.ldc;
+    }
     // Chunks holding columns < N; the two warps of a lane quarter swap parities every tile, so an
     // odd chunk count (N <= 32, N = 96, ...) is shared evenly over two tiles.
     const int nvalid = (min(a.BN, a.N - n0) + 31) >> 5;
@@ -326,7 +346,8 @@ __device__ __forceinline__ void epilogue_role_t(const TcArgs& a, const CUtensorM
     if (!mbar_wait_bounded(accf0 + 8 * buf, acc_ph, a.wait_limit, a.err, kDevErrTimeoutEpilogue)) break;
     tc_fence_after();
     const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(buf * a.BN);
-    const size_t row_off = static_cast<size_t>(b) * a.batch_stride + static_cast<size_t>(m) * a.ldc;
+    const size_t row_off =
+        (!PAIR && a.mode == 2) ? rt_off : static_cast<size_t>(b) * a.batch_stride + static_cast<size_t>(m) * a.ldc;
     uint32_t va[32], vb[32];
     if (nmine > 0) tmem_ld_32x32b_x32(tbase + sel * 32, va);
     tmem_ld_wait();
@@ -434,7 +455,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   // 1024-byte alignment by pointer arithmetic on the shared window (an integer round trip would
   // turn every later access through these pointers into a generic load / store).
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
-  const uint32_t stage_a = kTcBM * a.BK;
+  const uint32_t stage_a = a.mode == 2 ? static_cast<uint32_t>(a.rt_stage) : kTcBM * a.BK;
   const uint32_t stage_b = a.BN * a.BK;
   // Ring of stages: A (+ B unless B is resident).  A resident B holds num_kb blocks after the ring.
   uint8_t* sA = smem;
@@ -493,7 +514,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       uint32_t issued_mask = 0;  // stages that received a load
       uint32_t last_ph = 0;      // parity of the last load into each stage (bit per stage)
       bool ok = true;
-      const uint32_t tx = a.b_res ? stage_a : stage_a + stage_b;
+      const uint32_t tx = a.mode == 2 ? static_cast<uint32_t>(a.rt_box) : (a.b_res ? stage_a : stage_a + stage_b);
       // One B block (K block kb of N tile n0, batch bb) into shared memory at dB.
       auto load_b = [&](uint32_t dB, uint32_t bar, int kb, int n0, int bb) {
         if (a.conv_b) {
@@ -512,7 +533,27 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         mbar_arrive_expect_tx(b_full, a.num_kb * stage_b);
         for (int kb = 0; kb < a.num_kb; ++kb) load_b(smem_u32(sB + kb * stage_b), b_full, kb, 0, 0);
       }
-      for (int tile = blockIdx.x; tile < a.total_tiles && ok; tile += gridDim.x) {
+      for (int tile = blockIdx.x; tile < a.total_tiles && ok && a.mode == 2; tile += gridDim.x) {
+        // Row tiles: one window load per tile (all taps, all channels); tiles enumerate
+        // (image, block of rt_T output rows).
+        const int rblocks = (a.Ho + a.rt_T - 1) / a.rt_T;
+        const int img = tile / rblocks;
+        const int ho0 = (tile - img * rblocks) * a.rt_T;
+        if (!mbar_wait_bounded(empty0 + 8 * stage, ph ^ 1u, a.wait_limit, a.err, kDevErrTimeoutProducer)) {
+          ok = false;
+          break;
+        }
+        const uint32_t fb = full0 + 8 * stage;
+        mbar_arrive_expect_tx(fb, tx);
+        tma_load_5d(smem_u32(sA + stage * stage_a), &tmA, fb, 0, -1, ho0 - 1, 0, img);
+        issued_mask |= 1u << stage;
+        last_ph = (last_ph & ~(1u << stage)) | (ph << stage);
+        if (++stage == a.stages) {
+          stage = 0;
+          ph ^= 1u;
+        }
+      }
+      for (int tile = blockIdx.x; tile < a.total_tiles && ok && a.mode != 2; tile += gridDim.x) {
         const int b = tile / tiles_per_batch;
         const int rem = tile - b * tiles_per_batch;
         const int mt = rem / a.n_tiles;
@@ -590,7 +631,45 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const uint64_t b_desc0 = make_smem_desc(smem_u32(sB), b_lbo, b_sbo, b_layout);
       if (a.b_res && blockIdx.x < a.total_tiles)
         ok = __all_sync(0xFFFFFFFFu, mbar_wait_bounded(b_full, 0, a.wait_limit, a.err, kDevErrTimeoutMma));
-      for (int tile = blockIdx.x; tile < a.total_tiles && ok; tile += gridDim.x) {
+      // Row tiles: A in the no-swizzle K-major layout [C/16][pixel][16 B] (SBO = 8 pixels, LBO =
+      // one channel-chunk plane); tap (r, s) is the same window started (r * P + s) pixels later.
+      const uint64_t rt_desc0 = make_smem_desc(smem_u32(sA), static_cast<uint32_t>(a.rt_plane), 128u, 0u);
+      for (int tile = blockIdx.x; tile < a.total_tiles && ok && a.mode == 2; tile += gridDim.x) {
+        if (!__all_sync(0xFFFFFFFFu,
+                        mbar_wait_bounded(acce0 + 8 * buf, acc_ph ^ 1u, a.wait_limit, a.err, kDevErrTimeoutMma))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * a.BN);
+        if (!__all_sync(0xFFFFFFFFu, mbar_wait_bounded(full0 + 8 * stage, ph, a.wait_limit, a.err, kDevErrTimeoutMma))) {
+          ok = false;
+          break;
+        }
+        const uint64_t ad_s = rt_desc0 + ((stage * stage_a) >> 4);
+        for (int kb = 0; kb < a.num_kb; ++kb) {
+          const int tap = kb / a.cchunks;
+          const int cc = kb - tap * a.cchunks;
+          const int r = tap / 3, s = tap - r * 3;
+          const uint64_t ad_t = ad_s + static_cast<uint64_t>(r * a.rt_P + s) +
+                                ((static_cast<uint32_t>(cc * (a.BK / 16)) * static_cast<uint32_t>(a.rt_plane)) >> 4);
+          const uint64_t bd_s = b_desc0 + ((kb * stage_b) >> 4);
+          for (int j = 0; j < ksteps; ++j)
+            tc_mma_i8_elect(d_tmem, ad_t + ((2u * j * static_cast<uint32_t>(a.rt_plane)) >> 4),
+                            bd_s + ((j * b_step) >> 4), a.idesc, (kb | j) != 0 ? 1u : 0u);
+        }
+        tc_commit_elect(empty0 + 8 * stage);
+        if (++stage == a.stages) {
+          stage = 0;
+          ph ^= 1u;
+        }
+        tc_commit_elect(accf0 + 8 * buf);
+        if (++buf == a.nacc) {
+          buf = 0;
+          acc_ph ^= 1u;
+        }
+      }
+      for (int tile = blockIdx.x; tile < a.total_tiles && ok && a.mode != 2; tile += gridDim.x) {
         if (!__all_sync(0xFFFFFFFFu,
                         mbar_wait_bounded(acce0 + 8 * buf, acc_ph ^ 1u, a.wait_limit, a.err, kDevErrTimeoutMma))) {
           ok = false;

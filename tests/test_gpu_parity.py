@@ -127,8 +127,7 @@ def _conv_case(n, h, w, c, r, s, k, p, seed, epi_kind="all", groups=1):
 
 @pytest.mark.parametrize("shape", [
     # n, h, w, c, r, s, k, pad, stride, dil
-    (1, 56, 56, 64, 3, 3, 64, 1, 1, 1),    # BASELINE config 1
-    (2, 28, 28, 128, 3, 3, 128, 1, 1, 1),  # ResNet stage-2 3x3
+    (2, 28, 28, 128, 3, 3, 128, 1, 1, 1),  # ResNet stage-2 3x3 (weights too large for row tiles)
     (2, 34, 34, 64, 3, 3, 80, 1, 2, 1),    # stride 2, K edge (80 = 64 + 16)
     (1, 40, 36, 96, 3, 3, 48, 2, 1, 2),    # dilation 2, BK 32 chunks
     (2, 24, 24, 256, 1, 1, 272, 0, 2, 1),  # 1x1 stride 2 (projection shortcut) through im2col
@@ -170,7 +169,7 @@ def test_conv_s8_tcgen05_pointwise(cuda_lib, shape):
     ((2, 23, 23, 3, 7, 7, 64, 3, 2, 1), 1, "cuda-core-generic"),      # stem C = 3
     ((1, 12, 12, 24, 1, 1, 40, 0, 1, 1), 1, "cuda-core-generic"),     # C % 32 != 0
     ((2, 9, 9, 32, 3, 3, 64, 1, 1, 1), 2, "cuda-core-generic"),       # grouped
-    ((1, 6, 6, 64, 3, 3, 64, 1, 1, 1), 1, "cuda-core-generic"),       # tiny tensor (36 output rows)
+    ((1, 6, 6, 48, 3, 3, 64, 1, 1, 1), 1, "cuda-core-generic"),       # tiny tensor (36 output rows)
     ((2, 14, 14, 256, 3, 3, 256, 1, 1, 1), 1, "tcgen05-packed"),      # < 128 KiB: packed, not im2col
 ])
 def test_conv_s8_cuda_core_paths(cuda_lib, shape, groups, expect):
@@ -195,13 +194,32 @@ def test_conv_s8_packed_low_channel(cuda_lib, shape):
     assert paths == {"tcgen05-packed"}, paths
 
 
+@pytest.mark.parametrize("shape", [
+    # n, h, w, c, r, s, k, pad, stride, dil
+    (1, 56, 56, 64, 3, 3, 64, 1, 1, 1),    # BASELINE config 1
+    (4, 56, 56, 64, 3, 3, 64, 1, 1, 1),    # ResNet-50 stage-1 3x3 (2 output rows per tile)
+    (2, 13, 11, 64, 3, 3, 48, 1, 1, 1),    # ragged: H not a multiple of the tile rows, N = 48
+    (3, 9, 127, 32, 3, 3, 32, 1, 1, 1),    # widest row (W + 1 = 128: one output row per tile)
+    (2, 14, 14, 128, 3, 3, 64, 1, 1, 1),   # C = 128 (8 channel chunks per window)
+    (2, 7, 5, 64, 3, 3, 40, 1, 1, 1),      # N = 40 (scalar tail), tiny image
+    (1, 6, 6, 64, 3, 3, 64, 1, 1, 1),      # 36 output pixels: one tile, 6 rows
+])
+def test_conv_s8_tcgen05_rowtile(cuda_lib, shape):
+    """3x3 stride-1 convs on row tiles (one window load per tile for all nine taps)."""
+    b2q = _b2q()
+    n, h, w, c, r, s, k, pad, st, dil = shape
+    p = b2q.Conv2DParams(pad, pad, st, st, dil, dil, 1)
+    paths = _conv_case(n, h, w, c, r, s, k, p, seed=sum(shape))
+    assert paths == {"tcgen05-rowtile"}, paths
+
+
 def test_conv_forced_cuda_core_matches_tcgen05(cuda_lib):
     b2q = _b2q()
     x = torch.from_numpy(rng_s8(5, (2, 32, 32, 64))).cuda()
     w = torch.from_numpy(rng_s8(6, (64, 3, 3, 64))).cuda()
     p = b2q.Conv2DParams()
     y_tc = b2q.conv2d_s8(x, w, None, None, p, b2q.Epilogue.int32())
-    assert b2q.last_path() == "tcgen05-im2col"
+    assert b2q.last_path() == "tcgen05-rowtile"
     b2q.set_path_policy(1)
     try:
         y_cc = b2q.conv2d_s8(x, w, None, None, p, b2q.Epilogue.int32())
@@ -223,7 +241,7 @@ def test_conv_output_guard_band(cuda_lib):
     buf = torch.full((numel + 4096,), 0x5A, dtype=torch.int8, device="cuda")
     b2q.conv2d_s8_into(buf, x, wt, None, scale, n, h, w, c, 3, 3, k, b2q.Conv2DParams(), b2q.Epilogue.int8())
     torch.cuda.synchronize()
-    assert b2q.last_path() == "tcgen05-im2col"
+    assert b2q.last_path() == "tcgen05-rowtile"
     assert torch.all(buf[numel:] == 0x5A)
 
 
