@@ -23,6 +23,7 @@ from __future__ import annotations
 import argparse
 import json
 import os
+import re
 import statistics
 import subprocess
 import sys
@@ -358,6 +359,10 @@ def run_net(args, rank: int, world: int, local_rank: int) -> dict | None:
     dev = torch.device("cuda", local_rank)
     stream = torch.cuda.current_stream()
     specs = nets.NETS[args.config]()
+    if args.layers:
+        specs = [sp for sp in specs if re.fullmatch(args.layers, sp.name)]
+        if not specs:
+            raise SystemExit(f"--layers {args.layers!r} matches no layer of {args.config}")
     batch = args.batch or NET_BATCH[args.config]
     data = nets.NetData(specs, batch, SEED, dev, image_offset=rank)
     flush = torch.empty(256 << 20, dtype=torch.int8, device=dev)
@@ -423,7 +428,8 @@ def run_net(args, rank: int, world: int, local_rank: int) -> dict | None:
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_ms, 4), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "s8xs8->s32",
         "data": "synthetic (seeded splitmix64; half-normal / normal int8 codes via quantile tables)",
-        "config": {"workload": f"{args.config} conv stack, per-GPU batch {batch}, every conv on fresh input",
+        "config": {"workload": f"{args.config} conv stack, per-GPU batch {batch}, every conv on fresh input"
+                   + (f", layers matching {args.layers!r} only" if args.layers else ""),
                    "global_batch": batch * world, "per_gpu_batch": batch, "parallelism": f"dp{world} (batch shards)",
                    "l2": "flushed between timed steps (256 MiB write outside the events)"},
         "tops_per_gpu": round(sum(ops) / (step_ms * 1e-3) / 1e12, 1),
@@ -620,6 +626,8 @@ def main():
                     choices=["pointwise", "resnet50", "mobilenetv2", "resnet50-chain", "mobilenetv2-chain", "bmm"],
                     help="pointwise (BASELINE config 4, the default bench line); the others report configs 3 / 5 / 2")
     ap.add_argument("--batch", type=int, default=0, help="per-GPU batch for the network configs (0 = BASELINE)")
+    ap.add_argument("--layers", default="", help="regex on layer names: run only those layers of resnet50 / "
+                    "mobilenetv2 (profiling a single layer; the default runs the whole table)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -448,6 +448,52 @@ __device__ __forceinline__ void run_epilogue(const TcArgs& a, const CUtensorMap*
   }
 }
 
+// MMA issue of row tiles (mode 2): per tile, 9 taps x KS K-slices of 32 bytes, fully unrolled.
+// The operand descriptors are the stage base plus compile-time or per-CTA offsets, so the issuing
+// warp spends a few instructions per tcgen05.mma: runtime divisions and 64-bit products in this
+// loop cost more than a 64-column MMA itself (~48 SM cycles).  Returns false after a timed-out
+// wait (the error flag is already set).
+template <int KS>
+__device__ __forceinline__ bool rowtile_mma_loop(const TcArgs& a, uint32_t tmem_base, uint64_t rt_desc0,
+                                                 uint64_t b_desc0, uint32_t stage_a, uint32_t stage_b,
+                                                 uint32_t pl2, uint32_t full0, uint32_t empty0, uint32_t accf0,
+                                                 uint32_t acce0) {
+  const uint32_t P = static_cast<uint32_t>(a.rt_P);
+  const uint32_t bstep = stage_b >> 4;
+  const uint32_t idesc = a.idesc;
+  int stage = 0, buf = 0;
+  uint32_t ph = 0, acc_ph = 0;
+  for (int tile = blockIdx.x; tile < a.total_tiles; tile += gridDim.x) {
+    if (!__all_sync(0xFFFFFFFFu, mbar_wait_bounded(acce0 + 8 * buf, acc_ph ^ 1u, a.wait_limit, a.err,
+                                                   kDevErrTimeoutMma)))
+      return false;
+    tc_fence_after();
+    const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * a.BN);
+    if (!__all_sync(0xFFFFFFFFu, mbar_wait_bounded(full0 + 8 * stage, ph, a.wait_limit, a.err, kDevErrTimeoutMma)))
+      return false;
+    const uint64_t ad_s = rt_desc0 + ((stage * stage_a) >> 4);
+#pragma unroll
+    for (int tap = 0; tap < 9; ++tap) {
+      const uint64_t at = ad_s + static_cast<uint64_t>((tap / 3) * P + (tap % 3));
+#pragma unroll
+      for (int j = 0; j < KS; ++j)
+        tc_mma_i8_elect(d_tmem, at + static_cast<uint64_t>(j * pl2),
+                        b_desc0 + static_cast<uint64_t>(tap * bstep + j * 2), idesc, (tap | j) != 0 ? 1u : 0u);
+    }
+    tc_commit_elect(empty0 + 8 * stage);
+    if (++stage == a.stages) {
+      stage = 0;
+      ph ^= 1u;
+    }
+    tc_commit_elect(accf0 + 8 * buf);
+    if (++buf == a.nacc) {
+      buf = 0;
+      acc_ph ^= 1u;
+    }
+  }
+  return true;
+}
+
 __global__ void __launch_bounds__(kTcThreads, 1)
     tc_gemm_s8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                       const __grid_constant__ CUtensorMap tmC, const TcArgs a) {
@@ -634,39 +680,18 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       // Row tiles: A in the no-swizzle K-major layout [C/16][pixel][16 B] (SBO = 8 pixels, LBO =
       // one channel-chunk plane); tap (r, s) is the same window started (r * P + s) pixels later.
       const uint64_t rt_desc0 = make_smem_desc(smem_u32(sA), static_cast<uint32_t>(a.rt_plane), 128u, 0u);
-      for (int tile = blockIdx.x; tile < a.total_tiles && ok && a.mode == 2; tile += gridDim.x) {
-        if (!__all_sync(0xFFFFFFFFu,
-                        mbar_wait_bounded(acce0 + 8 * buf, acc_ph ^ 1u, a.wait_limit, a.err, kDevErrTimeoutMma))) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * a.BN);
-        if (!__all_sync(0xFFFFFFFFu, mbar_wait_bounded(full0 + 8 * stage, ph, a.wait_limit, a.err, kDevErrTimeoutMma))) {
-          ok = false;
-          break;
-        }
-        const uint64_t ad_s = rt_desc0 + ((stage * stage_a) >> 4);
-        for (int kb = 0; kb < a.num_kb; ++kb) {
-          const int tap = kb / a.cchunks;
-          const int cc = kb - tap * a.cchunks;
-          const int r = tap / 3, s = tap - r * 3;
-          const uint64_t ad_t = ad_s + static_cast<uint64_t>(r * a.rt_P + s) +
-                                ((static_cast<uint32_t>(cc * (a.BK / 16)) * static_cast<uint32_t>(a.rt_plane)) >> 4);
-          const uint64_t bd_s = b_desc0 + ((kb * stage_b) >> 4);
-          for (int j = 0; j < ksteps; ++j)
-            tc_mma_i8_elect(d_tmem, ad_t + ((2u * j * static_cast<uint32_t>(a.rt_plane)) >> 4),
-                            bd_s + ((j * b_step) >> 4), a.idesc, (kb | j) != 0 ? 1u : 0u);
-        }
-        tc_commit_elect(empty0 + 8 * stage);
-        if (++stage == a.stages) {
-          stage = 0;
-          ph ^= 1u;
-        }
-        tc_commit_elect(accf0 + 8 * buf);
-        if (++buf == a.nacc) {
-          buf = 0;
-          acc_ph ^= 1u;
+      if (ok && a.mode == 2) {
+        const uint32_t pl2 = static_cast<uint32_t>(a.rt_plane) >> 3;  // two channel-chunk planes
+        switch (a.BK) {
+          case 32:
+            ok = rowtile_mma_loop<1>(a, tmem_base, rt_desc0, b_desc0, stage_a, stage_b, pl2, full0, empty0, accf0, acce0);
+            break;
+          case 64:
+            ok = rowtile_mma_loop<2>(a, tmem_base, rt_desc0, b_desc0, stage_a, stage_b, pl2, full0, empty0, accf0, acce0);
+            break;
+          default:
+            ok = rowtile_mma_loop<4>(a, tmem_base, rt_desc0, b_desc0, stage_a, stage_b, pl2, full0, empty0, accf0, acce0);
+            break;
         }
       }
       for (int tile = blockIdx.x; tile < a.total_tiles && ok && a.mode != 2; tile += gridDim.x) {
