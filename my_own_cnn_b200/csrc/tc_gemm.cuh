@@ -494,6 +494,55 @@ __device__ __forceinline__ bool rowtile_mma_loop(const TcArgs& a, uint32_t tmem_
   return true;
 }
 
+// MMA issue of the tiled / im2col modes: per K block (one ring stage) KS K-slices of 32 bytes,
+// unrolled, with the stage offsets advanced by adds instead of products.  BRES: the weights are
+// resident (K block kb of B at kb * stage_b) rather than in the ring.
+template <int KS, bool BRES>
+__device__ __forceinline__ bool gemm_mma_loop(const TcArgs& a, uint32_t tmem_base, uint64_t a_desc0, uint64_t b_desc0,
+                                              uint32_t sa16, uint32_t sb16, uint32_t as16, uint32_t bs16,
+                                              uint32_t full0, uint32_t empty0, uint32_t accf0, uint32_t acce0) {
+  const uint32_t idesc = a.idesc;
+  const int num_kb = a.num_kb, stages = a.stages;
+  int stage = 0, buf = 0;
+  uint32_t ph = 0, acc_ph = 0, a_off = 0, b_off = 0;
+  for (int tile = blockIdx.x; tile < a.total_tiles; tile += gridDim.x) {
+    if (!__all_sync(0xFFFFFFFFu, mbar_wait_bounded(acce0 + 8 * buf, acc_ph ^ 1u, a.wait_limit, a.err,
+                                                   kDevErrTimeoutMma)))
+      return false;
+    tc_fence_after();
+    const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * a.BN);
+    uint32_t bres_off = 0;
+    for (int kb = 0; kb < num_kb; ++kb) {
+      // The TMA completion on the mbarrier orders the tiles for the tensor core; a tcgen05
+      // fence per stage is not needed.
+      if (!__all_sync(0xFFFFFFFFu, mbar_wait_bounded(full0 + 8 * stage, ph, a.wait_limit, a.err, kDevErrTimeoutMma)))
+        return false;
+      const uint64_t ad = a_desc0 + a_off;
+      const uint64_t bd = b_desc0 + (BRES ? bres_off : b_off);
+#pragma unroll
+      for (int j = 0; j < KS; ++j)
+        tc_mma_i8_elect(d_tmem, ad + static_cast<uint64_t>(j * as16), bd + static_cast<uint64_t>(j * bs16), idesc,
+                        (kb != 0 || j != 0) ? 1u : 0u);
+      tc_commit_elect(empty0 + 8 * stage);
+      bres_off += sb16;
+      a_off += sa16;
+      b_off += sb16;
+      if (++stage == stages) {
+        stage = 0;
+        ph ^= 1u;
+        a_off = 0;
+        b_off = 0;
+      }
+    }
+    tc_commit_elect(accf0 + 8 * buf);
+    if (++buf == a.nacc) {
+      buf = 0;
+      acc_ph ^= 1u;
+    }
+  }
+  return true;
+}
+
 __global__ void __launch_bounds__(kTcThreads, 1)
     tc_gemm_s8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                       const __grid_constant__ CUtensorMap tmC, const TcArgs a) {
@@ -657,10 +706,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     {
       // ----------------------------------------------------------------- MMA
       // The whole warp runs the loop converged; an elected lane issues each tcgen05 instruction.
-      int stage = 0;
-      uint32_t ph = 0;
-      int buf = 0;
-      uint32_t acc_ph = 0;
       bool ok = true;
       const uint32_t a_layout = a.a_major == 0 ? kmajor_layout(a.BK) : 2u;
       const uint32_t b_layout = a.b_major == 0 ? kmajor_layout(a.BK) : 2u;
@@ -694,39 +739,20 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             break;
         }
       }
-      for (int tile = blockIdx.x; tile < a.total_tiles && ok && a.mode != 2; tile += gridDim.x) {
-        if (!__all_sync(0xFFFFFFFFu,
-                        mbar_wait_bounded(acce0 + 8 * buf, acc_ph ^ 1u, a.wait_limit, a.err, kDevErrTimeoutMma))) {
-          ok = false;
-          break;
+      if (ok && a.mode != 2) {
+        const uint32_t sa16 = stage_a >> 4, sb16 = stage_b >> 4, as16 = a_step >> 4, bs16 = b_step >> 4;
+#define B200Q_GEMM_MMA(KS, BRES)                                                                              \
+  ok = gemm_mma_loop<KS, BRES>(a, tmem_base, a_desc0, b_desc0, sa16, sb16, as16, bs16, full0, empty0, accf0, acce0)
+        if (a.b_res) {
+          if (ksteps == 4) B200Q_GEMM_MMA(4, true);
+          else if (ksteps == 2) B200Q_GEMM_MMA(2, true);
+          else B200Q_GEMM_MMA(1, true);
+        } else {
+          if (ksteps == 4) B200Q_GEMM_MMA(4, false);
+          else if (ksteps == 2) B200Q_GEMM_MMA(2, false);
+          else B200Q_GEMM_MMA(1, false);
         }
-        tc_fence_after();
-        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * a.BN);
-        for (int kb = 0; kb < a.num_kb; ++kb) {
-          // The TMA completion on the mbarrier orders the tiles for the tensor core; a tcgen05
-          // fence per stage is not needed.
-          if (!__all_sync(0xFFFFFFFFu,
-                          mbar_wait_bounded(full0 + 8 * stage, ph, a.wait_limit, a.err, kDevErrTimeoutMma))) {
-            ok = false;
-            break;
-          }
-          const uint64_t ad_s = a_desc0 + ((stage * stage_a) >> 4);
-          const uint64_t bd_s = b_desc0 + (((a.b_res ? kb : stage) * stage_b) >> 4);
-          for (int j = 0; j < ksteps; ++j)
-            tc_mma_i8_elect(d_tmem, ad_s + ((j * a_step) >> 4), bd_s + ((j * b_step) >> 4), a.idesc,
-                            (kb | j) != 0 ? 1u : 0u);
-          tc_commit_elect(empty0 + 8 * stage);
-          if (++stage == a.stages) {
-            stage = 0;
-            ph ^= 1u;
-          }
-        }
-        if (!ok) break;
-        tc_commit_elect(accf0 + 8 * buf);
-        if (++buf == a.nacc) {
-          buf = 0;
-          acc_ph ^= 1u;
-        }
+#undef B200Q_GEMM_MMA
       }
       // Wait for every MMA issued by this warp before TMEM is released.
       tc_commit_elect(drain);
