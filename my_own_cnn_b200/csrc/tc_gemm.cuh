@@ -87,9 +87,30 @@ __device__ __forceinline__ uint32_t pack4_sat_s8(int a, int b, int c, int d) {
   return out;
 }
 
+// Four requantized int8 codes packed in a word: clamp(rint_sat(f), lo - zp, hi - zp) + zp.
+// CL selects how the clamp is done: 0 in integers (any bounds and zero point); 1 by the
+// saturating pack alone (the default range [-128, 127], zero point 0); 2 in floats before the
+// conversion (zero point 0 and lo = 0, the ReLU / ReLU6 forms: max(NaN, 0) = 0 matches
+// rint_sat(NaN) = 0, and integer bounds commute with rounding), the upper bound 127 by the pack.
+template <int CL>
+__device__ __forceinline__ uint32_t quant4_s8(const Epilogue& e, float f0, float f1, float f2, float f3) {
+  if constexpr (CL == 2) {
+    const float hi = static_cast<float>(e.hi);
+    f0 = fminf(fmaxf(f0, 0.0f), hi); f1 = fminf(fmaxf(f1, 0.0f), hi);
+    f2 = fminf(fmaxf(f2, 0.0f), hi); f3 = fminf(fmaxf(f3, 0.0f), hi);
+  }
+  int r0 = __float2int_rn(f0), r1 = __float2int_rn(f1), r2 = __float2int_rn(f2), r3 = __float2int_rn(f3);
+  if constexpr (CL == 0) {
+    const int lo = e.lo - e.zp, hi = e.hi - e.zp;
+    r0 = min(max(r0, lo), hi) + e.zp; r1 = min(max(r1, lo), hi) + e.zp;
+    r2 = min(max(r2, lo), hi) + e.zp; r3 = min(max(r3, lo), hi) + e.zp;
+  }
+  return pack4_sat_s8(r0, r1, r2, r3);
+}
+
 // Vector form of the fused epilogue: the first 4 * NQ columns of the chunk (NQ = 8: all 32,
 // NQ = 4: the first 16), 16-byte bias / scale reads and 16-byte stores.
-template <int KIND, bool DCL, int NQ, bool RES>
+template <int KIND, int CL, int NQ, bool RES>
 __device__ __forceinline__ void store_vec(const TcArgs& a, const uint32_t (&v)[32], size_t off, int n,
                                           const int32_t* bias, const float* scale, bool has_bias) {
   const Epilogue& e = a.epi;
@@ -129,13 +150,7 @@ __device__ __forceinline__ void store_vec(const TcArgs& a, const uint32_t (&v)[3
           f2 = __fadd_rn(f2, __fmul_rn(__int2float_rn(sbyte(rw[q], 2)), e.res_scale));
           f3 = __fadd_rn(f3, __fmul_rn(__int2float_rn(sbyte(rw[q], 3)), e.res_scale));
         }
-        int r0 = __float2int_rn(f0), r1 = __float2int_rn(f1), r2 = __float2int_rn(f2), r3 = __float2int_rn(f3);
-        if constexpr (!DCL) {
-          const int lo = e.lo - e.zp, hi = e.hi - e.zp;
-          r0 = min(max(r0, lo), hi) + e.zp; r1 = min(max(r1, lo), hi) + e.zp;
-          r2 = min(max(r2, lo), hi) + e.zp; r3 = min(max(r3, lo), hi) + e.zp;
-        }
-        packed[q] = pack4_sat_s8(r0, r1, r2, r3);
+        packed[q] = quant4_s8<CL>(e, f0, f1, f2, f3);
       }
     }
   }
@@ -149,17 +164,17 @@ __device__ __forceinline__ void store_vec(const TcArgs& a, const uint32_t (&v)[3
 // Fused epilogue for one row and 32 consecutive output columns [n, n + valid).
 // bias / scale point at shared memory (staged) or global memory; bias may be null.
 // All array indices are compile-time constants after unrolling: nothing spills to local memory.
-template <int KIND, bool DCL, bool RES>
+template <int KIND, int CL, bool RES>
 __device__ __forceinline__ void store_chunk(const TcArgs& a, const uint32_t (&v)[32], size_t off, int n, int valid,
                                             const int32_t* bias, const float* scale, bool has_bias) {
   const Epilogue& e = a.epi;
   if (a.vec_ok) {
     if (valid == 32) {
-      store_vec<KIND, DCL, 8, RES>(a, v, off, n, bias, scale, has_bias);
+      store_vec<KIND, CL, 8, RES>(a, v, off, n, bias, scale, has_bias);
       return;
     }
     if (valid == 16) {  // the 16-column tail of N = 16, 48, 80, ...
-      store_vec<KIND, DCL, 4, RES>(a, v, off, n, bias, scale, has_bias);
+      store_vec<KIND, CL, 4, RES>(a, v, off, n, bias, scale, has_bias);
       return;
     }
   }
@@ -219,7 +234,7 @@ __device__ __forceinline__ void stage_chunk_4b(const TcArgs& a, const uint32_t (
 // 32B-swizzled 1 KiB buffer (16-byte half h of row r at half h ^ ((r / 4) % 2), the layout of a
 // SWIZZLE_32B tensor map: conflict-free for one 16-byte store per lane) and leave with one TMA
 // store, which clips rows >= M and columns >= N.  The requantization is the one of store_chunk.
-template <bool DCL, bool RES>
+template <int CL, bool RES>
 __device__ __forceinline__ void stage_chunk_s8(const TcArgs& a, const uint32_t (&v)[32], int n, int lane,
                                                uint8_t* sbuf, const int32_t* bias, const float* scale,
                                                bool has_bias, const int8_t* rrow) {
@@ -256,13 +271,7 @@ __device__ __forceinline__ void stage_chunk_s8(const TcArgs& a, const uint32_t (
       f2 = __fadd_rn(f2, __fmul_rn(__int2float_rn(sbyte(rw[q], 2)), e.res_scale));
       f3 = __fadd_rn(f3, __fmul_rn(__int2float_rn(sbyte(rw[q], 3)), e.res_scale));
     }
-    int r0 = __float2int_rn(f0), r1 = __float2int_rn(f1), r2 = __float2int_rn(f2), r3 = __float2int_rn(f3);
-    if constexpr (!DCL) {
-      const int lo = e.lo - e.zp, hi = e.hi - e.zp;
-      r0 = min(max(r0, lo), hi) + e.zp; r1 = min(max(r1, lo), hi) + e.zp;
-      r2 = min(max(r2, lo), hi) + e.zp; r3 = min(max(r3, lo), hi) + e.zp;
-    }
-    packed[q] = pack4_sat_s8(r0, r1, r2, r3);
+    packed[q] = quant4_s8<CL>(e, f0, f1, f2, f3);
   }
   const int sw = (lane >> 2) & 1;
   *reinterpret_cast<uint4*>(sbuf + lane * 32 + (sw << 4)) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
@@ -272,9 +281,10 @@ __device__ __forceinline__ void stage_chunk_s8(const TcArgs& a, const uint32_t (
 
 // Epilogue role: 8 warps; warp w reads TMEM lanes 32*(w%4)..+31 (the hardware restricts a warp
 // to the lane quarter w%4) and, in the j-th tile of its CTA, the chunks of 32 columns with
-// chunk % 2 == ((w-2)/4 + j) % 2.  The TMEM load of the next chunk is issued before the current
-// chunk is processed (two register buffers).
-template <int KIND, bool TMA, bool DCL, bool RES>
+// chunk % 2 == ((w-2)/4 + j) % 2.  Each chunk is loaded and processed in turn: overlapping the
+// next chunk's TMEM load with two register buffers measured slower (the extra register moves
+// cost more issue slots than the load latency it hid).
+template <int KIND, bool TMA, int CL, bool RES>
 __device__ __forceinline__ void emit_chunk(const TcArgs& a, const CUtensorMap* tmC, const uint32_t (&v)[32], int b,
                                            int m, int mrow0, size_t row_off, int n, int lane, uint8_t* sbufs,
                                            int& sb, const int32_t* bias, const float* scale,
@@ -285,7 +295,7 @@ __device__ __forceinline__ void emit_chunk(const TcArgs& a, const CUtensorMap* t
     if (lane == 0) bulk_wait_group_read<1>();  // the store that used this buffer has read it
     __syncwarp();
     if constexpr (KIND == kOutS8)
-      stage_chunk_s8<DCL, RES>(a, v, n, lane, buf, bias, scale, has_bias,
+      stage_chunk_s8<CL, RES>(a, v, n, lane, buf, bias, scale, has_bias,
                                RES && m < a.M ? a.epi.res + row_off + n : nullptr);
     else
       stage_chunk_4b<KIND>(a, v, n, lane, buf, bias, scale, has_bias);
@@ -298,12 +308,12 @@ __device__ __forceinline__ void emit_chunk(const TcArgs& a, const CUtensorMap* t
     sb ^= 1;
     return;
   }
-  if (m < a.M) store_chunk<KIND, DCL, RES>(a, v, row_off + n, n, min(32, a.N - n), bias, scale, has_bias);
+  if (m < a.M) store_chunk<KIND, CL, RES>(a, v, row_off + n, n, min(32, a.N - n), bias, scale, has_bias);
 }
 
 // PAIR: the CTA is one half of a 2-SM pair (tiles of 2 x 128 rows; this CTA's TMEM holds rows
 // rank * 128 .. + 127 of each tile; the accumulator-empty barrier lives in the leader CTA).
-template <int KIND, bool TMA, bool DCL, bool PAIR, bool RES>
+template <int KIND, bool TMA, int CL, bool PAIR, bool RES>
 __device__ __forceinline__ void epilogue_role_t(const TcArgs& a, const CUtensorMap* tmC, uint32_t tmem_base,
                                               uint32_t accf0, uint32_t acce0, int warp, int lane,
                                               const int32_t* bias, const float* scale, bool has_bias,
@@ -348,22 +358,14 @@ __device__ __forceinline__ void epilogue_role_t(const TcArgs& a, const CUtensorM
     const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(buf * a.BN);
     const size_t row_off =
         (!PAIR && a.mode == 2) ? rt_off : static_cast<size_t>(b) * a.batch_stride + static_cast<size_t>(m) * a.ldc;
-    uint32_t va[32], vb[32];
-    if (nmine > 0) tmem_ld_32x32b_x32(tbase + sel * 32, va);
-    tmem_ld_wait();
-    for (int i = 0; i < nmine; i += 2) {
-      const int ca = sel + 2 * i, cb = ca + 2;
-      if (i + 1 < nmine) tmem_ld_32x32b_x32(tbase + cb * 32, vb);
-      const int mrow0 = mt * TM + rank * kTcBM + q * 32;
-      emit_chunk<KIND, TMA, DCL, RES>(a, tmC, va, b, m, mrow0, row_off, n0 + ca * 32, lane, sbufs, sb, bias, scale,
-                                 has_bias);
+    const int mrow0 = mt * TM + rank * kTcBM + q * 32;
+    for (int i = 0; i < nmine; ++i) {
+      uint32_t va[32];
+      const int ca = sel + 2 * i;
+      tmem_ld_32x32b_x32(tbase + ca * 32, va);
       tmem_ld_wait();
-      if (i + 1 < nmine) {
-        if (i + 2 < nmine) tmem_ld_32x32b_x32(tbase + (cb + 2) * 32, va);
-        emit_chunk<KIND, TMA, DCL, RES>(a, tmC, vb, b, m, mrow0, row_off, n0 + cb * 32, lane, sbufs, sb, bias, scale,
-                                   has_bias);
-        tmem_ld_wait();
-      }
+      emit_chunk<KIND, TMA, CL, RES>(a, tmC, va, b, m, mrow0, row_off, n0 + ca * 32, lane, sbufs, sb, bias, scale,
+                                 has_bias);
     }
     tc_fence_before();
     __syncwarp();
@@ -386,31 +388,39 @@ __device__ __forceinline__ void epilogue_role(const TcArgs& a, const CUtensorMap
                                               uint32_t accf0, uint32_t acce0, int warp, int lane,
                                               const int32_t* bias, const float* scale, bool has_bias,
                                               uint8_t* sbufs) {
-  // The default int8 range [-128, 127] with zero point 0 is clamped by the saturating pack alone;
-  // compiling it as its own variant keeps the per-element branch out of the unrolled loop.  A fused
-  // residual add (int8 outputs only) is a variant of its own too.
-  if (KIND == kOutS8 && a.epi.res) {
+  // int8 outputs: one compiled variant per clamp form (quant4_s8's CL: the per-element branch
+  // stays out of the unrolled loop) and per fused residual add.
+#define B200Q_EPI(TMA, CL, RES)                                                                                \
+  epilogue_role_t<KIND, TMA, CL, PAIR, RES>(a, tmC, tmem_base, accf0, acce0, warp, lane, bias, scale, has_bias, \
+                                            sbufs)
+#define B200Q_EPI_CL(TMA, RES)     \
+  if (cl == 1)                     \
+    B200Q_EPI(TMA, 1, RES);        \
+  else if (cl == 2)                \
+    B200Q_EPI(TMA, 2, RES);        \
+  else                             \
+    B200Q_EPI(TMA, 0, RES)
+  if constexpr (KIND != kOutS8) {
     if (a.tma_store)
-      epilogue_role_t<KIND, true, false, PAIR, true>(a, tmC, tmem_base, accf0, acce0, warp, lane, bias, scale,
-                                                     has_bias, sbufs);
+      B200Q_EPI(true, 0, false);
     else
-      epilogue_role_t<KIND, false, false, PAIR, true>(a, tmC, tmem_base, accf0, acce0, warp, lane, bias, scale,
-                                                      has_bias, sbufs);
-  } else if (KIND == kOutS8 && a.default_clamp) {
-    if (a.tma_store)
-      epilogue_role_t<KIND, true, true, PAIR, false>(a, tmC, tmem_base, accf0, acce0, warp, lane, bias, scale,
-                                                     has_bias, sbufs);
-    else
-      epilogue_role_t<KIND, false, true, PAIR, false>(a, tmC, tmem_base, accf0, acce0, warp, lane, bias, scale,
-                                                      has_bias, sbufs);
+      B200Q_EPI(false, 0, false);
   } else {
-    if (a.tma_store)
-      epilogue_role_t<KIND, true, false, PAIR, false>(a, tmC, tmem_base, accf0, acce0, warp, lane, bias, scale,
-                                                      has_bias, sbufs);
-    else
-      epilogue_role_t<KIND, false, false, PAIR, false>(a, tmC, tmem_base, accf0, acce0, warp, lane, bias, scale,
-                                                       has_bias, sbufs);
+    const int cl = a.default_clamp ? 1 : (a.epi.zp == 0 && a.epi.lo == 0) ? 2 : 0;
+    if (a.epi.res) {
+      if (a.tma_store) {
+        B200Q_EPI_CL(true, true);
+      } else {
+        B200Q_EPI_CL(false, true);
+      }
+    } else if (a.tma_store) {
+      B200Q_EPI_CL(true, false);
+    } else {
+      B200Q_EPI_CL(false, false);
+    }
   }
+#undef B200Q_EPI_CL
+#undef B200Q_EPI
 }
 
 // Epilogue warps: stage bias / scale in shared memory when they fit, then drain the accumulators.

@@ -133,3 +133,45 @@ def test_resnet_bottleneck_block_chained_on_device(cuda_lib):
     a3 = oracle.requant_res_s8(oracle.conv_s8(oracle.conv_args(n, hw, hw, width, 1, 1, cin, 0, 0), a2, ws[2], 4),
                                bs[2], ss[2], x, RES_SCALE, 0, 0, 127)
     np.testing.assert_array_equal(y3.cpu().numpy(), a3)
+
+
+@pytest.mark.parametrize("shape,expect", [
+    ((8, 28, 28, 64, 1, 1, 256, 0, 1), "tcgen05-tiled"),      # direct 16-byte stores
+    ((4, 14, 14, 256, 1, 1, 512, 0, 1), "tcgen05-tiled"),     # TMA-store epilogue
+    ((4, 28, 28, 64, 3, 3, 64, 1, 1), "tcgen05-rowtile"),
+    ((3, 7, 9, 32, 1, 1, 48, 0, 1), "tcgen05-tiled"),         # 16-column tail
+])
+@pytest.mark.parametrize("with_res", [False, True])
+def test_clamp_forms_with_special_scales(cuda_lib, shape, expect, with_res):
+    """Every clamp form of the int8 epilogue (default range, ReLU / ReLU6 clamped in floats before
+    the conversion, general bounds with a zero point) against the oracle, with per-column scales
+    that include NaN, +-inf, zero, negative and huge values and large biases: NaN products must
+    become 0 before the clamp, infinities saturate."""
+    b2q = _b2q()
+    n, h, w, c, r, s, k, pad, st = shape
+    p = b2q.Conv2DParams(pad, pad, st, st, 1, 1, 1)
+    seed = 900 + sum(shape)
+    x, wt = rng_s8(seed, (n, h, w, c)), rng_s8(seed + 1, (k, r, s, c))
+    rng = np.random.default_rng(seed + 2)
+    bias = rng.integers(-2**31, 2**31, size=k, dtype=np.int64).astype(np.int32)
+    bias[: k // 2] = rng.integers(-2**12, 2**12, size=k // 2)
+    scale = rng.uniform(-2e-3, 2e-3, size=k).astype(np.float32)
+    special = np.array([np.nan, np.inf, -np.inf, 0.0, -0.0, 3e38, -3e38, 1e-30, 0.5, -7.0], dtype=np.float32)
+    scale[: len(special)] = special
+    ho, wo = b2q.conv_out_shape(h, w, c, r, s, k, p)
+    res = rng_s8(seed + 3, (n, ho, wo, k), -128, 127)
+    acc = oracle.conv_s8(oracle.conv_args(n, h, w, c, r, s, k, pad, pad, st, st), x, wt, threads=4)
+    d = lambda a: torch.from_numpy(a).cuda()
+    forms = [(b2q.Epilogue.int8(), 0, -128, 127), (b2q.Epilogue.int8(relu=True), 0, 0, 127),
+             (b2q.Epilogue.int8(relu6_q=96), 0, 0, 96), (b2q.Epilogue.int8(relu=True, zp_out=-5), -5, -5, 127),
+             (b2q.Epilogue(1, 3, -100, 90), 3, -100, 90)]
+    for epi, zp, lo, hi in forms:
+        if with_res:
+            y = b2q.conv2d_s8_add(d(x), d(wt), d(bias), d(scale), d(res), RES_SCALE, p, epi)
+            want = oracle.requant_res_s8(acc, bias, scale, res, RES_SCALE, zp, lo, hi)
+        else:
+            y = b2q.conv2d_s8(d(x), d(wt), d(bias), d(scale), p, epi)
+            want = oracle.requant_s8(acc, bias, scale, zp, lo, hi)
+        torch.cuda.synchronize()
+        assert b2q.last_path() == expect
+        np.testing.assert_array_equal(y.cpu().numpy(), want, err_msg=f"zp={zp} lo={lo} hi={hi}")
