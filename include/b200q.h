@@ -173,7 +173,9 @@ int b200q_device_error(void);
  * 5 CUDA-core quantized-int32 (drop-in), 6 CUDA-core int32 bmm, 7 tcgen05 GEMM over an im2col matrix
  * packed into the stream's workspace (low channel counts), 8 tcgen05 tiled GEMM on 2-SM pairs
  * (256-row tiles, one M = 256 MMA per K slice across a cluster of two CTAs), 9 tcgen05 row-tile
- * 3x3 conv (one input-window load per tile serves all nine taps). */
+ * 3x3 conv (one input-window load per tile serves all nine taps), 10 tcgen05 row tiles over a
+ * space-to-depth copy of a stride-2 low-channel input (network stems; the input and weights are
+ * rearranged into the stream's workspace). */
 int b200q_last_path(void);
 
 /* 0 = automatic dispatch (default); 1 = force the CUDA-core kernels (cross-checks). */

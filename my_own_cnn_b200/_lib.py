@@ -32,6 +32,7 @@ PATH_NAMES = {
     7: "tcgen05-packed",
     8: "tcgen05-tiled-2sm",
     9: "tcgen05-rowtile",
+    10: "tcgen05-s2d",
 }
 
 

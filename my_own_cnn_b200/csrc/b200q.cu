@@ -203,15 +203,33 @@ int encode_out_1b(CUtensorMap* map, void* base, uint64_t n, uint64_t m, uint64_t
 
 // Row-tile window map over x [N][H][W][C]: dims {16 B, W, H, C/16, N}, box {16, P, T + 3, C/16, 1},
 // no swizzle: one box lands as [C/16][T+3 rows][P columns][16 B].
-int encode_rowtile(CUtensorMap* map, const int8_t* x, const ConvGeom& g, int P, int T) {
-  cuuint64_t dims[5] = {16, (cuuint64_t)g.w, (cuuint64_t)g.h, (cuuint64_t)(g.c / 16), (cuuint64_t)g.n};
-  cuuint64_t strides[4] = {(cuuint64_t)g.c, (cuuint64_t)g.c * g.w, 16, (cuuint64_t)g.c * g.w * g.h};
-  cuuint32_t box[5] = {16, (cuuint32_t)P, (cuuint32_t)(T + 3), (cuuint32_t)(g.c / 16), 1};
+// Row-tile window map of an NHWC int8 tensor: dims {16 B, w, h, c / 16, n}, box of `rows` rows x
+// P pixels x all channel planes, no swizzle (shared layout [c / 16][row * P + pixel][16 B]).
+int encode_rowtile(CUtensorMap* map, const int8_t* x, int n, int h, int w, int c, int P, int rows) {
+  cuuint64_t dims[5] = {16, (cuuint64_t)w, (cuuint64_t)h, (cuuint64_t)(c / 16), (cuuint64_t)n};
+  cuuint64_t strides[4] = {(cuuint64_t)c, (cuuint64_t)c * w, 16, (cuuint64_t)c * w * h};
+  cuuint32_t box[5] = {16, (cuuint32_t)P, (cuuint32_t)rows, (cuuint32_t)(c / 16), 1};
   cuuint32_t es[5] = {1, 1, 1, 1, 1};
   CUresult r = g_encode_tiled(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 5, const_cast<int8_t*>(x), dims, strides, box, es,
                               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(B200Q_ERR_CUDA, "cuTensorMapEncodeTiled (row-tile window) failed (%d)", (int)r);
+  return B200Q_OK;
+}
+
+// Row-tile window map of a 16-channel NHWC int8 tensor read in 8-byte elements: dims
+// {2 * w, h, n}, box {2 * P, rows, 1}, so each box row is P whole pixels (16 * P contiguous
+// bytes) and a window takes `rows` TMA rows instead of rows * P 16-byte ones.  Shared layout
+// [row * P + pixel][16 B], the same as encode_rowtile's for one channel plane.
+int encode_rowtile_wide(CUtensorMap* map, const int8_t* x, int n, int h, int w, int P, int rows) {
+  cuuint64_t dims[3] = {(cuuint64_t)(2 * w), (cuuint64_t)h, (cuuint64_t)n};
+  cuuint64_t strides[2] = {(cuuint64_t)w * 16, (cuuint64_t)w * h * 16};
+  cuuint32_t box[3] = {(cuuint32_t)(2 * P), (cuuint32_t)rows, 1};
+  cuuint32_t es[3] = {1, 1, 1};
+  CUresult r = g_encode_tiled(map, CU_TENSOR_MAP_DATA_TYPE_UINT64, 3, const_cast<int8_t*>(x), dims, strides, box, es,
+                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(B200Q_ERR_CUDA, "cuTensorMapEncodeTiled (wide row-tile window) failed (%d)", (int)r);
   return B200Q_OK;
 }
 
@@ -275,6 +293,13 @@ const bool g_pack_words = [] {
 // Row-tile switch (env B200Q_ROWTILE=0 keeps 3x3 convs on the im2col mode, for A/B timing).
 const bool g_rowtile = [] {
   const char* v = getenv("B200Q_ROWTILE");
+  return !(v && v[0] == '0');
+}();
+
+// Space-to-depth stem switch (env B200Q_S2D=0 keeps low-channel stride-2 convs on the packed
+// path, for A/B timing).
+const bool g_s2d = [] {
+  const char* v = getenv("B200Q_S2D");
   return !(v && v[0] == '0');
 }();
 
@@ -632,6 +657,79 @@ static int conv2d_s8_impl(const int8_t* d_x, const int8_t* d_w, const int32_t* d
   // at least 128 KiB (a driver limitation on small im2col maps).
   const bool tc_ok = g_policy.load() == 0 && g.groups == 1 && c % 16 == 0 && vec_ptrs &&
                      M < (1ll << 31) && (is_1x1_plain || (corners_ok && x_bytes >= (128u << 10)));
+  // Space-to-depth row tiles for stride-2 convs of 1-4 channels (network stems): the input is
+  // rearranged into 16-channel pixels of 2x2 blocks, the weights into an R2 x S2 stride-1 filter
+  // (S2 even: each K = 32 MMA slice covers two taps), and the conv runs as row tiles over it.
+  // Replaces the im2col pack of the low-channel path: the rearranged input is 16/(4C) times the
+  // input instead of R*S*C/C times.
+  if (g_s2d && g_policy.load() == 0 && g.groups == 1 && g.stride_h == 2 && g.stride_w == 2 && g.dil_h == 1 &&
+      g.dil_w == 1 && c >= 1 && c <= 4 && k <= 256 && M >= 1024 && M < (1ll << 31) && aligned16(d_y) &&
+      (!d_bias || aligned16(d_bias)) && (!d_scale || aligned16(d_scale)) && (!d_res || aligned16(d_res))) {
+    auto fdiv2 = [](int v) { return v >= 0 ? v / 2 : -((1 - v) / 2); };
+    const int yoff = -((g.pad_h + 1) / 2), xoff = -((g.pad_w + 1) / 2);
+    const int r2 = fdiv2(r - 1 - g.pad_h) - yoff + 1;
+    const int s2 = (fdiv2(s - 1 - g.pad_w) - xoff + 1 + 1) / 2 * 2;
+    const int P = g.wo + s2 - 1;
+    const int bn = pick_bn(k, 0);
+    if (r2 >= 2 && r2 <= 4 && (s2 == 2 || s2 == 4) && P <= 128 && g.ho > 0 && g.wo > 0) {
+      const int h2 = (h + 1) / 2, w2 = (w + 1) / 2;
+      const size_t xs_bytes = (static_cast<size_t>(n) * h2 * w2 * 16 + 1023) / 1024 * 1024;
+      const size_t ws_bytes = static_cast<size_t>(k) * r2 * s2 * 16;
+      void* ws = nullptr;
+      rc = get_workspace(xs_bytes + ws_bytes, cs, &ws);
+      if (rc) return rc;
+      int8_t* xs = static_cast<int8_t*>(ws);
+      int8_t* wsd = xs + xs_bytes;
+      const size_t px = static_cast<size_t>(n) * h2 * w2;
+      const int grid = grid_for(px, 256, st->sms);
+      if (c == 1) s2d_s8_kernel<1><<<grid, 256, 0, cs>>>(d_x, xs, n, h, w, h2, w2);
+      else if (c == 2) s2d_s8_kernel<2><<<grid, 256, 0, cs>>>(d_x, xs, n, h, w, h2, w2);
+      else if (c == 3) s2d_s8_kernel<3><<<grid, 256, 0, cs>>>(d_x, xs, n, h, w, h2, w2);
+      else s2d_s8_kernel<4><<<grid, 256, 0, cs>>>(d_x, xs, n, h, w, h2, w2);
+      rc = check_launch("s2d_s8_kernel launch");
+      if (rc) return rc;
+      s2d_weight_s8_kernel<<<grid_for(ws_bytes, 256, st->sms), 256, 0, cs>>>(d_w, wsd, k, r, s, c, r2, s2, g.pad_h,
+                                                                             g.pad_w);
+      rc = check_launch("s2d_weight_s8_kernel launch");
+      if (rc) return rc;
+      TcArgs a{};
+      a.mode = 2;
+      a.rt_pairs = 1;
+      a.rt_R = r2;
+      a.rt_S = s2;
+      a.BK = 32;
+      a.cchunks = 1;
+      a.num_kb = r2 * s2 / 2;
+      a.BN = bn;
+      a.M = static_cast<int>(M);
+      a.N = k;
+      a.batch = 1;
+      a.epi = e;
+      a.out = d_y;
+      a.ldc = k;
+      a.vec_ok = k % 16 == 0;
+      a.Ho = g.ho; a.Wo = g.wo; a.S = s2;
+      a.n_img = n;
+      a.rt_P = P;
+      a.rt_T = 128 / P;
+      a.rt_x0 = xoff;
+      a.rt_y0 = yoff;
+      a.rt_plane = 16;  // K-direction core-matrix stride: one pixel
+      // Window rows: the last tap slice of the tile's last accumulator row reads pixel
+      // (r2 - 1) * P + s2 - 1 + 127, which must stay inside the box.
+      const int rows = ((r2 - 1) * P + s2 - 1 + 128 + P - 1) / P;
+      a.rt_box = rows * P * 16;
+      a.rt_stage = (a.rt_box + 1023) / 1024 * 1024;
+      CUtensorMap ma, mb;
+      rc = encode_tiled_3d(&mb, wsd, static_cast<uint64_t>(r2 * s2 * 16), static_cast<uint64_t>(k), 1, 32, a.BN, 32);
+      if (rc) return rc;
+      a.rt_wide = 1;
+      rc = encode_rowtile_wide(&ma, xs, n, h2, w2, P, rows);
+      if (rc) return rc;
+      g_last_path = 10;
+      return launch_tc(*st, ma, mb, a, cs);
+    }
+  }
   // Row tiles for 3x3 / stride 1 / pad 1 convs whose weights stay resident: one window load per
   // tile serves all nine taps (the im2col mode loads the window nine times, one row per pixel).
   const int rt_P = g.wo + 1;
@@ -658,6 +756,8 @@ static int conv2d_s8_impl(const int8_t* d_x, const int8_t* d_w, const int32_t* d
     a.n_img = n;
     a.rt_P = rt_P;
     a.rt_T = 128 / rt_P;
+    a.rt_x0 = -1;
+    a.rt_y0 = -1;
     // T + 3 window rows: the right-border tap of the last output row reads index (T + 2) * P, the
     // zero column of one more row (without it that read would reach the next channel plane).
     a.rt_plane = (a.rt_T + 3) * rt_P * 16;
@@ -667,7 +767,7 @@ static int conv2d_s8_impl(const int8_t* d_x, const int8_t* d_w, const int32_t* d
     CUtensorMap ma, mb;
     rc = encode_tiled_3d(&mb, d_w, static_cast<uint64_t>(9 * c), static_cast<uint64_t>(k), 1, a.BK, a.BN, a.BK);
     if (rc) return rc;
-    rc = encode_rowtile(&ma, d_x, g, a.rt_P, a.rt_T);
+    rc = encode_rowtile(&ma, d_x, g.n, g.h, g.w, c, a.rt_P, a.rt_T + 3);
     if (rc) return rc;
     g_last_path = 9;
     return launch_tc(*st, ma, mb, a, cs);

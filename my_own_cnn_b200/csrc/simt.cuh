@@ -582,4 +582,61 @@ __global__ void weight_pad_s8_kernel(const int8_t* __restrict__ w, int8_t* __res
   }
 }
 
+// Space-to-depth of a stride-2 conv input: x [n][h][w][C] (C <= 4) -> xs [n][h2][w2][16] with
+// xs[i][Y][X][(dy * 2 + dx) * C + ci] = x[i][2Y + dy][2X + dx][ci], zero past the image and in
+// channels 4C..15.  A stride-2 R x S conv of x is then a stride-1 conv of xs (weights rearranged
+// by s2d_weight_s8_kernel) whose 16-byte pixels a TMA box can load.  One thread per output pixel.
+template <int C>
+__global__ void s2d_s8_kernel(const int8_t* __restrict__ x, int8_t* __restrict__ xs, int n, int h, int w, int h2,
+                              int w2) {
+  const size_t total = static_cast<size_t>(n) * h2 * w2;
+  for (size_t idx = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; idx < total;
+       idx += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const int X = static_cast<int>(idx % w2);
+    const size_t t = idx / w2;
+    const int Y = static_cast<int>(t % h2);
+    const int img = static_cast<int>(t / h2);
+    uint32_t wd[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int y = 2 * Y + (q >> 1), xx = 2 * X + (q & 1);
+      if (y < h && xx < w) {
+        const int8_t* src = x + ((static_cast<size_t>(img) * h + y) * w + xx) * C;
+#pragma unroll
+        for (int ci = 0; ci < C; ++ci) {
+          const int byte = q * C + ci;
+          wd[byte >> 2] |= static_cast<uint32_t>(static_cast<uint8_t>(src[ci])) << (8 * (byte & 3));
+        }
+      }
+    }
+    reinterpret_cast<uint4*>(xs)[idx] = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+  }
+}
+
+// Weights of a stride-2 conv [k][rk][sk][c] -> [k][r2][s2][16] for the space-to-depth input:
+// tap (R, S), channel (dy * 2 + dx) * c + ci holds w[kk][r][s][ci] with
+// r = 2 * (R + yoff) + dy + pad_h, s = 2 * (S + xoff) + dx + pad_w (zero outside the filter), where
+// yoff = floor(-pad_h / 2), xoff = floor(-pad_w / 2) place the window's first space-to-depth row /
+// column relative to the output row / column.
+__global__ void s2d_weight_s8_kernel(const int8_t* __restrict__ w, int8_t* __restrict__ ws, int k, int rk, int sk,
+                                     int c, int r2, int s2, int pad_h, int pad_w) {
+  const int total = k * r2 * s2 * 16;
+  const int yoff = -((pad_h + 1) / 2), xoff = -((pad_w + 1) / 2);
+  for (int idx = blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += gridDim.x * blockDim.x) {
+    const int cc = idx & 15;
+    int t = idx >> 4;
+    const int S = t % s2;
+    t /= s2;
+    const int R = t % r2;
+    const int kk = t / r2;
+    int8_t v = 0;
+    if (cc < 4 * c) {
+      const int q = cc / c, ci = cc - q * c;
+      const int r = 2 * (R + yoff) + (q >> 1) + pad_h, s = 2 * (S + xoff) + (q & 1) + pad_w;
+      if (r >= 0 && r < rk && s >= 0 && s < sk) v = w[((static_cast<size_t>(kk) * rk + r) * sk + s) * c + ci];
+    }
+    ws[idx] = v;
+  }
+}
+
 }  // namespace b200q

@@ -60,6 +60,12 @@ struct TcArgs {
   int rt_box;    // bytes of one window box (rt_plane * C / 16)
   int n_img;     // images (row tiles enumerate image x block of output rows)
   int rt_stage;  // ring stage size for row tiles (window + read-past slack, 1024-aligned)
+  int rt_x0, rt_y0;  // window origin relative to (output column 0, the tile's first output row)
+  // Tap-pair row tiles (space-to-depth stems): 16 channels per pixel, rt_R x rt_S taps, and each
+  // K = 32 MMA slice covers taps (r, s) and (r, s + 1): the A descriptor's K-direction core
+  // matrix stride is one pixel (rt_plane = 16), so the second half of the slice is the next pixel.
+  int rt_pairs, rt_R, rt_S;
+  int rt_wide;  // window map in 8-byte elements {2 * W, H, N} (one channel plane): rows of whole pixels
 };
 
 constexpr int kTcMaxAcc = 8;
@@ -311,6 +317,40 @@ __device__ __forceinline__ void emit_chunk(const TcArgs& a, const CUtensorMap* t
   if (m < a.M) store_chunk<KIND, CL, RES>(a, v, row_off + n, n, min(32, a.N - n), bias, scale, has_bias);
 }
 
+// Coordinates (b, mt, nt) of tile index b * (m_tiles * n_tiles) + mt * n_tiles + nt, advanced
+// by a fixed stride with carries (the persistent loops visit tile, tile + stride, ...).
+struct TileWalk {
+  int b, mt, nt;
+  int m_tiles, n_tiles, inc_b, inc_mt, inc_nt;
+  __device__ __forceinline__ TileWalk(int tile, int stride, int batch, int m_tiles_, int n_tiles_)
+      : m_tiles(m_tiles_), n_tiles(n_tiles_) {
+    const int per_b = m_tiles * n_tiles;
+    b = tile / per_b;
+    const int rem = tile - b * per_b;
+    mt = rem / n_tiles;
+    nt = rem - mt * n_tiles;
+    inc_b = stride / per_b;
+    const int srem = stride - inc_b * per_b;
+    inc_mt = srem / n_tiles;
+    inc_nt = srem - inc_mt * n_tiles;
+    (void)batch;
+  }
+  __device__ __forceinline__ void next() {
+    nt += inc_nt;
+    int c = 0;
+    if (nt >= n_tiles) {
+      nt -= n_tiles;
+      c = 1;
+    }
+    mt += inc_mt + c;
+    b += inc_b;
+    if (mt >= m_tiles) {
+      mt -= m_tiles;
+      ++b;
+    }
+  }
+};
+
 // PAIR: the CTA is one half of a 2-SM pair (tiles of 2 x 128 rows; this CTA's TMEM holds rows
 // rank * 128 .. + 127 of each tile; the accumulator-empty barrier lives in the leader CTA).
 template <int KIND, bool TMA, int CL, bool PAIR, bool RES>
@@ -326,28 +366,28 @@ __device__ __forceinline__ void epilogue_role_t(const TcArgs& a, const CUtensorM
   const int nunits = PAIR ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
   constexpr int TM = PAIR ? 2 * kTcBM : kTcBM;
   const int row = rank * kTcBM + q * 32 + lane;
-  const int tiles_per_batch = a.m_tiles * a.n_tiles;
   int buf = 0;
   uint32_t acc_ph = 0;
   int sel = half;  // this warp's chunks in the current tile: sel, sel + 2, ...
-  for (int tile = unit; tile < a.total_tiles; tile += nunits, sel ^= 1) {
-    const int b = tile / tiles_per_batch;
-    const int rem = tile - b * tiles_per_batch;
-    const int mt = rem / a.n_tiles;
-    const int nt = rem - mt * a.n_tiles;
+  // Tile coordinates advance by `nunits` tiles per iteration as mixed-radix counters (batch item,
+  // M tile, N tile; for row tiles image and block of output rows): no integer division per tile.
+  TileWalk tw(unit, nunits, a.batch, a.m_tiles, a.n_tiles);
+  const bool rt = !PAIR && a.mode == 2;
+  const int rblocks = rt ? (a.Ho + a.rt_T - 1) / a.rt_T : 1;
+  TileWalk rw(rt ? unit : 0, nunits, 1 << 30, rblocks, 1);  // (image, row block) of mode-2 tiles
+  // Row tile: TMEM row -> (tile row ti, column wo) at pitch P; pitch padding and rows past the
+  // tile or the image are not stored.
+  const int ti = rt ? row / a.rt_P : 0, two = rt ? row - ti * a.rt_P : 0;
+  for (int tile = unit; tile < a.total_tiles; tile += nunits, sel ^= 1, tw.next(), rw.next()) {
+    const int b = tw.b, mt = tw.mt, nt = tw.nt;
     int m = mt * TM + row;
     const int n0 = nt * a.BN;
     size_t rt_off = 0;
-    if (!PAIR && a.mode == 2) {
-      // Row tile: TMEM row -> (tile row i, column wo) at pitch P; pitch padding and rows past the
-      // tile or the image are not stored.
-      const int rblocks = (a.Ho + a.rt_T - 1) / a.rt_T;
-      const int img = mt / rblocks;
-      const int ho0 = (mt - img * rblocks) * a.rt_T;
-      const int i = row / a.rt_P, wo = row - i * a.rt_P;
-      const bool valid = i < a.rt_T && ho0 + i < a.Ho && wo < a.Wo;
+    if (rt) {
+      const int img = rw.b, ho0 = rw.mt * a.rt_T;
+      const bool valid = ti < a.rt_T && ho0 + ti < a.Ho && two < a.Wo;
       m = valid ? 0 : a.M;
-      rt_off = (static_cast<size_t>(img * a.Ho + ho0 + i) * a.Wo + wo) * a.ldc;
+      rt_off = (static_cast<size_t>(img * a.Ho + ho0 + ti) * a.Wo + two) * a.ldc;
     }
     // Chunks holding columns < N; the two warps of a lane quarter swap parities every tile, so an
     // odd chunk count (N <= 32, N = 96, ...) is shared evenly over two tiles.
@@ -506,6 +546,48 @@ __device__ __forceinline__ bool rowtile_mma_loop(const TcArgs& a, uint32_t tmem_
 
 // MMA issue of the tiled / im2col modes: per K block (one ring stage) KS K-slices of 32 bytes,
 // unrolled, with the stage offsets advanced by adds instead of products.  BRES: the weights are
+// MMA issue of tap-pair row tiles: R x S taps over 16-channel pixels, S / 2 K = 32 slices per tap
+// row (taps s and s + 1), fully unrolled; weights resident (slice kb at kb * stage_b).
+template <int R, int S>
+__device__ __forceinline__ bool rowtile_pair_loop(const TcArgs& a, uint32_t tmem_base, uint64_t rt_desc0,
+                                                  uint64_t b_desc0, uint32_t stage_a, uint32_t stage_b,
+                                                  uint32_t full0, uint32_t empty0, uint32_t accf0, uint32_t acce0) {
+  const uint32_t P = static_cast<uint32_t>(a.rt_P);
+  const uint32_t bstep = stage_b >> 4;
+  const uint32_t idesc = a.idesc;
+  int stage = 0, buf = 0;
+  uint32_t ph = 0, acc_ph = 0;
+  for (int tile = blockIdx.x; tile < a.total_tiles; tile += gridDim.x) {
+    if (!__all_sync(0xFFFFFFFFu, mbar_wait_bounded(acce0 + 8 * buf, acc_ph ^ 1u, a.wait_limit, a.err,
+                                                   kDevErrTimeoutMma)))
+      return false;
+    tc_fence_after();
+    const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * a.BN);
+    if (!__all_sync(0xFFFFFFFFu, mbar_wait_bounded(full0 + 8 * stage, ph, a.wait_limit, a.err, kDevErrTimeoutMma)))
+      return false;
+    const uint64_t ad_s = rt_desc0 + ((stage * stage_a) >> 4);
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+#pragma unroll
+      for (int sp = 0; sp < S / 2; ++sp) {
+        const int kb = r * (S / 2) + sp;
+        tc_mma_i8_elect(d_tmem, ad_s + static_cast<uint64_t>(r * P + 2 * sp), b_desc0 + static_cast<uint64_t>(kb * bstep),
+                        idesc, kb != 0 ? 1u : 0u);
+      }
+    tc_commit_elect(empty0 + 8 * stage);
+    if (++stage == a.stages) {
+      stage = 0;
+      ph ^= 1u;
+    }
+    tc_commit_elect(accf0 + 8 * buf);
+    if (++buf == a.nacc) {
+      buf = 0;
+      acc_ph ^= 1u;
+    }
+  }
+  return true;
+}
+
 // resident (K block kb of B at kb * stage_b) rather than in the ring.
 template <int KS, bool BRES>
 __device__ __forceinline__ bool gemm_mma_loop(const TcArgs& a, uint32_t tmem_base, uint64_t a_desc0, uint64_t b_desc0,
@@ -650,7 +732,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
         const uint32_t fb = full0 + 8 * stage;
         mbar_arrive_expect_tx(fb, tx);
-        tma_load_5d(smem_u32(sA + stage * stage_a), &tmA, fb, 0, -1, ho0 - 1, 0, img);
+        if (a.rt_wide)
+          tma_load_3d(smem_u32(sA + stage * stage_a), &tmA, fb, 2 * a.rt_x0, ho0 + a.rt_y0, img);
+        else
+          tma_load_5d(smem_u32(sA + stage * stage_a), &tmA, fb, 0, a.rt_x0, ho0 + a.rt_y0, 0, img);
         issued_mask |= 1u << stage;
         last_ph = (last_ph & ~(1u << stage)) | (ph << stage);
         if (++stage == a.stages) {
@@ -735,7 +820,18 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       // Row tiles: A in the no-swizzle K-major layout [C/16][pixel][16 B] (SBO = 8 pixels, LBO =
       // one channel-chunk plane); tap (r, s) is the same window started (r * P + s) pixels later.
       const uint64_t rt_desc0 = make_smem_desc(smem_u32(sA), static_cast<uint32_t>(a.rt_plane), 128u, 0u);
-      if (ok && a.mode == 2) {
+      if (ok && a.mode == 2 && a.rt_pairs) {
+#define B200Q_PAIR_MMA(R, S) \
+  ok = rowtile_pair_loop<R, S>(a, tmem_base, rt_desc0, b_desc0, stage_a, stage_b, full0, empty0, accf0, acce0)
+        const int rs = a.rt_R * 8 + a.rt_S;
+        if (rs == 4 * 8 + 4) B200Q_PAIR_MMA(4, 4);
+        else if (rs == 4 * 8 + 2) B200Q_PAIR_MMA(4, 2);
+        else if (rs == 3 * 8 + 4) B200Q_PAIR_MMA(3, 4);
+        else if (rs == 3 * 8 + 2) B200Q_PAIR_MMA(3, 2);
+        else if (rs == 2 * 8 + 4) B200Q_PAIR_MMA(2, 4);
+        else B200Q_PAIR_MMA(2, 2);
+#undef B200Q_PAIR_MMA
+      } else if (ok && a.mode == 2) {
         const uint32_t pl2 = static_cast<uint32_t>(a.rt_plane) >> 3;  // two channel-chunk planes
         switch (a.BK) {
           case 32:

@@ -25,7 +25,8 @@ def _b2q():
     ((4, 14, 14, 256, 1, 1, 512, 0, 1), "tcgen05-tiled"),     # reduction 256: TMA-store epilogue
     ((4, 28, 28, 64, 3, 3, 64, 1, 1), "tcgen05-rowtile"),
     ((4, 28, 28, 128, 3, 3, 128, 1, 1), "tcgen05-im2col"),
-    ((4, 64, 64, 3, 7, 7, 64, 3, 2), "tcgen05-packed"),        # C = 3 stem geometry
+    ((4, 64, 64, 3, 7, 7, 64, 3, 2), "tcgen05-s2d"),           # C = 3 stem geometry
+    ((2, 56, 56, 24, 3, 3, 40, 1, 1), "tcgen05-packed"),       # C = 24: im2col pack
     ((1, 6, 6, 48, 3, 3, 64, 1, 1), "cuda-core-generic"),
     ((3, 7, 9, 32, 1, 1, 48, 0, 1), "tcgen05-tiled"),         # ragged M, N = 48 (16-column tail)
 ])

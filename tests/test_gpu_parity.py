@@ -181,8 +181,6 @@ def test_conv_s8_cuda_core_paths(cuda_lib, shape, groups, expect):
 
 
 @pytest.mark.parametrize("shape", [
-    (4, 64, 64, 3, 7, 7, 64, 3, 2, 1),     # ResNet-50 stem geometry (7x7/2, C = 3)
-    (2, 128, 128, 3, 3, 3, 32, 1, 2, 1),   # MobileNetV2 stem (3x3/2, C = 3 -> 32)
     (2, 56, 56, 24, 1, 1, 144, 0, 1, 1),   # MobileNetV2 expand 24 -> 144
     (2, 48, 48, 24, 3, 3, 40, 1, 1, 1),    # C = 24, 3x3, K = 40 (scalar edge stores)
 ])
@@ -192,6 +190,28 @@ def test_conv_s8_packed_low_channel(cuda_lib, shape):
     p = b2q.Conv2DParams(pad, pad, st, st, dil, dil, 1)
     paths = _conv_case(n, h, w, c, r, s, k, p, seed=3 + sum(shape))
     assert paths == {"tcgen05-packed"}, paths
+
+
+@pytest.mark.parametrize("shape", [
+    # n, h, w, c, r, s, k, pad, stride, dil
+    (4, 64, 64, 3, 7, 7, 64, 3, 2, 1),     # ResNet-50 stem geometry (7x7/2, C = 3): 4x4 tap pairs
+    (2, 128, 128, 3, 3, 3, 32, 1, 2, 1),   # MobileNetV2 stem (3x3/2, C = 3 -> 32): 2x2 taps
+    (3, 45, 39, 3, 7, 7, 64, 3, 2, 1),     # odd H / W: zero row / column in the last 2x2 blocks
+    (3, 64, 64, 1, 3, 3, 16, 1, 2, 1),     # C = 1, N = 16
+    (3, 40, 40, 4, 5, 5, 48, 2, 2, 1),     # C = 4, 5x5 pad 2: 3 x 4 taps, N = 48
+    (3, 41, 41, 2, 3, 3, 40, 0, 2, 1),     # C = 2, no padding, N = 40 (scalar tail)
+    (1, 40, 250, 3, 7, 7, 64, 3, 2, 1),    # Wo = 125: row pitch 128, one output row per tile
+    (4, 32, 32, 3, 7, 7, 256, 3, 2, 1),    # N = 256
+])
+def test_conv_s8_tcgen05_s2d_stem(cuda_lib, shape):
+    """Stride-2 low-channel convs (network stems; at least 1024 output pixels) as row tiles over a
+    space-to-depth copy of the input: 2x2 pixel blocks become 16-channel pixels and each MMA slice
+    covers two taps."""
+    b2q = _b2q()
+    n, h, w, c, r, s, k, pad, st, dil = shape
+    p = b2q.Conv2DParams(pad, pad, st, st, dil, dil, 1)
+    paths = _conv_case(n, h, w, c, r, s, k, p, seed=11 + sum(shape))
+    assert paths == {"tcgen05-s2d"}, paths
 
 
 @pytest.mark.parametrize("shape", [
