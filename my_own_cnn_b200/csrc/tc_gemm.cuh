@@ -114,6 +114,40 @@ __device__ __forceinline__ uint32_t quant4_s8(const Epilogue& e, float f0, float
   return pack4_sat_s8(r0, r1, r2, r3);
 }
 
+// Coordinates (b, mt, nt) of tile index b * (m_tiles * n_tiles) + mt * n_tiles + nt, advanced
+// by a fixed stride with carries (the persistent loops visit tile, tile + stride, ...).
+struct TileWalk {
+  int b, mt, nt;
+  int m_tiles, n_tiles, inc_b, inc_mt, inc_nt;
+  __device__ __forceinline__ TileWalk(int tile, int stride, int batch, int m_tiles_, int n_tiles_)
+      : m_tiles(m_tiles_), n_tiles(n_tiles_) {
+    const int per_b = m_tiles * n_tiles;
+    b = tile / per_b;
+    const int rem = tile - b * per_b;
+    mt = rem / n_tiles;
+    nt = rem - mt * n_tiles;
+    inc_b = stride / per_b;
+    const int srem = stride - inc_b * per_b;
+    inc_mt = srem / n_tiles;
+    inc_nt = srem - inc_mt * n_tiles;
+    (void)batch;
+  }
+  __device__ __forceinline__ void next() {
+    nt += inc_nt;
+    int c = 0;
+    if (nt >= n_tiles) {
+      nt -= n_tiles;
+      c = 1;
+    }
+    mt += inc_mt + c;
+    b += inc_b;
+    if (mt >= m_tiles) {
+      mt -= m_tiles;
+      ++b;
+    }
+  }
+};
+
 // Vector form of the fused epilogue: the first 4 * NQ columns of the chunk (NQ = 8: all 32,
 // NQ = 4: the first 16), 16-byte bias / scale reads and 16-byte stores.
 template <int KIND, int CL, int NQ, bool RES>
@@ -316,40 +350,6 @@ __device__ __forceinline__ void emit_chunk(const TcArgs& a, const CUtensorMap* t
   }
   if (m < a.M) store_chunk<KIND, CL, RES>(a, v, row_off + n, n, min(32, a.N - n), bias, scale, has_bias);
 }
-
-// Coordinates (b, mt, nt) of tile index b * (m_tiles * n_tiles) + mt * n_tiles + nt, advanced
-// by a fixed stride with carries (the persistent loops visit tile, tile + stride, ...).
-struct TileWalk {
-  int b, mt, nt;
-  int m_tiles, n_tiles, inc_b, inc_mt, inc_nt;
-  __device__ __forceinline__ TileWalk(int tile, int stride, int batch, int m_tiles_, int n_tiles_)
-      : m_tiles(m_tiles_), n_tiles(n_tiles_) {
-    const int per_b = m_tiles * n_tiles;
-    b = tile / per_b;
-    const int rem = tile - b * per_b;
-    mt = rem / n_tiles;
-    nt = rem - mt * n_tiles;
-    inc_b = stride / per_b;
-    const int srem = stride - inc_b * per_b;
-    inc_mt = srem / n_tiles;
-    inc_nt = srem - inc_mt * n_tiles;
-    (void)batch;
-  }
-  __device__ __forceinline__ void next() {
-    nt += inc_nt;
-    int c = 0;
-    if (nt >= n_tiles) {
-      nt -= n_tiles;
-      c = 1;
-    }
-    mt += inc_mt + c;
-    b += inc_b;
-    if (mt >= m_tiles) {
-      mt -= m_tiles;
-      ++b;
-    }
-  }
-};
 
 // PAIR: the CTA is one half of a 2-SM pair (tiles of 2 x 128 rows; this CTA's TMEM holds rows
 // rank * 128 .. + 127 of each tile; the accumulator-empty barrier lives in the leader CTA).
@@ -691,7 +691,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   tc_fence_after();
   // Broadcast from lane 0 so the compiler treats the TMEM base as warp-uniform.
   const uint32_t tmem_base = __shfl_sync(0xFFFFFFFFu, *tmem_slot, 0);
-  const int tiles_per_batch = a.m_tiles * a.n_tiles;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -720,12 +719,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         mbar_arrive_expect_tx(b_full, a.num_kb * stage_b);
         for (int kb = 0; kb < a.num_kb; ++kb) load_b(smem_u32(sB + kb * stage_b), b_full, kb, 0, 0);
       }
-      for (int tile = blockIdx.x; tile < a.total_tiles && ok && a.mode == 2; tile += gridDim.x) {
-        // Row tiles: one window load per tile (all taps, all channels); tiles enumerate
-        // (image, block of rt_T output rows).
-        const int rblocks = (a.Ho + a.rt_T - 1) / a.rt_T;
-        const int img = tile / rblocks;
-        const int ho0 = (tile - img * rblocks) * a.rt_T;
+      // Row tiles: one window load per tile (all taps, all channels); tiles enumerate
+      // (image, block of rt_T output rows).
+      TileWalk rw(a.mode == 2 ? static_cast<int>(blockIdx.x) : 0, gridDim.x, 1 << 30,
+                  a.mode == 2 ? (a.Ho + a.rt_T - 1) / a.rt_T : 1, 1);
+      for (int tile = blockIdx.x; tile < a.total_tiles && ok && a.mode == 2; tile += gridDim.x, rw.next()) {
+        const int img = rw.b;
+        const int ho0 = rw.mt * a.rt_T;
         if (!mbar_wait_bounded(empty0 + 8 * stage, ph ^ 1u, a.wait_limit, a.err, kDevErrTimeoutProducer)) {
           ok = false;
           break;
@@ -743,11 +743,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           ph ^= 1u;
         }
       }
-      for (int tile = blockIdx.x; tile < a.total_tiles && ok && a.mode != 2; tile += gridDim.x) {
-        const int b = tile / tiles_per_batch;
-        const int rem = tile - b * tiles_per_batch;
-        const int mt = rem / a.n_tiles;
-        const int nt = rem - mt * a.n_tiles;
+      TileWalk tw(blockIdx.x, gridDim.x, a.batch, a.m_tiles, a.n_tiles);
+      for (int tile = blockIdx.x; tile < a.total_tiles && ok && a.mode != 2; tile += gridDim.x, tw.next()) {
+        const int b = tw.b, mt = tw.mt, nt = tw.nt;
         const int m0 = mt * kTcBM, n0 = nt * a.BN;
         int img = 0, wbase = 0, hbase = 0;
         if (a.mode == 1) {
