@@ -343,6 +343,7 @@ int launch_tc(const DeviceState& st, const CUtensorMap& ma, const CUtensorMap& m
   // Stage per-column bias / scale in shared memory when they fit (4096 columns = 32 KiB).
   a.stage_cols = (a.epi.out_kind != kOutS32 || a.epi.bias) && a.N <= 4096 ? (a.N + 31) / 32 * 32 : 0;
   a.default_clamp = a.epi.out_kind == kOutS8 && a.epi.zp == 0 && a.epi.lo == -128 && a.epi.hi == 127;
+  a.hi_f = static_cast<float>(a.epi.hi);
   // int8 outputs: TMA stores when the row pitch allows a map and every 32-column chunk can read
   // its bias / scale (staged columns are zero-padded to a multiple of 32).  GEMMs with a reduction
   // shorter than 128 keep direct stores: there the epilogue alone sets the pace and the staging
@@ -734,10 +735,14 @@ static int conv2d_s8_impl(const int8_t* d_x, const int8_t* d_w, const int32_t* d
   // tile serves all nine taps (the im2col mode loads the window nine times, one row per pixel).
   const int rt_P = g.wo + 1;
   const int rt_bn = pick_bn(k, 0);
+  // Resident weights plus at least two window stages must fit in shared memory.
+  const long long rt_T0 = rt_P <= 128 ? 128 / rt_P : 1;
+  const long long rt_stage0 = ((rt_T0 + 3) * rt_P * c + (2 * rt_P + 2 + 128) * 16 + 1023) / 1024 * 1024;
+  const bool rt_fits = 9ll * c * rt_bn + 2 * rt_stage0 + kSmemReserve + 8 * 1024 <= kSmemLimit;
   const bool rowtile_ok = g_rowtile && g_policy.load() == 0 && g.groups == 1 && r == 3 && s == 3 &&
                           g.stride_h == 1 && g.stride_w == 1 && g.pad_h == 1 && g.pad_w == 1 && g.dil_h == 1 &&
                           g.dil_w == 1 && (c == 32 || c == 64 || c == 128) && k <= 256 && rt_P <= 128 &&
-                          9ll * c * rt_bn <= 72 * 1024 && vec_ptrs && M < (1ll << 31);
+                          rt_fits && vec_ptrs && M < (1ll << 31);
   if (rowtile_ok) {
     TcArgs a{};
     a.mode = 2;

@@ -66,6 +66,7 @@ struct TcArgs {
   // matrix stride is one pixel (rt_plane = 16), so the second half of the slice is the next pixel.
   int rt_pairs, rt_R, rt_S;
   int rt_wide;  // window map in 8-byte elements {2 * W, H, N} (one channel plane): rows of whole pixels
+  float hi_f;   // float(epi.hi), for the float-domain clamp of quant4_s8<2>
 };
 
 constexpr int kTcMaxAcc = 8;
@@ -99,9 +100,10 @@ __device__ __forceinline__ uint32_t pack4_sat_s8(int a, int b, int c, int d) {
 // conversion (zero point 0 and lo = 0, the ReLU / ReLU6 forms: max(NaN, 0) = 0 matches
 // rint_sat(NaN) = 0, and integer bounds commute with rounding), the upper bound 127 by the pack.
 template <int CL>
-__device__ __forceinline__ uint32_t quant4_s8(const Epilogue& e, float f0, float f1, float f2, float f3) {
+__device__ __forceinline__ uint32_t quant4_s8(const TcArgs& a, float f0, float f1, float f2, float f3) {
+  const Epilogue& e = a.epi;
   if constexpr (CL == 2) {
-    const float hi = static_cast<float>(e.hi);
+    const float hi = a.hi_f;
     f0 = fminf(fmaxf(f0, 0.0f), hi); f1 = fminf(fmaxf(f1, 0.0f), hi);
     f2 = fminf(fmaxf(f2, 0.0f), hi); f3 = fminf(fmaxf(f3, 0.0f), hi);
   }
@@ -190,7 +192,7 @@ __device__ __forceinline__ void store_vec(const TcArgs& a, const uint32_t (&v)[3
           f2 = __fadd_rn(f2, __fmul_rn(__int2float_rn(sbyte(rw[q], 2)), e.res_scale));
           f3 = __fadd_rn(f3, __fmul_rn(__int2float_rn(sbyte(rw[q], 3)), e.res_scale));
         }
-        packed[q] = quant4_s8<CL>(e, f0, f1, f2, f3);
+        packed[q] = quant4_s8<CL>(a, f0, f1, f2, f3);
       }
     }
   }
@@ -311,7 +313,7 @@ __device__ __forceinline__ void stage_chunk_s8(const TcArgs& a, const uint32_t (
       f2 = __fadd_rn(f2, __fmul_rn(__int2float_rn(sbyte(rw[q], 2)), e.res_scale));
       f3 = __fadd_rn(f3, __fmul_rn(__int2float_rn(sbyte(rw[q], 3)), e.res_scale));
     }
-    packed[q] = quant4_s8<CL>(e, f0, f1, f2, f3);
+    packed[q] = quant4_s8<CL>(a, f0, f1, f2, f3);
   }
   const int sw = (lane >> 2) & 1;
   *reinterpret_cast<uint4*>(sbuf + lane * 32 + (sw << 4)) = make_uint4(packed[0], packed[1], packed[2], packed[3]);

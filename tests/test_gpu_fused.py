@@ -24,7 +24,8 @@ def _b2q():
     ((8, 28, 28, 64, 1, 1, 256, 0, 1), "tcgen05-tiled"),      # reduction 64 < 128: direct 16-byte stores
     ((4, 14, 14, 256, 1, 1, 512, 0, 1), "tcgen05-tiled"),     # reduction 256: TMA-store epilogue
     ((4, 28, 28, 64, 3, 3, 64, 1, 1), "tcgen05-rowtile"),
-    ((4, 28, 28, 128, 3, 3, 128, 1, 1), "tcgen05-im2col"),
+    ((4, 28, 28, 128, 3, 3, 128, 1, 1), "tcgen05-rowtile"),   # 144 KiB of resident weights
+    ((4, 14, 14, 256, 3, 3, 256, 1, 1), "tcgen05-im2col"),
     ((4, 64, 64, 3, 7, 7, 64, 3, 2), "tcgen05-s2d"),           # C = 3 stem geometry
     ((2, 56, 56, 24, 3, 3, 40, 1, 1), "tcgen05-packed"),       # C = 24: im2col pack
     ((1, 6, 6, 48, 3, 3, 64, 1, 1), "cuda-core-generic"),

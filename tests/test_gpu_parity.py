@@ -127,7 +127,7 @@ def _conv_case(n, h, w, c, r, s, k, p, seed, epi_kind="all", groups=1):
 
 @pytest.mark.parametrize("shape", [
     # n, h, w, c, r, s, k, pad, stride, dil
-    (2, 28, 28, 128, 3, 3, 128, 1, 1, 1),  # ResNet stage-2 3x3 (weights too large for row tiles)
+    (4, 14, 14, 256, 3, 3, 256, 1, 1, 1),  # ResNet stage-3 3x3 (C = 256: no row tiles)
     (2, 34, 34, 64, 3, 3, 80, 1, 2, 1),    # stride 2, K edge (80 = 64 + 16)
     (1, 40, 36, 96, 3, 3, 48, 2, 1, 2),    # dilation 2, BK 32 chunks
     (2, 24, 24, 256, 1, 1, 272, 0, 2, 1),  # 1x1 stride 2 (projection shortcut) through im2col
@@ -221,6 +221,7 @@ def test_conv_s8_tcgen05_s2d_stem(cuda_lib, shape):
     (2, 13, 11, 64, 3, 3, 48, 1, 1, 1),    # ragged: H not a multiple of the tile rows, N = 48
     (3, 9, 127, 32, 3, 3, 32, 1, 1, 1),    # widest row (W + 1 = 128: one output row per tile)
     (2, 14, 14, 128, 3, 3, 64, 1, 1, 1),   # C = 128 (8 channel chunks per window)
+    (2, 28, 28, 128, 3, 3, 128, 1, 1, 1),  # ResNet stage-2 3x3: 144 KiB of resident weights, 2 stages
     (2, 7, 5, 64, 3, 3, 40, 1, 1, 1),      # N = 40 (scalar tail), tiny image
     (1, 6, 6, 64, 3, 3, 64, 1, 1, 1),      # 36 output pixels: one tile, 6 rows
 ])
