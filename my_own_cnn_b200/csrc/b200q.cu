@@ -344,6 +344,9 @@ int launch_tc(const DeviceState& st, const CUtensorMap& ma, const CUtensorMap& m
   a.stage_cols = (a.epi.out_kind != kOutS32 || a.epi.bias) && a.N <= 4096 ? (a.N + 31) / 32 * 32 : 0;
   a.default_clamp = a.epi.out_kind == kOutS8 && a.epi.zp == 0 && a.epi.lo == -128 && a.epi.hi == 127;
   a.hi_f = static_cast<float>(a.epi.hi);
+  a.vec8_ok = a.epi.out_kind == kOutS8 && a.stage_cols > 0 && a.N % 8 == 0 && a.ldc % 8 == 0 &&
+              reinterpret_cast<uintptr_t>(a.out) % 8 == 0 &&
+              (!a.epi.res || reinterpret_cast<uintptr_t>(a.epi.res) % 8 == 0);
   // int8 outputs: TMA stores when the row pitch allows a map and every 32-column chunk can read
   // its bias / scale (staged columns are zero-padded to a multiple of 32).  GEMMs with a reduction
   // shorter than 128 keep direct stores: there the epilogue alone sets the pace and the staging

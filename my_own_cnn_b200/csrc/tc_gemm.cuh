@@ -42,6 +42,7 @@ struct TcArgs {
   long long ldc;            // elements between output rows
   long long batch_stride;   // elements between output batch items
   int vec_ok;               // rows and bias/scale allow 16-byte vector stores
+  int vec8_ok;              // int8 rows allow 8-byte vector stores (N % 8 == 0; bias / scale staged)
   uint32_t idesc;
   uint32_t tmem_cols;
   int nacc;           // TMEM accumulator buffers (nacc x BN columns), 2..kTcMaxAcc
@@ -203,6 +204,49 @@ __device__ __forceinline__ void store_vec(const TcArgs& a, const uint32_t (&v)[3
   }
 }
 
+// int8 output of the first 4 * NQ columns of a chunk (NQ even) with 8-byte residual loads and
+// stores: rows of N % 16 == 8 bytes (N = 24, 40, ...) are only 8-byte aligned.  The arithmetic is
+// store_vec's.
+template <int CL, int NQ, bool RES>
+__device__ __forceinline__ void store_vec8(const TcArgs& a, const uint32_t (&v)[32], size_t off, int n,
+                                           const int32_t* bias, const float* scale, bool has_bias) {
+  const Epilogue& e = a.epi;
+  const int4* bp = reinterpret_cast<const int4*>(bias + n);
+  const float4* sp = reinterpret_cast<const float4*>(scale + n);
+  uint32_t packed[NQ];
+  uint32_t rw[NQ];
+  if constexpr (RES) {
+#pragma unroll
+    for (int i = 0; i < NQ / 2; ++i) {
+      const uint2 r = *reinterpret_cast<const uint2*>(e.res + off + 8 * i);
+      rw[2 * i] = r.x;
+      rw[2 * i + 1] = r.y;
+    }
+  }
+#pragma unroll
+  for (int q = 0; q < NQ; ++q) {
+    int t0 = static_cast<int>(v[4 * q + 0]), t1 = static_cast<int>(v[4 * q + 1]);
+    int t2 = static_cast<int>(v[4 * q + 2]), t3 = static_cast<int>(v[4 * q + 3]);
+    if (has_bias) {
+      const int4 bb = bp[q];
+      t0 = wrap_add(t0, bb.x); t1 = wrap_add(t1, bb.y); t2 = wrap_add(t2, bb.z); t3 = wrap_add(t3, bb.w);
+    }
+    const float4 s4 = sp[q];
+    float f0 = __fmul_rn(__int2float_rn(t0), s4.x), f1 = __fmul_rn(__int2float_rn(t1), s4.y);
+    float f2 = __fmul_rn(__int2float_rn(t2), s4.z), f3 = __fmul_rn(__int2float_rn(t3), s4.w);
+    if constexpr (RES) {
+      f0 = __fadd_rn(f0, __fmul_rn(__int2float_rn(sbyte(rw[q], 0)), e.res_scale));
+      f1 = __fadd_rn(f1, __fmul_rn(__int2float_rn(sbyte(rw[q], 1)), e.res_scale));
+      f2 = __fadd_rn(f2, __fmul_rn(__int2float_rn(sbyte(rw[q], 2)), e.res_scale));
+      f3 = __fadd_rn(f3, __fmul_rn(__int2float_rn(sbyte(rw[q], 3)), e.res_scale));
+    }
+    packed[q] = quant4_s8<CL>(a, f0, f1, f2, f3);
+  }
+  uint2* o = reinterpret_cast<uint2*>(static_cast<int8_t*>(a.out) + off);
+#pragma unroll
+  for (int i = 0; i < NQ / 2; ++i) o[i] = make_uint2(packed[2 * i], packed[2 * i + 1]);
+}
+
 // Fused epilogue for one row and 32 consecutive output columns [n, n + valid).
 // bias / scale point at shared memory (staged) or global memory; bias may be null.
 // All array indices are compile-time constants after unrolling: nothing spills to local memory.
@@ -210,6 +254,22 @@ template <int KIND, int CL, bool RES>
 __device__ __forceinline__ void store_chunk(const TcArgs& a, const uint32_t (&v)[32], size_t off, int n, int valid,
                                             const int32_t* bias, const float* scale, bool has_bias) {
   const Epilogue& e = a.epi;
+  if constexpr (KIND == kOutS8) {
+    if (!a.vec_ok && a.vec8_ok) {  // N % 16 == 8: 8-byte rows
+      if (valid == 32) {
+        store_vec8<CL, 8, RES>(a, v, off, n, bias, scale, has_bias);
+        return;
+      }
+      if (valid == 24) {
+        store_vec8<CL, 6, RES>(a, v, off, n, bias, scale, has_bias);
+        return;
+      }
+      if (valid == 8) {
+        store_vec8<CL, 2, RES>(a, v, off, n, bias, scale, has_bias);
+        return;
+      }
+    }
+  }
   if (a.vec_ok) {
     if (valid == 32) {
       store_vec<KIND, CL, 8, RES>(a, v, off, n, bias, scale, has_bias);

@@ -142,6 +142,8 @@ def test_resnet_bottleneck_block_chained_on_device(cuda_lib):
     ((4, 14, 14, 256, 1, 1, 512, 0, 1), "tcgen05-tiled"),     # TMA-store epilogue
     ((4, 28, 28, 64, 3, 3, 64, 1, 1), "tcgen05-rowtile"),
     ((3, 7, 9, 32, 1, 1, 48, 0, 1), "tcgen05-tiled"),         # 16-column tail
+    ((2, 28, 28, 144, 1, 1, 24, 0, 1), "tcgen05-tiled"),      # N = 24: 8-byte rows (MobileNetV2 project)
+    ((3, 7, 9, 32, 1, 1, 40, 0, 1), "tcgen05-tiled"),         # N = 40: 32 + 8-column tail, 8-byte rows
 ])
 @pytest.mark.parametrize("with_res", [False, True])
 def test_clamp_forms_with_special_scales(cuda_lib, shape, expect, with_res):
