@@ -296,6 +296,12 @@ const bool g_rowtile = [] {
   return !(v && v[0] == '0');
 }();
 
+// Shortest reduction of an int8-output GEMM that takes 2-SM tiles (env B200Q_PAIR_MIN_K, for A/B).
+const int g_pair_min_k = [] {
+  const char* v = getenv("B200Q_PAIR_MIN_K");
+  return v ? atoi(v) : 2048;
+}();
+
 // Space-to-depth stem switch (env B200Q_S2D=0 keeps low-channel stride-2 convs on the packed
 // path, for A/B timing).
 const bool g_s2d = [] {
@@ -316,7 +322,7 @@ const int g_nacc_max = [] {
 // caller encodes the B map with BN / 2 rows per box when this holds.
 bool want_pair(const DeviceState& st, const TcArgs& a) {
   if (!g_pair || a.mode != 0 || a.a_major != 0 || a.b_major != 0 || a.conv_b || a.BN != 256) return false;
-  if (a.num_kb * a.BK < 2048 && a.epi.out_kind == kOutS8) return false;
+  if (a.num_kb * a.BK < g_pair_min_k && a.epi.out_kind == kOutS8) return false;
   const long long n_tiles = (a.N + a.BN - 1) / a.BN;
   const long long pair_tiles = static_cast<long long>(a.batch) * ((a.M + 2 * kTcBM - 1) / (2 * kTcBM)) * n_tiles;
   return n_tiles >= 2 && pair_tiles >= st.sms;
