@@ -157,6 +157,13 @@ size_t b200q_noalloc_scratch_bytes(void);
 
 /* ---- host utilities ---- */
 
+/* Kernel family (b200q_last_path code) that b200q_conv2d_s8 / b200q_conv2d_s8_add
+ * (has_residual != 0) would dispatch this conv to, assuming 16-byte aligned tensor pointers and
+ * the current path policy; decided on the host without launching anything (the SM count of the
+ * current device, or 148 when no GPU is visible).  The same decision drives the dispatch. */
+int b200q_conv2d_s8_plan(int n, int h, int w, int c, int r, int s, int k, const b200q_conv_params* p,
+                         const b200q_epilogue* epi, int has_residual, int* path);
+
 /* Output shape with the checks of infer_conv_shape (src/conv_types.h:125-146). */
 int b200q_conv_out_shape(int h, int w, int c, int r, int s, int k, const b200q_conv_params* p,
                          int* ho, int* wo);

@@ -8,7 +8,7 @@ from .quant import (DataType, QuantizationParametersU8, QuantizationParametersS5
                     qparams_to_device)
 from .conv import (Conv2DParams, BlockConv2DParams, ConvShape, BlockConvShape, Epilogue, infer_conv_shape,
                    infer_block_conv_shape, launch_fprop_nhwc_qi32, launch_block_fprop_nhwc_qi32, conv2d_s8,
-                   conv2d_s8_into, conv2d_s8_add, conv2d_s8_add_into, conv_out_shape)
+                   conv2d_s8_into, conv2d_s8_add, conv2d_s8_add_into, conv2d_s8_plan, conv_out_shape)
 from .pool import global_avgpool_s8, maxpool_s8
 from .bmm import BMM_TRANSPOSE_NONE, BMM_TRANSPOSE_YES, bmm_matmul_i32, bmm_s8, bmm_s8_into
 from ._lib import B200QError, last_path, set_path_policy, tc_launch_count
@@ -17,6 +17,6 @@ __all__ = [
     "DataType", "QuantizationParametersU8", "QuantizationParametersS5", "get_zero_point", "qparams_to_device",
     "Conv2DParams", "BlockConv2DParams", "ConvShape", "BlockConvShape", "Epilogue", "infer_conv_shape",
     "infer_block_conv_shape", "launch_fprop_nhwc_qi32", "launch_block_fprop_nhwc_qi32", "conv2d_s8",
-    "conv2d_s8_into", "conv2d_s8_add", "conv2d_s8_add_into", "maxpool_s8", "global_avgpool_s8", "conv_out_shape", "BMM_TRANSPOSE_NONE", "BMM_TRANSPOSE_YES", "bmm_matmul_i32", "bmm_s8",
+    "conv2d_s8_into", "conv2d_s8_add", "conv2d_s8_add_into", "conv2d_s8_plan", "maxpool_s8", "global_avgpool_s8", "conv_out_shape", "BMM_TRANSPOSE_NONE", "BMM_TRANSPOSE_YES", "bmm_matmul_i32", "bmm_s8",
     "bmm_s8_into", "B200QError", "last_path", "set_path_policy", "tc_launch_count",
 ]

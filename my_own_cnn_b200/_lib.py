@@ -79,6 +79,7 @@ def lib() -> ctypes.CDLL:
         "b200q_global_avgpool_s8": [vp, vp, i, i, i, i, vp],
         "b200q_bmm_s8": [vp, vp, vp, vp, vp, i, i, i, i, i, i, pepi, vp],
         "b200q_conv_out_shape": [i, i, i, i, i, i, pconv, POINTER(c_int), POINTER(c_int)],
+        "b200q_conv2d_s8_plan": [i, i, i, i, i, i, i, pconv, pepi, i, POINTER(c_int)],
         "b200q_device_error": [],
         "b200q_last_path": [],
         "b200q_fill_s8_uniform": [vp, c_size_t, c_uint64, c_uint64, i, i, vp],
@@ -126,5 +127,5 @@ EXPORTED_SYMBOLS = [
     "b200q_device_error", "b200q_last_path", "b200q_set_path_policy", "b200q_tc_launch_count",
     "b200q_fill_s8_uniform", "b200q_fill_i32_uniform", "b200q_fill_s8_table",
     "b200q_selftest_wait_timeout", "b200q_conv2d_s8_packed_noalloc", "b200q_noalloc_scratch_bytes",
-    "b200q_conv2d_s8_add", "b200q_maxpool_s8", "b200q_global_avgpool_s8",
+    "b200q_conv2d_s8_add", "b200q_maxpool_s8", "b200q_global_avgpool_s8", "b200q_conv2d_s8_plan",
 ]

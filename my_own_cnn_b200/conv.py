@@ -196,6 +196,16 @@ def conv_out_shape(h, w, c, r, s, k, p: Conv2DParams):
     return ho.value, wo.value
 
 
+def conv2d_s8_plan(n, h, w, c, r, s, k, p: Conv2DParams, epi: Epilogue, residual: bool = False) -> str:
+    """Kernel family conv2d_s8 (conv2d_s8_add when residual) would use for this conv with 16-byte
+    aligned tensors (a b200q_last_path name), decided on the host: no GPU needed."""
+    path = ctypes.c_int()
+    cp, ce = p.to_c(), epi.to_c()
+    _lib.check(_lib.lib().b200q_conv2d_s8_plan(n, h, w, c, r, s, k, ctypes.byref(cp), ctypes.byref(ce), int(residual),
+                                               ctypes.byref(path)))
+    return _lib.PATH_NAMES.get(path.value, "?")
+
+
 def conv2d_s8_into(y, x, w, bias, scale, n, h, wd, c, r, s, k, p: Conv2DParams, epi: Epilogue, stream=None) -> None:
     """Raw-pointer form: every tensor argument is a device tensor or address."""
     ce = epi.to_c()

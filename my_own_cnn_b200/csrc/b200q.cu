@@ -320,12 +320,12 @@ const int g_nacc_max = [] {
 // for reductions of 2048 and more or 4-byte outputs (config 4b +16 %); equal or slower for int8
 // outputs of shorter reductions, where both CTAs' epilogues gate every accumulator buffer.  The
 // caller encodes the B map with BN / 2 rows per box when this holds.
-bool want_pair(const DeviceState& st, const TcArgs& a) {
+bool want_pair(int sms, const TcArgs& a) {
   if (!g_pair || a.mode != 0 || a.a_major != 0 || a.b_major != 0 || a.conv_b || a.BN != 256) return false;
   if (a.num_kb * a.BK < g_pair_min_k && a.epi.out_kind == kOutS8) return false;
   const long long n_tiles = (a.N + a.BN - 1) / a.BN;
   const long long pair_tiles = static_cast<long long>(a.batch) * ((a.M + 2 * kTcBM - 1) / (2 * kTcBM)) * n_tiles;
-  return n_tiles >= 2 && pair_tiles >= st.sms;
+  return n_tiles >= 2 && pair_tiles >= sms;
 }
 
 int launch_tc(const DeviceState& st, const CUtensorMap& ma, const CUtensorMap& mb, TcArgs a, cudaStream_t stream) {
@@ -533,7 +533,7 @@ int run_packed_conv(const DeviceState& st, const int8_t* x, const int8_t* w, voi
   CUtensorMap ma, mb;
   rc = encode_tiled_3d(&ma, a_buf, static_cast<uint64_t>(kp), static_cast<uint64_t>(rows), 1, a.BK, kTcBM, a.BK);
   if (rc) return rc;
-  a.pair = want_pair(st, a);
+  a.pair = want_pair(st.sms, a);
   rc = encode_tiled_3d(&mb, w_buf, static_cast<uint64_t>(kp), static_cast<uint64_t>(g.k), 1, a.BK,
                        a.pair ? a.BN / 2 : a.BN, a.BK);
   if (rc) return rc;
@@ -636,6 +636,104 @@ int b200q_bmm_matmul_i32(const int32_t* A, const int32_t* B, int32_t* C, int bat
 }
 
 // Dispatch of the int8 conv (shared by the plain and the residual-add entry points).
+// Kernel family of a conv2d_s8 call (b200q_last_path codes), decided from the geometry, the
+// epilogue, pointer alignment and the SM count only, so that b200q_conv2d_s8_plan can predict it
+// without a GPU.  conv2d_s8_impl dispatches on the same decision.
+struct ConvRoute {
+  int path;            // 10 s2d row tiles, 9 row tiles, 2 tiled, 1 im2col, 8 tiled 2-SM, 7 packed, 4 depthwise, 3 generic
+  int s2d_r2, s2d_s2;  // path 10: taps of the stride-1 filter over the 2x2-block copy
+  int tc_bk;           // paths 1 / 2 / 8: K block bytes per ring stage
+};
+
+static int tc_pick_bk(int c) {
+  // The largest of 128/64/32 bytes whose channel padding (zero-filled by TMA past C) stays within
+  // 1/8 of C; 32 otherwise.
+  for (int bk : {128, 64}) {
+    const int padded = (c + bk - 1) / bk * bk;
+    if (padded * 8 <= c * 9) return bk;
+  }
+  return 32;
+}
+
+static ConvRoute route_conv_s8(const ConvGeom& g, int h, int w, int c, int r, int s, int k, bool x_aligned,
+                               bool w_aligned, bool y_aligned, bool epi_aligned, bool has_res, int out_kind, int sms) {
+  const bool out_aligned = y_aligned && epi_aligned;
+  (void)h;
+  (void)w;
+  (void)out_kind;
+  ConvRoute rt{3, 0, 0, 0};
+  const bool auto_policy = g_policy.load() == 0;
+  const long long M = static_cast<long long>(g.n) * g.ho * g.wo;
+  const size_t x_bytes = static_cast<size_t>(g.n) * g.h * g.w * c;
+  const bool vec_ptrs = x_aligned && w_aligned && out_aligned;
+  const bool is_1x1_plain = r == 1 && s == 1 && g.stride_h == 1 && g.stride_w == 1 && g.pad_h == 0 && g.pad_w == 0;
+  const bool corners_ok = g.pad_w <= 127 && g.pad_h <= 127 && g.pad_w - (s - 1) * g.dil_w >= -128 &&
+                          g.pad_h - (r - 1) * g.dil_h >= -128 && (s - 1) * g.dil_w <= 255 && (r - 1) * g.dil_h <= 255 &&
+                          g.stride_h <= 8 && g.stride_w <= 8;
+  // Space-to-depth row tiles for stride-2 convs of 1-4 channels (network stems).
+  if (g_s2d && auto_policy && g.groups == 1 && g.stride_h == 2 && g.stride_w == 2 && g.dil_h == 1 && g.dil_w == 1 &&
+      c >= 1 && c <= 4 && k <= 256 && M >= 1024 && M < (1ll << 31) && out_aligned && g.ho > 0 && g.wo > 0) {
+    auto fdiv2 = [](int v) { return v >= 0 ? v / 2 : -((1 - v) / 2); };
+    const int yoff = -((g.pad_h + 1) / 2), xoff = -((g.pad_w + 1) / 2);
+    const int r2 = fdiv2(r - 1 - g.pad_h) - yoff + 1;
+    const int s2 = (fdiv2(s - 1 - g.pad_w) - xoff + 1 + 1) / 2 * 2;
+    if (r2 >= 2 && r2 <= 4 && (s2 == 2 || s2 == 4) && g.wo + s2 - 1 <= 128) {
+      rt.path = 10;
+      rt.s2d_r2 = r2;
+      rt.s2d_s2 = s2;
+      return rt;
+    }
+  }
+  // Row tiles for 3x3 / stride 1 / pad 1 convs whose weights stay resident beside two window stages.
+  {
+    const int rt_P = g.wo + 1;
+    const int rt_bn = pick_bn(k, 0);
+    const long long rt_T0 = rt_P <= 128 ? 128 / rt_P : 1;
+    const long long rt_stage0 = ((rt_T0 + 3) * rt_P * c + (2 * rt_P + 2 + 128) * 16 + 1023) / 1024 * 1024;
+    const bool rt_fits = 9ll * c * rt_bn + 2 * rt_stage0 + kSmemReserve + 8 * 1024 <= kSmemLimit;
+    if (g_rowtile && auto_policy && g.groups == 1 && r == 3 && s == 3 && g.stride_h == 1 && g.stride_w == 1 &&
+        g.pad_h == 1 && g.pad_w == 1 && g.dil_h == 1 && g.dil_w == 1 && (c == 32 || c == 64 || c == 128) &&
+        k <= 256 && rt_P <= 128 && rt_fits && vec_ptrs && M < (1ll << 31)) {
+      rt.path = 9;
+      return rt;
+    }
+  }
+  // tcgen05 tiled (1x1 / s1 / p0) or im2col: C % 16 == 0; im2col only for activations of at least
+  // 128 KiB (a driver limitation on small im2col maps).
+  if (auto_policy && g.groups == 1 && c % 16 == 0 && vec_ptrs && M < (1ll << 31) &&
+      (is_1x1_plain || (corners_ok && x_bytes >= (128u << 10)))) {
+    rt.tc_bk = tc_pick_bk(c);
+    rt.path = is_1x1_plain ? 2 : 1;
+    if (is_1x1_plain) {
+      TcArgs a{};
+      a.mode = 0;
+      a.BK = rt.tc_bk;
+      a.BN = pick_bn(k, 0);
+      a.M = static_cast<int>(M);
+      a.N = k;
+      a.batch = 1;
+      a.conv_b = c % a.BK != 0;
+      a.num_kb = (c + a.BK - 1) / a.BK;
+      a.epi.out_kind = out_kind;
+      if (want_pair(sms, a)) rt.path = 8;
+    }
+    return rt;
+  }
+  // Low-channel / small convs: im2col pack into the stream's workspace, then tcgen05.
+  const int kp_packed = (r * s * c + 31) / 32 * 32;
+  if (auto_policy && g.groups == 1 && (c % 16 != 0 ? M >= 4096 : M >= 64) && M < (1ll << 31) && kp_packed <= 16384 &&
+      out_aligned) {
+    rt.path = 7;
+    return rt;
+  }
+  if (!has_res && g.groups == c && k == c && c % 8 == 0 && c <= 8 * 256 && r == 3 && s == 3 && M < (1ll << 31) &&
+      x_aligned && y_aligned) {
+    rt.path = 4;
+    return rt;
+  }
+  return rt;
+}
+
 static int conv2d_s8_impl(const int8_t* d_x, const int8_t* d_w, const int32_t* d_bias, const float* d_scale,
                    const int8_t* d_res, float res_scale, void* d_y, int n, int h, int w, int c, int r, int s, int k,
                    const b200q_conv_params* p, const b200q_epilogue* epi, void* stream) {
@@ -656,32 +754,22 @@ static int conv2d_s8_impl(const int8_t* d_x, const int8_t* d_w, const int32_t* d
   if (rc) return rc;
   cudaStream_t cs = as_stream(stream);
   const long long M = static_cast<long long>(n) * g.ho * g.wo;
-  const size_t x_bytes = static_cast<size_t>(n) * h * w * c;
-  const bool vec_ptrs = aligned16(d_x) && aligned16(d_w) && aligned16(d_y) && (!d_bias || aligned16(d_bias)) &&
-                        (!d_scale || aligned16(d_scale)) && (!d_res || aligned16(d_res));
   const bool is_1x1_plain = r == 1 && s == 1 && g.stride_h == 1 && g.stride_w == 1 && g.pad_h == 0 && g.pad_w == 0;
-  const bool corners_ok = g.pad_w <= 127 && g.pad_h <= 127 && g.pad_w - (s - 1) * g.dil_w >= -128 &&
-                          g.pad_h - (r - 1) * g.dil_h >= -128 && (s - 1) * g.dil_w <= 255 && (r - 1) * g.dil_h <= 255 &&
-                          g.stride_h <= 8 && g.stride_w <= 8;
-  // Small activations take the CUDA-core path: the im2col TMA mode is only used on tensors of
-  // at least 128 KiB (a driver limitation on small im2col maps).
-  const bool tc_ok = g_policy.load() == 0 && g.groups == 1 && c % 16 == 0 && vec_ptrs &&
-                     M < (1ll << 31) && (is_1x1_plain || (corners_ok && x_bytes >= (128u << 10)));
+  const bool epi_aligned = (!d_bias || aligned16(d_bias)) && (!d_scale || aligned16(d_scale)) &&
+                           (!d_res || aligned16(d_res));
+  const ConvRoute route = route_conv_s8(g, h, w, c, r, s, k, aligned16(d_x), aligned16(d_w), aligned16(d_y),
+                                        epi_aligned, d_res != nullptr, e.out_kind, st->sms);
   // Space-to-depth row tiles for stride-2 convs of 1-4 channels (network stems): the input is
   // rearranged into 16-channel pixels of 2x2 blocks, the weights into an R2 x S2 stride-1 filter
   // (S2 even: each K = 32 MMA slice covers two taps), and the conv runs as row tiles over it.
   // Replaces the im2col pack of the low-channel path: the rearranged input is 16/(4C) times the
   // input instead of R*S*C/C times.
-  if (g_s2d && g_policy.load() == 0 && g.groups == 1 && g.stride_h == 2 && g.stride_w == 2 && g.dil_h == 1 &&
-      g.dil_w == 1 && c >= 1 && c <= 4 && k <= 256 && M >= 1024 && M < (1ll << 31) && aligned16(d_y) &&
-      (!d_bias || aligned16(d_bias)) && (!d_scale || aligned16(d_scale)) && (!d_res || aligned16(d_res))) {
-    auto fdiv2 = [](int v) { return v >= 0 ? v / 2 : -((1 - v) / 2); };
+  if (route.path == 10) {
     const int yoff = -((g.pad_h + 1) / 2), xoff = -((g.pad_w + 1) / 2);
-    const int r2 = fdiv2(r - 1 - g.pad_h) - yoff + 1;
-    const int s2 = (fdiv2(s - 1 - g.pad_w) - xoff + 1 + 1) / 2 * 2;
+    const int r2 = route.s2d_r2, s2 = route.s2d_s2;
     const int P = g.wo + s2 - 1;
     const int bn = pick_bn(k, 0);
-    if (r2 >= 2 && r2 <= 4 && (s2 == 2 || s2 == 4) && P <= 128 && g.ho > 0 && g.wo > 0) {
+    {
       const int h2 = (h + 1) / 2, w2 = (w + 1) / 2;
       const size_t xs_bytes = (static_cast<size_t>(n) * h2 * w2 * 16 + 1023) / 1024 * 1024;
       const size_t ws_bytes = static_cast<size_t>(k) * r2 * s2 * 16;
@@ -744,15 +832,7 @@ static int conv2d_s8_impl(const int8_t* d_x, const int8_t* d_w, const int32_t* d
   // tile serves all nine taps (the im2col mode loads the window nine times, one row per pixel).
   const int rt_P = g.wo + 1;
   const int rt_bn = pick_bn(k, 0);
-  // Resident weights plus at least two window stages must fit in shared memory.
-  const long long rt_T0 = rt_P <= 128 ? 128 / rt_P : 1;
-  const long long rt_stage0 = ((rt_T0 + 3) * rt_P * c + (2 * rt_P + 2 + 128) * 16 + 1023) / 1024 * 1024;
-  const bool rt_fits = 9ll * c * rt_bn + 2 * rt_stage0 + kSmemReserve + 8 * 1024 <= kSmemLimit;
-  const bool rowtile_ok = g_rowtile && g_policy.load() == 0 && g.groups == 1 && r == 3 && s == 3 &&
-                          g.stride_h == 1 && g.stride_w == 1 && g.pad_h == 1 && g.pad_w == 1 && g.dil_h == 1 &&
-                          g.dil_w == 1 && (c == 32 || c == 64 || c == 128) && k <= 256 && rt_P <= 128 &&
-                          rt_fits && vec_ptrs && M < (1ll << 31);
-  if (rowtile_ok) {
+  if (route.path == 9) {
     TcArgs a{};
     a.mode = 2;
     a.BK = c;
@@ -786,18 +866,9 @@ static int conv2d_s8_impl(const int8_t* d_x, const int8_t* d_w, const int32_t* d
     g_last_path = 9;
     return launch_tc(*st, ma, mb, a, cs);
   }
-  if (tc_ok) {
+  if (route.path == 1 || route.path == 2 || route.path == 8) {
     TcArgs a{};
-    // K block per stage: the largest of 128/64/32 bytes whose channel padding (zero-filled by TMA
-    // past C) stays within 1/8 of C; 32 otherwise.
-    a.BK = 32;
-    for (int bk : {128, 64}) {
-      const int padded = (c + bk - 1) / bk * bk;
-      if (padded * 8 <= c * 9) {
-        a.BK = bk;
-        break;
-      }
-    }
+    a.BK = route.tc_bk;
     a.cchunks = (c + a.BK - 1) / a.BK;
     a.BN = pick_bn(k, 0);
     a.M = static_cast<int>(M);
@@ -816,7 +887,7 @@ static int conv2d_s8_impl(const int8_t* d_x, const int8_t* d_w, const int32_t* d
     const int kdim = r * s * c;
     a.mode = is_1x1_plain ? 0 : 1;
     a.num_kb = is_1x1_plain ? a.cchunks : r * s * a.cchunks;
-    a.pair = want_pair(*st, a);
+    a.pair = route.path == 8;
     if (a.conv_b)  // weights as {C, R*S, K}: a box of BK channels x 1 tap x BN output channels
       rc = encode_tiled_3d(&mb, d_w, static_cast<uint64_t>(c), static_cast<uint64_t>(r * s),
                            static_cast<uint64_t>(k), a.BK, 1, a.BK, a.BN);
@@ -847,10 +918,7 @@ static int conv2d_s8_impl(const int8_t* d_x, const int8_t* d_w, const int32_t* d
   // (tc_ok was false here, so a C % 16 == 0 conv reaching this point is one im2col TMA cannot take.)
   const int kp_packed = (r * s * c + 31) / 32 * 32;
   // Also taken by groups == 1 convs the im2col TMA cannot read (activations < 128 KiB, corner limits).
-  if (g_policy.load() == 0 && g.groups == 1 && (c % 16 != 0 ? M >= 4096 : M >= 64) && M < (1ll << 31) &&
-      kp_packed <= 16384 &&
-      aligned16(d_y) && (!d_bias || aligned16(d_bias)) && (!d_scale || aligned16(d_scale)) &&
-      (!d_res || aligned16(d_res))) {
+  if (route.path == 7) {
     void* ws = nullptr;
     rc = get_workspace(packed_scratch_bytes(M, k, kp_packed), cs, &ws);
     if (rc) return rc;
@@ -858,9 +926,7 @@ static int conv2d_s8_impl(const int8_t* d_x, const int8_t* d_w, const int32_t* d
     return run_packed_conv(*st, d_x, d_w, d_y, g, e, static_cast<int8_t*>(ws), cs);
   }
   const size_t total = static_cast<size_t>(M) * k;
-  if (!d_res && g.groups == c && k == c && c % 8 == 0 && c <= 8 * 256 && r == 3 && s == 3 && M < (1ll << 31) &&
-      aligned16(d_x) &&
-      aligned16(d_y)) {
+  if (route.path == 4) {
     const int groups8 = c / 8;
     const int lanes = 256 / groups8;
     g_last_path = 4;
@@ -903,6 +969,28 @@ static int conv2d_s8_impl(const int8_t* d_x, const int8_t* d_w, const int32_t* d
   conv_s8_generic_kernel<<<grid_for(total, 256, st->sms), 256, 0, cs>>>(d_x, d_w, d_y, g, e, dp4a);
   g_last_path = 3;
   return check_launch("conv_s8_generic_kernel launch");
+}
+
+int b200q_conv2d_s8_plan(int n, int h, int w, int c, int r, int s, int k, const b200q_conv_params* p,
+                         const b200q_epilogue* epi, int has_residual, int* path) {
+  if (!path) return fail(B200Q_ERR_INVALID_ARG, "null argument");
+  ConvGeom g;
+  int rc = conv_geom(n, h, w, c, r, s, k, p, 1, 1, &g);
+  if (rc) return rc;
+  if (!epi) return fail(B200Q_ERR_INVALID_ARG, "epilogue descriptor is null");
+  if (epi->out_kind < 0 || epi->out_kind > 2) return fail(B200Q_ERR_INVALID_ARG, "bad out_kind %d", epi->out_kind);
+  if (has_residual && epi->out_kind != B200Q_OUT_S8)
+    return fail(B200Q_ERR_INVALID_ARG, "a residual add needs int8 outputs");
+  int sms = 148;
+  int dev = 0, count = 0;
+  if (cudaGetDeviceCount(&count) == cudaSuccess && count > 0 && cudaGetDevice(&dev) == cudaSuccess) {
+    int v = 0;
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && v > 0) sms = v;
+  } else {
+    cudaGetLastError();  // no device here: clear the sticky error of the query
+  }
+  *path = route_conv_s8(g, h, w, c, r, s, k, true, true, true, true, has_residual != 0, epi->out_kind, sms).path;
+  return B200Q_OK;
 }
 
 int b200q_conv2d_s8(const int8_t* d_x, const int8_t* d_w, const int32_t* d_bias, const float* d_scale, void* d_y,
@@ -958,7 +1046,7 @@ int b200q_bmm_s8(const int8_t* A, const int8_t* B, const int32_t* d_bias, const 
     else
       rc = encode_tiled_3d(&ma, A, (uint64_t)M, (uint64_t)K, (uint64_t)batch, kTcBM, a.BK, 128);
     if (rc) return rc;
-    a.pair = want_pair(*st, a);
+    a.pair = want_pair(st->sms, a);
     if (tb)
       rc = encode_tiled_3d(&mb, B, (uint64_t)K, (uint64_t)N, (uint64_t)batch, a.BK, a.pair ? a.BN / 2 : a.BN, 128);
     else

@@ -122,6 +122,10 @@ def _conv_case(n, h, w, c, r, s, k, p, seed, epi_kind="all", groups=1):
             torch.cuda.synchronize()
             np.testing.assert_allclose(y.cpu().numpy(), oracle.dequant_f32(acc, bias, scale), rtol=FP32_RTOL, atol=0)
         paths.add(b2q.last_path())
+        # the host-side plan (no launch) names the kernel family the call dispatched to
+        epi = {"s32": b2q.Epilogue.int32(), "s8": b2q.Epilogue.int8(), "relu": b2q.Epilogue.int8(relu6_q=97),
+               "f32": b2q.Epilogue.fp32()}[kind]
+        assert b2q.conv2d_s8_plan(n, h, w, c, r, s, k, p, epi) == b2q.last_path(), kind
     return paths
 
 

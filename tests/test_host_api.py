@@ -155,3 +155,35 @@ def test_new_entry_points_validate_arguments():
     assert L.b200q_conv2d_s8_add(None, None, None, None, None, 1.0, None, 1, 8, 8, 16, 1, 1, 16,
                                  ctypes.byref(cp), ctypes.byref(ce), None) == 1
     assert b"residual" in L.b200q_last_error()
+
+
+def test_conv_plan_dispatch_tables():
+    """The host-side dispatch decision (b200q_conv2d_s8_plan, the same function the GPU dispatch
+    uses) for the BASELINE workloads: network stems on space-to-depth row tiles, stride-1 3x3
+    convs with C <= 128 on row tiles, other 3x3 convs on im2col, 1x1 convs tiled (config 4's long
+    reduction on 2-SM tiles), depthwise on CUDA cores, C = 24 expands packed."""
+    from collections import Counter
+
+    import my_own_cnn_b200 as b2q
+    from my_own_cnn_b200 import nets
+
+    E, P = b2q.Epilogue, b2q.Conv2DParams
+    assert b2q.conv2d_s8_plan(1, 56, 56, 64, 3, 3, 64, P(), E.int8()) == "tcgen05-rowtile"   # config 1 / smoke
+    assert b2q.conv2d_s8_plan(512, 14, 14, 1024, 1, 1, 2048, P(0, 0), E.int8()) == "tcgen05-tiled"
+    assert b2q.conv2d_s8_plan(512, 14, 14, 2048, 1, 1, 512, P(0, 0), E.int8()) == "tcgen05-tiled-2sm"
+    want = {"resnet50": {"tcgen05-s2d": 1, "tcgen05-tiled": 33, "tcgen05-rowtile": 6, "tcgen05-im2col": 13},
+            "mobilenetv2": {"tcgen05-s2d": 1, "cuda-core-depthwise": 17, "tcgen05-tiled": 32, "tcgen05-packed": 2}}
+    for net, batch in (("resnet50", 256), ("mobilenetv2", 512)):
+        got = Counter(b2q.conv2d_s8_plan(batch, sp.h, sp.w, sp.c, sp.r, sp.r, sp.k, sp.params(), sp.epilogue())
+                      for sp in nets.NETS[net]())
+        assert dict(got) == want[net], (net, dict(got))
+    # residual adds never take the depthwise kernel; forced CUDA-core policy
+    assert b2q.conv2d_s8_plan(2, 20, 20, 48, 3, 3, 48, P(groups=48), E.int8(), residual=True) == "cuda-core-generic"
+    b2q.set_path_policy(1)
+    try:
+        assert b2q.conv2d_s8_plan(1, 56, 56, 64, 3, 3, 64, P(), E.int8()) == "cuda-core-generic"
+        assert b2q.conv2d_s8_plan(2, 20, 20, 48, 3, 3, 48, P(groups=48), E.int8()) == "cuda-core-depthwise"
+    finally:
+        b2q.set_path_policy(0)
+    with pytest.raises(RuntimeError, match="residual add needs int8"):
+        b2q.conv2d_s8_plan(1, 8, 8, 16, 1, 1, 16, P(0, 0), E.int32(), residual=True)
