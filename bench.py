@@ -95,6 +95,14 @@ class ClockSampler:
 
 # ---------------------------------------------------------------------------- our arm
 
+def headline_config(world: int) -> dict:
+    """`config` of the headline line; both arms print exactly this dict."""
+    return {"workload": "config4 pointwise 1x1 pair: b512 14x14 C1024->K2048 then C2048->K512, "
+                        "bias+per-channel requant int8 epilogue",
+            "global_batch": BATCH * world, "per_gpu_batch": BATCH, "parallelism": f"dp{world} (batch shards)",
+            "l2": "flushed between timed steps (256 MiB write outside the events)"}
+
+
 def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     import torch
     import torch.distributed as dist
@@ -160,6 +168,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     launches = b2q.tc_launch_count() - launches0
     t1 = [a.elapsed_time(b) for a, b, _ in ev]
     t2 = [b.elapsed_time(c) for _, b, c in ev]
+    sustained = sustained_window(step, x, flush, stream, barrier, rank, args.sustain_s)
     step_ms = sum(t1) / len(t1) + sum(t2) / len(t2)
     total_ms = sum(t1) + sum(t2)
     if _lib.lib().b200q_device_error() != 0:
@@ -196,6 +205,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     step_ms = total_ms / args.steps
     chk = torch.cat([checksum(y2), checksum(y1)])
     checksums = [g.tolist() for g in gather_tensors(chk)]
+    strong = strong_scaling(args, x, w1, w2, b1, b2, s1, s2, y1, y2, flush, stream, barrier, rank, world) \
+        if world > 1 else None
     if rank != 0:
         return None
 
@@ -227,10 +238,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         "vs_baseline": None,
         "dtype": "s8xs8->s32",
         "data": "synthetic (seeded splitmix64, random-init int8 weights)",
-        "config": {"workload": "config4 pointwise 1x1 pair: b512 14x14 C1024->K2048 then C2048->K512, "
-                               "bias+per-channel requant int8 epilogue",
-                   "global_batch": BATCH * world, "per_gpu_batch": BATCH, "parallelism": f"dp{world} (batch shards)",
-                   "l2": "flushed between timed steps (256 MiB write outside the events)"},
+        "config": headline_config(world),
         "tops_per_gpu": round(tops_per_gpu, 1),
         "frac_of_int8_peak": round(tops_per_gpu / int8_peak_tops, 4),
         "layer_ms": [round(mean1, 5), round(mean2, 5)],
@@ -244,11 +252,81 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         "gpu_launches": int(launches),
         "clocks": clocks,
         "wall_s_timed": round(wall, 3),
+        "sustained": sustained,
+        **({"strong": strong} if strong else {}),
         "verify": {"checksums_y2_y1_per_rank": checksums},
     }
     if world == 1 and not args.no_cpu_baseline:
         out["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
     return out
+
+
+def strong_scaling(args, x, w1, w2, b1, b2, s1, s2, y1, y2, flush, stream, barrier, rank: int, world: int) -> dict:
+    """Strong scaling of the headline: one global batch of 512 images split over the ranks
+    (shard_range: contiguous, balanced), the same two layers, max over ranks of the device time."""
+    import torch
+
+    import my_own_cnn_b200 as b2q
+    from my_own_cnn_b200.shard import max_over_ranks, shard_range
+
+    (c1, k1), (c2, k2) = LAYERS
+    start, cnt = shard_range(BATCH, rank, world)
+    p = b2q.Conv2DParams(0, 0, 1, 1, 1, 1, 1)
+    epi = b2q.Epilogue.int8()
+    xs, y1s, y2s = x[:cnt], y1[:cnt], y2[:cnt]
+
+    def step():
+        b2q.conv2d_s8_into(y1s, xs, w1, b1, s1, cnt, HW, HW, c1, 1, 1, k1, p, epi)
+        b2q.conv2d_s8_into(y2s, y1s, w2, b2, s2, cnt, HW, HW, c2, 1, 1, k2, p, epi)
+
+    for _ in range(args.warmup):
+        step()
+    paths = b2q.last_path()
+    barrier()
+    torch.cuda.synchronize()
+    ms = _timed_ms(step, args.steps, flush, stream)
+    barrier()
+    (total,) = max_over_ranks([sum(ms)], device=x.device)
+    step_ms = total / args.steps
+    return {"scaling": "strong", "global_batch": BATCH, "per_gpu_batch": f"{BATCH // world}-{-(-BATCH // world)}",
+            "value": round(BATCH / (step_ms * 1e-3), 1), "unit": "images/s", "ms_per_step": round(step_ms, 5),
+            "layer2_path_rank0": paths}
+
+
+def sustained_window(step, x, flush, stream, barrier, rank: int, seconds: float) -> dict | None:
+    """The headline step back to back for at least `seconds` (L2 flushed between steps, outside the
+    events), with the clocks sampled over the whole window: a long enough record to show the clocks
+    the headline's short timed region ran at."""
+    import torch
+
+    if seconds <= 0:
+        return None
+    sampler = ClockSampler()
+    if rank == 0:
+        sampler.start()
+    barrier()
+    torch.cuda.synchronize()
+    n, dev_ms, t0 = 0, 0.0, time.perf_counter()
+    while time.perf_counter() - t0 < seconds:
+        evs = []
+        for i in range(50):
+            flush.fill_(i & 0x7F)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            step(x)
+            b.record(stream)
+            evs.append((a, b))
+        torch.cuda.synchronize()
+        dev_ms += sum(a.elapsed_time(b) for a, b in evs)
+        n += len(evs)
+    barrier()
+    clocks = sampler.stop() if rank == 0 else None
+    from my_own_cnn_b200.shard import max_over_ranks
+
+    (dev_ms,) = max_over_ranks([dev_ms], device=x.device)
+    return {"steps": n, "device_s": round(dev_ms / 1e3, 3), "wall_s": round(time.perf_counter() - t0, 2),
+            "ms_per_step": round(dev_ms / n, 5), "images_per_s_per_gpu": round(BATCH / (dev_ms / n * 1e-3), 1),
+            "clocks": clocks}
 
 
 # ---------------------------------------------------------------------- CPU baseline
@@ -332,13 +410,74 @@ def run_reference(args) -> dict:
         "metric": METRIC, "value": round(val, 3), "unit": "images/s", "n_gpus": args.gpus, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "s8xs8->s32", "data": "synthetic (seeded splitmix64)",
-        "config": {"workload": "config4 pointwise 1x1 pair: b512 14x14 C1024->K2048 then C2048->K512, "
-                               "bias+per-channel requant int8 epilogue", "per_step_sample_images": images},
+        "config": headline_config(args.gpus),
         "impl": "reference",
         "cpu_baseline": {"value": round(val, 3), "unit": "images/s", "cores": threads, "kind": kind,
-                         "sample": f"{images} images per step, images split over {threads} threads"},
+                         "sample": f"{images} of the {BATCH} images of the workload per step, images split over "
+                                   f"{threads} threads; src/cpu_ref.cpp cpu_fprop_nhwc_qi32 + CPU requant"},
         "e2e": {"value": round(val, 3), "unit": "images/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+
+
+def run_reference_gpu(args) -> list[dict]:
+    """Secondary baseline: the reference's own CUDA quantized conv (src/cuda_kernels.cu:1336-1392:
+    per-call cudaMalloc/cudaFree, im2col to int32, SIMT int32 GEMM, unpack; compiled unmodified into
+    oracle/_ref/libref_gpu.so) against this library's drop-in for the same entry point
+    (launch_fprop_nhwc_qi32, float codes, S5 zero points 0) and its int8 entry, on BASELINE
+    configs 1 and 4.  One JSON record per case, with an identical-int32 check."""
+    import ctypes
+
+    import torch
+
+    import my_own_cnn_b200 as b2q
+    from my_own_cnn_b200 import synth
+
+    lib = ROOT / "oracle" / "_ref" / "libref_gpu.so"
+    if not lib.exists():
+        return [{"impl": "reference-gpu", "unavailable": "oracle/_ref/libref_gpu.so was not built"}]
+    ref = ctypes.CDLL(str(lib))
+    ref.refgpu_fprop_qi32_s5.argtypes = [ctypes.c_void_p] * 3 + [ctypes.c_int] * 9 + [ctypes.c_void_p] * 2
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    stream = torch.cuda.current_stream()
+    flush = torch.empty(256 << 20, dtype=torch.int8, device=dev)
+    cases = [("config1 3x3 N1 56x56 C64->K64", 1, 56, 56, 64, 3, 64, 1, 1),
+             ("config4a 1x1 b512 14x14 C1024->K2048", 512, 14, 14, 1024, 1, 2048, 0, 1),
+             ("config4b 1x1 b512 14x14 C2048->K512", 512, 14, 14, 2048, 1, 512, 0, 1)]
+    out = []
+    for name, n, h, w, c, r, k, pad, st in cases:
+        x8 = synth.fill_s8_uniform(torch.empty((n, h, w, c), dtype=torch.int8, device=dev), SEED, 1)
+        w8 = synth.fill_s8_uniform(torch.empty((k, r, r, c), dtype=torch.int8, device=dev), SEED, 2)
+        xf, wf = x8.float(), w8.float()
+        p = b2q.Conv2DParams(pad, pad, st, st, 1, 1, 1)
+        ho, wo = b2q.conv_out_shape(h, w, c, r, r, k, p)
+        y_ref = torch.empty((n, ho, wo, k), dtype=torch.int32, device=dev)
+        y_drop = torch.empty_like(y_ref)
+        y_s8 = torch.empty_like(y_ref)
+        qp_in = b2q.qparams_to_device([b2q.QuantizationParametersS5(0, 31, 1.0)] * n)
+        qp_f = b2q.qparams_to_device([b2q.QuantizationParametersS5(0, 31, 1.0)])
+
+        def run_ref():
+            assert ref.refgpu_fprop_qi32_s5(xf.data_ptr(), wf.data_ptr(), y_ref.data_ptr(), n, h, w, c, r, r, k, pad,
+                                            st, qp_in.data_ptr(), qp_f.data_ptr()) == 0
+
+        run_drop = lambda: b2q.launch_fprop_nhwc_qi32(xf, wf, y_drop, n, h, w, c, r, r, k, p, qp_in, qp_f,
+                                                      qtype=b2q.DataType.LinQuantS5)
+        run_s8 = lambda: b2q.conv2d_s8_into(y_s8, x8, w8, None, None, n, h, w, c, r, r, k, p, b2q.Epilogue.int32())
+        run_ref(); run_drop(); drop_path = b2q.last_path(); run_s8(); s8_path = b2q.last_path()
+        t_ref = statistics.median(_timed_ms(run_ref, 3, flush, stream))
+        t_drop = statistics.median(_timed_ms(run_drop, 20, flush, stream))
+        t_s8 = statistics.median(_timed_ms(run_s8, 20, flush, stream))
+        ops = 2 * n * ho * wo * k * r * r * c
+        out.append({"impl": "reference-gpu", "case": name, "reference_gpu_ms": round(t_ref, 4),
+                    "dropin_qi32_ms": round(t_drop, 4), "dropin_path": drop_path,
+                    "int8_entry_ms": round(t_s8, 4), "int8_entry_path": s8_path,
+                    "dropin_speedup": round(t_ref / t_drop, 1), "int8_speedup": round(t_ref / t_s8, 1),
+                    "dropin_tops": round(ops / t_drop / 1e9, 1),
+                    "identical_int32": bool(torch.equal(y_ref, y_drop) and torch.equal(y_ref, y_s8))})
+        del xf, wf, y_ref, y_drop, y_s8
+        torch.cuda.empty_cache()
+    return out
 
 
 # ------------------------------------------------------------------ other BASELINE configs
@@ -613,13 +752,246 @@ def run_bmm(args, rank: int, world: int, local_rank: int) -> dict | None:
                          "frac_of_int8_peak": round(ops / t8 / 1e9 / (2 * peaks["bf16_tflops"]), 4)}}
 
 
+# ------------------------------------------------------------- per-config sub-records (N = 1)
+
+SUB_KEEP = ("value", "unit", "ms_per_step", "steps", "warmup", "tops_per_gpu", "frac_of_int8_peak", "by_path",
+            "roofline", "roofline_depthwise", "slowest_layers", "cpu_baseline", "int32_out", "int8_out", "config",
+            "gpu_launches", "clocks")
+
+
+def _trim(rec: dict) -> dict:
+    out = {k: rec[k] for k in SUB_KEEP if k in rec}
+    if "config" in out:
+        out["workload"] = out.pop("config").get("workload")
+    return out
+
+
+def _timed_ms(fn, steps: int, flush, stream) -> list[float]:
+    """Per-step CUDA-event times of fn on `stream`, L2 flushed between steps outside the events."""
+    import torch
+
+    out = []
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for i, (a, b) in enumerate(evs):
+        flush.fill_(i & 0x7F)
+        a.record(stream)
+        fn()
+        b.record(stream)
+    torch.cuda.synchronize()
+    return [a.elapsed_time(b) for a, b in evs]
+
+
+def _roof(ops: float, nbytes: float, ms: float, peaks: dict) -> dict:
+    """Binding roof of one launch: the slower of the int8 tensor time and the HBM time."""
+    int8_peak = 2.0 * peaks["bf16_tflops"]
+    t_tensor = ops / (int8_peak * 1e12) * 1e3
+    t_hbm = nbytes / (peaks["hbm_gbs"] * 1e9) * 1e3
+    bound = "tensor" if t_tensor >= t_hbm else "hbm"
+    if bound == "tensor":
+        ach, peak, unit = ops / (ms * 1e-3) / 1e12, int8_peak, "TOP/s"
+    else:
+        ach, peak, unit = nbytes / (ms * 1e-3) / 1e9, peaks["hbm_gbs"], "GB/s"
+    return {"bound": bound, "achieved": round(ach, 2), "peak": round(peak, 1), "unit": unit,
+            "frac": round(ach / peak, 4), "roof_ms": round(max(t_tensor, t_hbm), 5),
+            "peak_source": peaks["source"]}
+
+
+def run_config1(args, dev) -> dict:
+    """one conv, 1x56x56x64, 3x3 pad 1, K = 64, bias + per-channel requant to int8.
+    Also the reference-API drop-in (launch_fprop_nhwc_qi32, float codes, U8 zero points) at the same
+    geometry, and both back to back without an L2 flush (the latency a caller sees in a loop)."""
+    import numpy as np
+    import torch
+
+    import my_own_cnn_b200 as b2q
+    from my_own_cnn_b200 import synth
+
+    n, h, w, c, k = 1, 56, 56, 64, 64
+    p = b2q.Conv2DParams()
+    x = synth.fill_s8_uniform(torch.empty((n, h, w, c), dtype=torch.int8, device=dev), SEED, 201)
+    wt = synth.fill_s8_uniform(torch.empty((k, 3, 3, c), dtype=torch.int8, device=dev), SEED, 202)
+    b = synth.fill_i32_uniform(torch.empty(k, dtype=torch.int32, device=dev), SEED, 203, -2**15, 2**15)
+    sc = torch.from_numpy(synth.scales_f32(k, SEED, 204)).to(dev)
+    y = torch.empty((n, h, w, k), dtype=torch.int8, device=dev)
+    epi = b2q.Epilogue.int8()
+    stream = torch.cuda.current_stream()
+    flush = torch.empty(256 << 20, dtype=torch.int8, device=dev)
+    run = lambda: b2q.conv2d_s8_into(y, x, wt, b, sc, n, h, w, c, 3, 3, k, p, epi)
+    for _ in range(args.warmup):
+        run()
+    path = b2q.last_path()
+    steps = max(args.steps, 20)
+    ms = statistics.median(_timed_ms(run, steps, flush, stream))
+    hot = _timed_ms(lambda: [run() for _ in range(100)], 3, flush, stream)
+    hot_us = min(hot) * 10.0
+    # drop-in: U8 float codes (x + 127 in [0, 254]), per-image zero point 91, filter zero point 37
+    xf = (x.float() + 127.0).contiguous()
+    wf = (wt.float() + 127.0).contiguous()
+    y32 = torch.empty((n, h, w, k), dtype=torch.int32, device=dev)
+    qin = b2q.qparams_to_device([b2q.QuantizationParametersU8(91, 0.25)])
+    qf = b2q.qparams_to_device([b2q.QuantizationParametersU8(37, 0.5)])
+    drop = lambda: b2q.launch_fprop_nhwc_qi32(xf, wf, y32, n, h, w, c, 3, 3, k, p, qin, qf)
+    for _ in range(args.warmup):
+        drop()
+    dpath = b2q.last_path()
+    dms = statistics.median(_timed_ms(drop, steps, flush, stream))
+    dhot = min(_timed_ms(lambda: [drop() for _ in range(100)], 3, flush, stream)) * 10.0
+    peaks = load_peaks()
+    ops = 2 * n * h * w * k * 9 * c
+    nbytes = n * h * w * c + k * 9 * c + n * h * w * k + 8 * k
+    rec = {"workload": "config1 conv 1x56x56x64 3x3/1 p1 K64, bias+per-channel requant int8",
+           "value": round(1.0 / (ms * 1e-3), 1), "unit": "images/s", "ms_per_step": round(ms, 5), "steps": steps,
+           "path": path, "tops": round(ops / ms / 1e9, 2), "back_to_back_us": round(hot_us, 2),
+           "roofline": _roof(ops, nbytes, ms, peaks),
+           "note": "M = 3136 rows: 25 row tiles of 128 on 148 SMs; latency-bound (roof_ms is the tensor/HBM roof)",
+           "dropin_qi32": {"entry": "launch_fprop_nhwc_qi32 (U8 float codes, zero points 91 / 37)", "path": dpath,
+                           "ms_per_step": round(dms, 5), "back_to_back_us": round(dhot, 2),
+                           "roofline": _roof(ops, 4 * (n * h * w * c + k * 9 * c + n * h * w * k), dms, peaks)}}
+    if not args.no_cpu_baseline:
+        from oracle import oracle
+
+        xs, ws_ = x.cpu().numpy().astype(np.float32), wt.cpu().numpy().astype(np.float32)
+        bh, sh = b.cpu().numpy(), sc.cpu().numpy()
+        a = oracle.conv_args(n, h, w, c, 3, 3, k)
+        use_ref = oracle.ref_available()
+        reps, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < min(args.cpu_seconds, 5.0) or reps == 0:
+            acc = (oracle.ref_conv_qi32(a, 1, xs, ws_, np.zeros(1, np.int32), 0, False) if use_ref
+                   else oracle.conv_s8(a, x.cpu().numpy(), wt.cpu().numpy()))
+            oracle.requant_s8(acc, bh, sh)
+            reps += 1
+        dt = time.perf_counter() - t0
+        rec["cpu_baseline"] = {"value": round(reps / dt, 3), "unit": "images/s", "cores": 1,
+                               "kind": "reference" if use_ref else "port",
+                               "sample": f"the whole conv (one image) {reps} times; src/cpu_ref.cpp cpu_fprop_nhwc_qi32 "
+                                         "+ CPU requant, one thread (one image does not split over images)"}
+    return rec
+
+
+def net_cpu_baseline(name: str, batch: int, budget_s: float) -> dict:
+    """Configs 3 / 5 per layer on the host cores: the reference's cpu_fprop_nhwc_qi32 (float codes,
+    zero points 0) + the CPU requant for every layer of the table, images split over threads."""
+    import numpy as np
+
+    from my_own_cnn_b200 import nets
+    from oracle import oracle
+
+    threads = oracle.cpu_threads()
+    specs = nets.NETS[name]()
+    use_ref = oracle.ref_available()
+    rng = np.random.default_rng(7)
+
+    def run(images: int) -> float:
+        total = 0.0
+        for sp in specs:
+            x = rng.integers(0, 128, size=(images, sp.h, sp.w, sp.c)).astype(np.int8)
+            w = rng.integers(-127, 128, size=(sp.k, sp.r, sp.r, sp.c // sp.groups)).astype(np.int8)
+            b = rng.integers(-2**15, 2**15, size=sp.k).astype(np.int32)
+            s = np.full(sp.k, 5e-4, np.float32)
+            a = oracle.conv_args(images, sp.h, sp.w, sp.c, sp.r, sp.r, sp.k, sp.pad, sp.pad, sp.stride, sp.stride,
+                                 groups=sp.groups)
+            xf, wf = x.astype(np.float32), w.astype(np.float32)
+            t0 = time.perf_counter()
+            acc = oracle.ref_conv_qi32_threaded(a, xf, wf, threads) if use_ref else oracle.conv_s8(a, x, w, threads)
+            oracle.requant_s8(acc, b, s, 0, 0, 127)
+            total += time.perf_counter() - t0
+        return total
+
+    t_probe = run(1)
+    images = threads
+    if t_probe * images / threads * 1.2 > budget_s:
+        images = max(1, int(budget_s / t_probe))
+    dt = run(images)
+    return {"value": round(images / dt, 3), "unit": "images/s", "cores": threads,
+            "kind": "reference" if use_ref else "port",
+            "sample": f"{images} images (of {batch}) through every conv of the {name} table, fresh inputs per layer; "
+                      f"src/cpu_ref.cpp cpu_fprop_nhwc_qi32 on float codes + CPU requant, images split over "
+                      f"{threads} threads", "seconds": round(dt, 2)}
+
+
+def bmm_cpu_baseline(budget_s: float) -> dict:
+    import numpy as np
+
+    from oracle import oracle
+
+    threads = oracle.cpu_threads()
+    M = 1024
+    rng = np.random.default_rng(3)
+    A = rng.integers(-127, 128, size=(1, M, M)).astype(np.int8)
+    B = rng.integers(-127, 128, size=(1, M, M)).astype(np.int8)
+    t0 = time.perf_counter()
+    oracle.bmm_s8(A, B, 1, M, M, M, 0, 0, 1)
+    t_one = time.perf_counter() - t0
+    items = max(threads, min(64, int(budget_s / max(t_one, 1e-3)) * threads // threads))
+    items = max(threads, items // threads * threads)
+    A = rng.integers(-127, 128, size=(items, M, M)).astype(np.int8)
+    B = rng.integers(-127, 128, size=(items, M, M)).astype(np.int8)
+    t0 = time.perf_counter()
+    oracle.bmm_s8(A, B, items, M, M, M, 0, 0, threads)
+    dt = time.perf_counter() - t0
+    ops = 2.0 * items * M ** 3
+    return {"value": round(ops / dt / 1e12, 5), "unit": "TOP/s", "cores": threads, "kind": "port",
+            "sample": f"{items} of the 64 batch items (int32 out), restated CPU GEMM (bmm.h:9-29) over {threads} "
+                      f"threads", "seconds": round(dt, 2)}
+
+
+def run_subconfigs(args, dev) -> dict:
+    """Every other BASELINE config at N = 1, each as a sub-record of the default line."""
+    import copy
+
+    import torch
+
+    sub_steps = max(5, min(args.steps, 20))
+    out = {}
+
+    def sub(config: str, fn):
+        a = copy.copy(args)
+        a.config, a.steps, a.warmup, a.batch, a.layers = config, sub_steps, 3, 0, ""
+        a.cpu_seconds = args.sub_cpu_seconds
+        a.no_cpu_baseline = True
+        try:
+            rec = _trim(fn(a, 0, 1, dev.index or 0))
+        finally:
+            torch.cuda.synchronize()
+            torch.cuda.empty_cache()
+        return rec
+
+    a1 = copy.copy(args)
+    a1.cpu_seconds = args.sub_cpu_seconds
+    out["config1"] = run_config1(a1, dev)
+    torch.cuda.empty_cache()
+    out["config2_bmm"] = sub("bmm", run_bmm)
+    out["config3_resnet50_layers"] = sub("resnet50", run_net)
+    out["config3_resnet50_chain"] = sub("resnet50-chain", run_chain)
+    out["config5_mobilenetv2_layers"] = sub("mobilenetv2", run_net)
+    out["config5_mobilenetv2_chain"] = sub("mobilenetv2-chain", run_chain)
+    if not args.no_cpu_baseline:
+        from my_own_cnn_b200 import nets
+
+        out["config2_bmm"]["cpu_baseline"] = bmm_cpu_baseline(args.sub_cpu_seconds)
+        out["config3_resnet50_layers"]["cpu_baseline"] = net_cpu_baseline("resnet50", 256, args.sub_cpu_seconds)
+        out["config5_mobilenetv2_layers"]["cpu_baseline"] = net_cpu_baseline("mobilenetv2", 512, args.sub_cpu_seconds)
+        model_dev = torch.device("cuda", dev.index or 0)
+        for key, name in (("config3_resnet50_chain", "resnet50"), ("config5_mobilenetv2_chain", "mobilenetv2")):
+            out[key]["cpu_baseline"] = chain_cpu_baseline(nets.ChainedNet(name, SEED, model_dev), args.sub_cpu_seconds)
+            torch.cuda.empty_cache()
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
-    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference", "reference-gpu"],
+                    help="reference = the reference's CPU path (the reference arm); reference-gpu = the reference's "
+                         "own CUDA quantized conv against this library's drop-in (secondary baseline)")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--sustain-s", type=float, default=1.5,
+                    help="seconds of back-to-back headline steps with clocks sampled (0 = off)")
+    ap.add_argument("--sub-cpu-seconds", type=float, default=6.0, help="CPU budget of each sub-record's baseline")
+    ap.add_argument("--no-subconfigs", action="store_true",
+                    help="N=1: skip the per-config sub-records (configs 1, 2, 3, 5) of the default line")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--chunk", type=int, default=64, help="images per chunk of the e2e pipeline")
     ap.add_argument("--config", default="pointwise",
@@ -640,6 +1012,12 @@ def main():
             return
         print(json.dumps(run_reference(args)), flush=True)
         return
+    if args.impl == "reference-gpu":
+        if rank != 0:
+            return
+        for rec in run_reference_gpu(args):
+            print(json.dumps(rec), flush=True)
+        return
 
     if world > 1:
         import torch
@@ -655,6 +1033,10 @@ def main():
         out = run_bmm(args, rank, world, local_rank)
     else:
         out = run_ours(args, rank, world, local_rank)
+        if world == 1 and not args.no_subconfigs and out is not None:
+            import torch
+
+            out["configs"] = run_subconfigs(args, torch.device("cuda", local_rank))
     if out is not None:
         print(json.dumps(out), flush=True)
     if world > 1:

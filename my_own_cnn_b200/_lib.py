@@ -33,6 +33,7 @@ PATH_NAMES = {
     8: "tcgen05-tiled-2sm",
     9: "tcgen05-rowtile",
     10: "tcgen05-s2d",
+    11: "tcgen05-qi32",
 }
 
 

@@ -29,6 +29,7 @@
 #include "common.cuh"
 #include "simt.cuh"
 #include "tc_gemm.cuh"
+#include "qi32_tc.cuh"
 
 namespace b200q {
 namespace {
@@ -383,8 +384,9 @@ int launch_tc(const DeviceState& st, const CUtensorMap& ma, const CUtensorMap& m
   a.nacc = g_nacc_max < 512 / a.BN ? g_nacc_max : 512 / a.BN;
   if (a.nacc < 2) a.nacc = 2;
   a.tmem_cols = static_cast<uint32_t>(a.nacc * a.BN);
+  const uint32_t sgn = a.ab_unsigned ? 0u : 1u;       // kind::i8 operand type: 0 = u8, 1 = s8
   a.idesc = (2u << 4)                                   // D = s32
-            | (1u << 7) | (1u << 10)                    // A, B signed int8
+            | (sgn << 7) | (sgn << 10)                  // A, B type
             | (static_cast<uint32_t>(a.a_major) << 15)  // A major
             | (static_cast<uint32_t>(a.b_major) << 16)  // B major
             | (static_cast<uint32_t>(a.BN >> 3) << 17)  // N
@@ -429,6 +431,93 @@ int conv_geom(int n, int h, int w, int c, int r, int s, int k, const b200q_conv_
   return B200Q_OK;
 }
 
+int get_workspace(size_t bytes, cudaStream_t stream, void** out);
+size_t round256(size_t v);
+
+// Tensor-core route of the drop-in (see qi32_tc.cuh): pack 8-bit rows and filter rows with their
+// zero-point terms, one batched tcgen05 GEMM over (output block x group), then the correction /
+// scatter pass.  Returns B200Q_ERR_UNSUPPORTED (nothing launched) for shapes it does not take.
+int qi32_tensor_core(const DeviceState& st, int qtype, const float* x, const float* w, int32_t* y, const ConvGeom& g,
+                     const void* in_qp, const void* f_qp, cudaStream_t stream) {
+  Qi32Pack q{};
+  q.T = g.r * g.s * g.cg;
+  q.kp = (q.T + 31) / 32 * 32;
+  q.gcount = g.by * g.bx * g.groups;
+  const long long mb = static_cast<long long>(g.n) * g.bho * g.bwo;
+  q.qp_stride = qtype == B200Q_LINQUANT_U8 ? (int)sizeof(b200q_qparams_u8) : (int)sizeof(b200q_qparams_s5);
+  q.qp_signed = qtype == B200Q_LINQUANT_S5;
+  if (q.kp > 16384 || mb >= (1ll << 31) || static_cast<long long>(q.gcount) * mb >= (1ll << 40))
+    return B200Q_ERR_UNSUPPORTED;
+  q.mb = static_cast<int>(mb);
+  const long long arows = static_cast<long long>(q.gcount) * mb;
+  const long long brows = static_cast<long long>(q.gcount) * g.kg;
+  const bool in_place = q.gcount == 1;  // the GEMM writes y directly; the fixup corrects in place
+  const size_t a_bytes = round256(static_cast<size_t>(arows) * q.kp);
+  const size_t b_bytes = round256(static_cast<size_t>(brows) * q.kp);
+  const size_t rt_bytes = round256(static_cast<size_t>(arows) * 4);
+  const size_t cs_bytes = round256(static_cast<size_t>(brows) * 4);
+  const size_t c_bytes = in_place ? 0 : round256(static_cast<size_t>(arows) * g.kg * 4);
+  void* ws = nullptr;
+  int rc = get_workspace(a_bytes + b_bytes + rt_bytes + cs_bytes + c_bytes + 256, stream, &ws);
+  if (rc) return rc;
+  uint8_t* base = static_cast<uint8_t*>(ws);
+  uint32_t* a_buf = reinterpret_cast<uint32_t*>(base);
+  uint32_t* b_buf = reinterpret_cast<uint32_t*>(base + a_bytes);
+  int32_t* rowterm = reinterpret_cast<int32_t*>(base + a_bytes + b_bytes);
+  int32_t* colsum = reinterpret_cast<int32_t*>(base + a_bytes + b_bytes + rt_bytes);
+  int32_t* cbuf = in_place ? y : reinterpret_cast<int32_t*>(base + a_bytes + b_bytes + rt_bytes + cs_bytes);
+  int* flag = reinterpret_cast<int*>(base + a_bytes + b_bytes + rt_bytes + cs_bytes + c_bytes);
+  cudaError_t ce = cudaMemsetAsync(flag, 0, sizeof(int), stream);
+  if (ce != cudaSuccess) return cuda_fail(ce, "cudaMemsetAsync(qi32 flag)");
+  const uint8_t* iq = static_cast<const uint8_t*>(in_qp);
+  const uint8_t* fq = static_cast<const uint8_t*>(f_qp);
+  qi32_pack_rows_kernel<<<grid_for(static_cast<size_t>(arows) * 32, 256, st.sms), 256, 0, stream>>>(
+      x, a_buf, rowterm, g, q, iq, fq, flag);
+  rc = check_launch("qi32_pack_rows_kernel launch");
+  if (rc) return rc;
+  qi32_pack_filter_kernel<<<grid_for(static_cast<size_t>(brows) * 32, 256, st.sms), 256, 0, stream>>>(
+      w, b_buf, colsum, g, q, flag);
+  rc = check_launch("qi32_pack_filter_kernel launch");
+  if (rc) return rc;
+  TcArgs a{};
+  a.mode = 0;
+  a.BK = q.kp % 128 == 0 ? 128 : (q.kp % 64 == 0 ? 64 : 32);
+  a.BN = pick_bn(g.kg, 0);
+  a.M = q.mb;
+  a.N = g.kg;
+  a.batch = q.gcount;
+  a.b_batched = q.gcount > 1;
+  a.num_kb = q.kp / a.BK;
+  a.epi = Epilogue{kOutS32, 0, 0, 0, nullptr, nullptr, nullptr, 0.0f};
+  a.out = cbuf;
+  a.ldc = g.kg;
+  a.batch_stride = static_cast<long long>(q.mb) * g.kg;
+  a.vec_ok = g.kg % 16 == 0 && aligned16(cbuf);
+  a.ab_unsigned = qtype == B200Q_LINQUANT_U8;
+  CUtensorMap ma, mb_map;
+  rc = encode_tiled_3d(&ma, a_buf, static_cast<uint64_t>(q.kp), static_cast<uint64_t>(q.mb),
+                       static_cast<uint64_t>(q.gcount), a.BK, kTcBM, a.BK);
+  if (rc) return rc;
+  a.pair = want_pair(st.sms, a);
+  rc = encode_tiled_3d(&mb_map, b_buf, static_cast<uint64_t>(q.kp), static_cast<uint64_t>(g.kg),
+                       static_cast<uint64_t>(q.gcount), a.BK, a.pair ? a.BN / 2 : a.BN, a.BK);
+  if (rc) return rc;
+  rc = launch_tc(st, ma, mb_map, a, stream);
+  if (rc) return rc;
+  const size_t total = static_cast<size_t>(g.n) * g.ho * g.wo * g.k;
+  const bool v4 = g.kg % 4 == 0 && aligned16(y) && aligned16(cbuf);
+  if (v4)
+    qi32_fixup_kernel<4><<<grid_for(total / 4, 256, st.sms), 256, 0, stream>>>(cbuf, y, rowterm, colsum, g, q, iq, fq,
+                                                                              flag, x, w);
+  else
+    qi32_fixup_kernel<1><<<grid_for(total, 256, st.sms), 256, 0, stream>>>(cbuf, y, rowterm, colsum, g, q, iq, fq,
+                                                                          flag, x, w);
+  rc = check_launch("qi32_fixup_kernel launch");
+  if (rc) return rc;
+  g_last_path = 11;
+  return B200Q_OK;
+}
+
 int qi32_common(int qtype, const float* x, const float* w, int32_t* y, const ConvGeom& g, const void* in_qp,
                 const void* f_qp, void* stream) {
   if (qtype != B200Q_LINQUANT_U8 && qtype != B200Q_LINQUANT_S5)
@@ -438,6 +527,10 @@ int qi32_common(int qtype, const float* x, const float* w, int32_t* y, const Con
   DeviceState* st = nullptr;
   int rc = device_state(&st);
   if (rc) return rc;
+  if (g_policy.load() == 0) {
+    rc = qi32_tensor_core(*st, qtype, x, w, y, g, in_qp, f_qp, as_stream(stream));
+    if (rc != B200Q_ERR_UNSUPPORTED) return rc;
+  }
   const int stride = qtype == B200Q_LINQUANT_U8 ? (int)sizeof(b200q_qparams_u8) : (int)sizeof(b200q_qparams_s5);
   const size_t total = static_cast<size_t>(g.n) * g.ho * g.wo * g.k;
   qi32_conv_kernel<<<grid_for(total, 256, st->sms), 256, 0, as_stream(stream)>>>(

@@ -68,6 +68,7 @@ struct TcArgs {
   int rt_pairs, rt_R, rt_S;
   int rt_wide;  // window map in 8-byte elements {2 * W, H, N} (one channel plane): rows of whole pixels
   float hi_f;   // float(epi.hi), for the float-domain clamp of quant4_s8<2>
+  int ab_unsigned;  // both operands unsigned 8-bit (the quantized-int32 drop-in's U8 codes)
 };
 
 constexpr int kTcMaxAcc = 8;
