@@ -142,9 +142,11 @@ int b200q_bmm_s8(const int8_t* A, const int8_t* B, const int32_t* d_bias, const 
  * groups == 1 conv; the im2col matrix and padded weights live in one fixed 32 MiB device array
  * of this library instead of a workspace (every GPU that loads the library holds that array
  * until the process exits).  Limit: round256(N*Ho*Wo*kp) + round256(K*kp) <= 32 MiB with
- * kp = round_up(R*S*C, 32) <= 4096; larger requests return B200Q_ERR_INVALID_ARG with the sizes
+ * kp = round_up(R*S*C, 32) <= 16384 (the packed path's own limit; a larger kp returns
+ * B200Q_ERR_UNSUPPORTED); larger scratch requests return B200Q_ERR_INVALID_ARG with the sizes
  * in b200q_last_error().  The first call on a device looks up the array's device address
- * (cudaGetSymbolAddress); make that first call before any stream capture.  All calls on a
+ * (cudaGetSymbolAddress) and keeps it for the life of the process; make that first call before
+ * any stream capture, and do not reset the device (cudaDeviceReset) between calls.  All calls on a
  * device share the array: every byte the kernels read is rewritten by the same call, but calls
  * that overlap on the GPU (different streams, or host threads sharing a device) race. */
 int b200q_conv2d_s8_packed_noalloc(const int8_t* d_x, const int8_t* d_w, const int32_t* d_bias,

@@ -34,6 +34,7 @@ PATH_NAMES = {
     9: "tcgen05-rowtile",
     10: "tcgen05-s2d",
     11: "tcgen05-qi32",
+    12: "cuda-core-depthwise-tma",
 }
 
 

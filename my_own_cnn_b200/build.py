@@ -9,6 +9,12 @@ written next to the sources, so the built files travel with the source tree:
   reference headers (src/conv_types.h, src/nnalgebra_quantization.h, bmm.h) at build time
 * ``oracle/_ref/quant_conv_test_b200``       -- the reference's unmodified quant_conv_test.cu
   linked against the shim instead of the reference kernels (drop-in proof)
+* ``oracle/_ref/qconv_bench_b200``           -- shim/qconv_bench.cu, the reference's conv_bench
+  driver pattern for the quantized path, with the reference's src/bench.cpp, src/cuda_utils.cpp and
+  src/cpu_ref.cpp compiled from their sources
+
+The reference checkout is taken from ``B200Q_REFERENCE`` or, when that is unset, from a
+``reference`` directory beside this repository; without one only the library is built.
 """
 from __future__ import annotations
 
@@ -23,6 +29,7 @@ CSRC = PKG / "csrc"
 LIB = PKG / "libb200q.so"
 SHIM_LIB = PKG / "libb200q_refshim.so"
 REF_TEST_BIN = ROOT / "oracle" / "_ref" / "quant_conv_test_b200"
+QCONV_BENCH_BIN = ROOT / "oracle" / "_ref" / "qconv_bench_b200"
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-Wall"]
@@ -48,6 +55,12 @@ def _stale(target: Path, deps: list[Path]) -> bool:
     return any(d.stat().st_mtime > t for d in deps)
 
 
+def reference_root() -> Path:
+    """Reference checkout: $B200Q_REFERENCE, else a `reference` directory beside this repository."""
+    env = os.environ.get("B200Q_REFERENCE")
+    return Path(env) if env else ROOT.parent / "reference"
+
+
 def build_library(force: bool = False) -> Path:
     deps = sorted(CSRC.glob("*.cu*")) + [ROOT / "include" / "b200q.h"]
     if force or _stale(LIB, deps):
@@ -62,7 +75,7 @@ def build_reference_shim(ref_root: str | os.PathLike | None = None, force: bool 
     Returns False (and builds nothing) when the reference sources are not present,
     e.g. on a GPU box, where the prebuilt files are used.
     """
-    ref = Path(ref_root or os.environ.get("B200Q_REFERENCE", "/root/reference"))
+    ref = Path(ref_root) if ref_root else reference_root()
     if not (ref / "src" / "conv_types.h").exists():
         return False
     build_library()
@@ -78,13 +91,20 @@ def build_reference_shim(ref_root: str | os.PathLike | None = None, force: bool 
               str(ref / "src" / "cuda_utils.cpp"),
               "-L", str(PKG), "-lb200q_refshim", "-lb200q",
               "-Xlinker", "-rpath,$ORIGIN/../../my_own_cnn_b200"])
+    bench_src = PKG / "shim" / "qconv_bench.cu"
+    if force or _stale(QCONV_BENCH_BIN, [bench_src, SHIM_LIB]):
+        _run([_nvcc(), *ARCH, "-O2", "-std=c++17", *inc, "-o", str(QCONV_BENCH_BIN), str(bench_src),
+              str(ref / "src" / "bench.cpp"), str(ref / "src" / "cuda_utils.cpp"),
+              str(ref / "src" / "cpu_ref.cpp"),
+              "-L", str(PKG), "-lb200q_refshim", "-lb200q",
+              "-Xlinker", "-rpath,$ORIGIN/../../my_own_cnn_b200"])
     return True
 
 
 def build_oracle() -> None:
     """CPU oracle (test infrastructure): oracle/liboracle.so and, with the reference present,
     oracle/_ref/libref_oracle.so."""
-    ref = Path(os.environ.get("B200Q_REFERENCE", "/root/reference"))
+    ref = reference_root()
     target = "all" if (ref / "src" / "cpu_ref.cpp").exists() else "liboracle.so"
     _run(["make", "-s", "-C", str(ROOT / "oracle"), f"REF={ref}", target])
 

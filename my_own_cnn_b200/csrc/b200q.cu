@@ -30,6 +30,7 @@
 #include "simt.cuh"
 #include "tc_gemm.cuh"
 #include "qi32_tc.cuh"
+#include "dw_tma.cuh"
 
 namespace b200q {
 namespace {
@@ -97,6 +98,10 @@ int device_state(DeviceState** out) {
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(tc_gemm_s8_kernel)");
     e = cudaFuncSetAttribute(tc_gemm_s8_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(tc_gemm_s8_pair_kernel)");
+    e = cudaFuncSetAttribute(dw_tma_s8_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(dw_tma_s8_kernel<1>)");
+    e = cudaFuncSetAttribute(dw_tma_s8_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(dw_tma_s8_kernel<2>)");
     if (!g_encode_tiled) {
       cudaDriverEntryPointQueryResult q;
       void* fn = nullptr;
@@ -276,6 +281,12 @@ const bool g_b_resident = [] {
 // 2-SM tiles switch (env B200Q_PAIR=0 turns them off, for A/B timing).
 const bool g_pair = [] {
   const char* v = getenv("B200Q_PAIR");
+  return !(v && v[0] == '0');
+}();
+
+// TMA-staged depthwise switch (env B200Q_DW_TMA=0 keeps the register-window kernel, for A/B timing).
+const bool g_dw_tma = [] {
+  const char* v = getenv("B200Q_DW_TMA");
   return !(v && v[0] == '0');
 }();
 
@@ -728,6 +739,74 @@ int b200q_bmm_matmul_i32(const int32_t* A, const int32_t* B, int32_t* C, int bat
   return B200Q_OK;
 }
 
+// Tile plan of dw_tma_s8_kernel for a 3x3 depthwise conv of stride 1 or 2 (see dw_tma.cuh);
+// false when the geometry does not fit the kernel's limits (TMA boxes of at most 256 per dimension).
+static bool dw_tma_plan(const ConvGeom& g, DwPlan* out) {
+  DwPlan p{};
+  const int s = g.stride_h;
+  if (g.c <= 256) {
+    p.CB = g.c;
+  } else {
+    p.CB = 16;
+    for (int d = 16; d >= 1; --d)
+      if ((g.c / 16) % d == 0) {
+        p.CB = 16 * d;
+        break;
+      }
+  }
+  p.g8 = p.CB / 8;
+  const int max_cols = 256 / p.g8;
+  p.col_tiles = (g.wo + max_cols - 1) / max_cols;
+  for (;;) {
+    p.TW = (g.wo + p.col_tiles - 1) / p.col_tiles;
+    p.wbox = (p.TW - 1) * s + 3;
+    if (p.wbox <= 256) break;
+    ++p.col_tiles;
+  }
+  p.RG = 256 / (p.g8 * p.TW);
+  if (p.RG < 1) return false;
+  if (p.RG > g.ho) p.RG = g.ho;
+  // rows per thread: the largest count whose box stays within 32 KiB and 256 rows, at most enough
+  // to cover the image
+  p.rpt = (g.ho + p.RG - 1) / p.RG;
+  for (;; --p.rpt) {
+    if (p.rpt < 1) return false;
+    p.TH = p.RG * p.rpt;
+    p.rows_in = (p.TH - 1) * s + 3;
+    p.box_bytes = p.CB * p.wbox * p.rows_in;
+    if (p.rows_in <= 256 && p.box_bytes <= 32 * 1024) break;
+  }
+  p.stage = (p.box_bytes + 1023) / 1024 * 1024;
+  p.stages = 3;
+  p.slabs = g.c / p.CB;
+  p.row_tiles = (g.ho + p.TH - 1) / p.TH;
+  const long long total = static_cast<long long>(p.slabs) * g.n * p.row_tiles * p.col_tiles;
+  if (total >= (1ll << 31)) return false;
+  p.total = static_cast<int>(total);
+  *out = p;
+  return true;
+}
+
+static bool dw_tma_ok(const ConvGeom& g, int r, int s, int k, int c, bool has_res, int out_kind) {
+  DwPlan p;
+  return !has_res && out_kind == kOutS8 && g.groups == c && k == c && c % 16 == 0 && r == 3 && s == 3 &&
+         g.dil_h == 1 && g.dil_w == 1 && g.stride_h == g.stride_w && (g.stride_h == 1 || g.stride_h == 2) &&
+         dw_tma_plan(g, &p);
+}
+
+// Depthwise input map: x as [N][H][W][C] uint8, box {CB, wbox, rows_in, 1}, no swizzle.
+static int encode_dw(CUtensorMap* map, const int8_t* x, const ConvGeom& g, const DwPlan& p) {
+  cuuint64_t dims[4] = {(cuuint64_t)g.c, (cuuint64_t)g.w, (cuuint64_t)g.h, (cuuint64_t)g.n};
+  cuuint64_t strides[3] = {(cuuint64_t)g.c, (cuuint64_t)g.c * g.w, (cuuint64_t)g.c * g.w * g.h};
+  cuuint32_t box[4] = {(cuuint32_t)p.CB, (cuuint32_t)p.wbox, (cuuint32_t)p.rows_in, 1};
+  cuuint32_t es[4] = {1, 1, 1, 1};
+  CUresult r = g_encode_tiled(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<int8_t*>(x), dims, strides, box, es,
+                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(B200Q_ERR_CUDA, "cuTensorMapEncodeTiled (depthwise tile) failed (%d)", (int)r);
+  return B200Q_OK;
+}
+
 // Dispatch of the int8 conv (shared by the plain and the residual-add entry points).
 // Kernel family of a conv2d_s8 call (b200q_last_path codes), decided from the geometry, the
 // epilogue, pointer alignment and the SM count only, so that b200q_conv2d_s8_plan can predict it
@@ -753,7 +832,6 @@ static ConvRoute route_conv_s8(const ConvGeom& g, int h, int w, int c, int r, in
   const bool out_aligned = y_aligned && epi_aligned;
   (void)h;
   (void)w;
-  (void)out_kind;
   ConvRoute rt{3, 0, 0, 0};
   const bool auto_policy = g_policy.load() == 0;
   const long long M = static_cast<long long>(g.n) * g.ho * g.wo;
@@ -817,6 +895,10 @@ static ConvRoute route_conv_s8(const ConvGeom& g, int h, int w, int c, int r, in
   if (auto_policy && g.groups == 1 && (c % 16 != 0 ? M >= 4096 : M >= 64) && M < (1ll << 31) && kp_packed <= 16384 &&
       out_aligned) {
     rt.path = 7;
+    return rt;
+  }
+  if (g_dw_tma && auto_policy && x_aligned && y_aligned && dw_tma_ok(g, r, s, k, c, has_res, out_kind)) {
+    rt.path = 12;
     return rt;
   }
   if (!has_res && g.groups == c && k == c && c % 8 == 0 && c <= 8 * 256 && r == 3 && s == 3 && M < (1ll << 31) &&
@@ -1018,6 +1100,26 @@ static int conv2d_s8_impl(const int8_t* d_x, const int8_t* d_w, const int32_t* d
     g_last_path = 7;
     return run_packed_conv(*st, d_x, d_w, d_y, g, e, static_cast<int8_t*>(ws), cs);
   }
+  if (route.path == 12) {
+    DwPlan dp;
+    dw_tma_plan(g, &dp);
+    dp.wait_limit = wait_limit();
+    dp.err = st->err;
+    CUtensorMap mx;
+    rc = encode_dw(&mx, d_x, g, dp);
+    if (rc) return rc;
+    const size_t smem = static_cast<size_t>(dp.stages) * dp.stage + 1024;
+    int per_sm = static_cast<int>((kSmemLimit + 1024) / (smem + 1024));
+    if (per_sm > 3) per_sm = 3;
+    if (per_sm < 1) per_sm = 1;
+    const int grid = dp.total < st->sms * per_sm ? dp.total : st->sms * per_sm;
+    g_last_path = 12;
+    if (g.stride_h == 1)
+      dw_tma_s8_kernel<1><<<grid, 256, smem, cs>>>(mx, static_cast<int8_t*>(d_y), d_w, g, e, dp);
+    else
+      dw_tma_s8_kernel<2><<<grid, 256, smem, cs>>>(mx, static_cast<int8_t*>(d_y), d_w, g, e, dp);
+    return check_launch("dw_tma_s8_kernel launch");
+  }
   const size_t total = static_cast<size_t>(M) * k;
   if (route.path == 4) {
     const int groups8 = c / 8;
@@ -1163,9 +1265,6 @@ int b200q_bmm_s8(const int8_t* A, const int8_t* B, const int32_t* d_bias, const 
   return B200Q_OK;
 }
 
-// Packed low-channel conv with fixed scratch: see include/b200q.h.  Same arithmetic and kernels as
-// the packed path of b200q_conv2d_s8, but the im2col matrix and padded weights go to the static
-// array above instead of a workspace, and nothing is allocated.
 int b200q_maxpool_s8(const int8_t* d_x, int8_t* d_y, int n, int h, int w, int c, int r, int s, int stride_h,
                      int stride_w, int pad_h, int pad_w, void* stream) {
   if (n < 0 || h <= 0 || w <= 0 || c <= 0 || r <= 0 || s <= 0) return fail(B200Q_ERR_INVALID_ARG, "bad pool shape");
@@ -1204,6 +1303,9 @@ int b200q_global_avgpool_s8(const int8_t* d_x, int8_t* d_y, int n, int h, int w,
   return check_launch("global_avgpool_s8_kernel launch");
 }
 
+// Packed low-channel conv with fixed scratch: see include/b200q.h.  Same arithmetic and kernels as
+// the packed path of b200q_conv2d_s8, but the im2col matrix and padded weights go to the static
+// array above instead of a workspace, and nothing is allocated.
 int b200q_conv2d_s8_packed_noalloc(const int8_t* d_x, const int8_t* d_w, const int32_t* d_bias, const float* d_scale,
                                    void* d_y, int n, int h, int w, int c, int r, int s, int k,
                                    const b200q_conv_params* p, const b200q_epilogue* epi, void* stream) {
@@ -1219,7 +1321,7 @@ int b200q_conv2d_s8_packed_noalloc(const int8_t* d_x, const int8_t* d_w, const i
     return fail(B200Q_ERR_INVALID_ARG, "output, bias and scale must be 16-byte aligned");
   const long long rows = static_cast<long long>(n) * g.ho * g.wo;
   const int kp = (r * s * c + 31) / 32 * 32;
-  if (kp > 4096) return fail(B200Q_ERR_UNSUPPORTED, "R*S*C = %d exceeds 4096", r * s * c);
+  if (kp > 16384) return fail(B200Q_ERR_UNSUPPORTED, "R*S*C = %d exceeds 16384", r * s * c);
   const size_t need = packed_scratch_bytes(rows, k, kp);
   if (rows >= (1ll << 31) || need > kNoAllocScratchBytes)
     return fail(B200Q_ERR_INVALID_ARG,

@@ -13,6 +13,7 @@ constexpr int kDevErrTimeoutProducer = 0x101;
 constexpr int kDevErrTimeoutMma = 0x102;
 constexpr int kDevErrTimeoutEpilogue = 0x103;
 constexpr int kDevErrTimeoutProbe = 0x104;
+constexpr int kDevErrTimeoutDw = 0x105;
 
 struct Epilogue {
   int out_kind;

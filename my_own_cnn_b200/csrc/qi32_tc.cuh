@@ -28,7 +28,7 @@
 namespace b200q {
 
 // Direct quantized-int32 output element idx (the reference's loop nest, src/cpu_ref.cpp:36-112).
-__device__ __forceinline__ int32_t qi32_direct(const float* __restrict__ x, const float* __restrict__ w,
+__device__ __noinline__ int32_t qi32_direct(const float* __restrict__ x, const float* __restrict__ w,
                                                const ConvGeom& g, size_t idx, const uint8_t* __restrict__ in_qp,
                                                int zf, int qp_stride, int qp_signed) {
   const int kk = static_cast<int>(idx % g.k);

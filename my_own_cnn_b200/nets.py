@@ -105,14 +105,16 @@ NETS = {"resnet50": resnet50, "mobilenetv2": mobilenetv2}
 
 class NetData:
     """Device tensors for every layer of a spec list: input, weights, bias, scale, output.
-    Tensor ids per layer i: 100*i + {1 input, 2 weights, 3 bias, 4 scale}."""
+    Tensor ids per layer i: 100*i + {1 input, 2 weights, 3 bias, 4 scale}; `first_layer` numbers the
+    first spec as layer `first_layer` of its table (a slice of a table keeps the table's tensors)."""
 
-    def __init__(self, specs: list[LayerSpec], batch: int, seed: int, device, image_offset: int = 0):
+    def __init__(self, specs: list[LayerSpec], batch: int, seed: int, device, image_offset: int = 0,
+                 first_layer: int = 0):
         self.specs, self.batch, self.seed = specs, batch, seed
         act = torch.from_numpy(act_table()).to(device)
         wtab = torch.from_numpy(weight_table()).to(device)
         self.layers = []
-        for i, sp in enumerate(specs):
+        for i, sp in enumerate(specs, start=first_layer):
             x = torch.empty((batch, sp.h, sp.w, sp.c), dtype=torch.int8, device=device)
             synth.fill_s8_table(x, seed + image_offset, 100 * i + 1, act)
             w = synth.fill_s8_table(torch.empty((sp.k, sp.r, sp.r, sp.c // sp.groups), dtype=torch.int8,

@@ -8,7 +8,8 @@ layers; intermediate buffers are allocated once per batch size and reused).
 the kernels: the batch is cut into chunks of images (images are independent), and three CUDA
 streams carry host->device copies of chunk i+1, the layers of chunk i and device->host copies of
 chunk i-1 at the same time.  Each slot of device buffers is reused only after the events of the
-chunk that last used it have completed.
+chunk that last used it have completed.  The streams and slot buffers are created on the first
+call and reused by later calls with the same chunk shape.
 """
 from __future__ import annotations
 
@@ -40,6 +41,16 @@ class ConvStack:
             self.shapes.append((h, w, c))
         self.out_dtype = layers[-1].epi.torch_dtype
         self._bufs: dict[tuple[int, int], list[torch.Tensor]] = {}
+        # run_host's side streams and input slots, created once per (device, chunk shape, slots)
+        self._pipes: dict[tuple, tuple[list[torch.cuda.Stream], list[torch.Tensor]]] = {}
+
+    def _pipeline(self, device, chunk: int, slots: int, x_shape: tuple, x_dtype):
+        key = (device, chunk, slots, x_shape, x_dtype)
+        if key not in self._pipes:
+            streams = [torch.cuda.Stream(device) for _ in range(3)]
+            x_slots = [torch.empty((chunk,) + x_shape, dtype=x_dtype, device=device) for _ in range(slots)]
+            self._pipes[key] = (streams, x_slots)
+        return self._pipes[key]
 
     def _buffers(self, n: int, slot: int, device) -> list[torch.Tensor]:
         key = (n, slot)
@@ -72,12 +83,13 @@ class ConvStack:
         device = device or torch.device("cuda", torch.cuda.current_device())
         n = h_x.shape[0]
         cur = torch.cuda.current_stream(device)
-        s_in, s_cmp, s_out = (torch.cuda.Stream(device) for _ in range(3))
+        (s_in, s_cmp, s_out), x_slots = self._pipeline(device, chunk, slots, tuple(h_x.shape[1:]), h_x.dtype)
+        # every side stream starts after all work already on the current stream, which includes the
+        # previous call's joins: the reused slots are free again
         start = torch.cuda.Event()
         start.record(cur)
         for s in (s_in, s_cmp, s_out):
             s.wait_event(start)
-        x_slots = [torch.empty((chunk,) + tuple(h_x.shape[1:]), dtype=h_x.dtype, device=device) for _ in range(slots)]
         in_done, cmp_done, out_done = {}, {}, {}
         nchunks = (n + chunk - 1) // chunk
         for i in range(nchunks):

@@ -172,7 +172,7 @@ def test_conv_plan_dispatch_tables():
     assert b2q.conv2d_s8_plan(512, 14, 14, 1024, 1, 1, 2048, P(0, 0), E.int8()) == "tcgen05-tiled"
     assert b2q.conv2d_s8_plan(512, 14, 14, 2048, 1, 1, 512, P(0, 0), E.int8()) == "tcgen05-tiled-2sm"
     want = {"resnet50": {"tcgen05-s2d": 1, "tcgen05-tiled": 33, "tcgen05-rowtile": 6, "tcgen05-im2col": 13},
-            "mobilenetv2": {"tcgen05-s2d": 1, "cuda-core-depthwise": 17, "tcgen05-tiled": 32, "tcgen05-packed": 2}}
+            "mobilenetv2": {"tcgen05-s2d": 1, "cuda-core-depthwise-tma": 17, "tcgen05-tiled": 32, "tcgen05-packed": 2}}
     for net, batch in (("resnet50", 256), ("mobilenetv2", 512)):
         got = Counter(b2q.conv2d_s8_plan(batch, sp.h, sp.w, sp.c, sp.r, sp.r, sp.k, sp.params(), sp.epilogue())
                       for sp in nets.NETS[net]())

@@ -51,6 +51,8 @@ def test_noalloc_conv_matches_existing_entry_on_two_calls_in_a_row(cuda_lib):
         _case(7, (2, 128, 128, 3, 3, 3, 32), (1, 1, 2, 2, 1, 1, 1), (_lib.OUT_S8, 0, 0, 127), torch.int8),
         # ResNet-50 stem geometry (7x7/2, C = 3 -> 64), int32 accumulators + bias
         _case(11, (3, 64, 64, 3, 7, 7, 64), (3, 3, 2, 2, 1, 1, 1), (_lib.OUT_S32, 0, 0, 0), torch.int32),
+        # M = 100 rows (one partial 128-row tile), K = 24 output channels (no 16-byte vector stores)
+        _case(13, (1, 10, 10, 16, 3, 3, 24), (1, 1, 1, 1, 1, 1, 1), (_lib.OUT_S8, 0, -128, 127), torch.int8),
     ]
     for cs in cases:  # two no-alloc calls back to back; the second overwrites the shared scratch
         rc = _call("b200q_conv2d_s8_packed_noalloc", cs["x"], cs["w"], cs["bias"], cs["scale"], cs["y_new"],
@@ -75,3 +77,29 @@ def test_noalloc_conv_rejects_requests_beyond_its_scratch(cuda_lib):
                big["shape"], big["params"], big["epi"])
     assert rc == _lib.B200Q_ERR_INVALID_ARG
     assert b"maximum" in _lib.lib().b200q_last_error()
+
+
+def test_noalloc_conv_leaves_device_memory_unchanged(cuda_lib):
+    """After a first call (which looks up the array's address), further calls on a new stream take
+    no device memory: the free-memory figure of the device does not move."""
+    cs = _case(17, (2, 96, 96, 3, 3, 3, 32), (1, 1, 2, 2, 1, 1, 1), (_lib.OUT_S8, 0, 0, 127), torch.int8)
+    args = (cs["x"], cs["w"], cs["bias"], cs["scale"], cs["y_new"], cs["shape"], cs["params"], cs["epi"])
+    assert _call("b200q_conv2d_s8_packed_noalloc", *args) == 0, _lib.lib().b200q_last_error()
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info()
+    side = torch.cuda.Stream()
+    with torch.cuda.stream(side):
+        for _ in range(3):
+            assert _call("b200q_conv2d_s8_packed_noalloc", *args) == 0, _lib.lib().b200q_last_error()
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info()
+    assert free1 == free0
+
+
+def test_noalloc_conv_rejects_filter_rows_beyond_the_packed_limit(cuda_lib):
+    """round_up(R*S*C, 32) above 16384 (here 3x3x1824 -> 16416) is refused, like the packed path."""
+    cs = _case(19, (1, 3, 3, 1824, 3, 3, 16), (1, 1, 1, 1, 1, 1, 1), (_lib.OUT_S32, 0, 0, 0), torch.int32)
+    rc = _call("b200q_conv2d_s8_packed_noalloc", cs["x"], cs["w"], cs["bias"], cs["scale"], cs["y_new"],
+               cs["shape"], cs["params"], cs["epi"])
+    assert rc == _lib.B200Q_ERR_UNSUPPORTED
+    assert b"16384" in _lib.lib().b200q_last_error()
