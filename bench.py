@@ -796,6 +796,37 @@ def _roof(ops: float, nbytes: float, ms: float, peaks: dict) -> dict:
             "peak_source": peaks["source"]}
 
 
+def _graph_us(fn, dev, calls: int = 100) -> float | None:
+    """Device time per call of `fn` when `calls` calls are captured in one CUDA graph and replayed
+    (no host work between the kernels), min of 5 replays; None if the capture is refused."""
+    import torch
+
+    side = torch.cuda.Stream(dev)
+    try:
+        g = torch.cuda.CUDAGraph()
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            fn()
+            torch.cuda.synchronize()
+            with torch.cuda.graph(g, stream=side):
+                for _ in range(calls):
+                    fn()
+        torch.cuda.synchronize()
+        best = None
+        for _ in range(5):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            g.replay()
+            b.record()
+            torch.cuda.synchronize()
+            t = a.elapsed_time(b) * 1e3 / calls
+            best = t if best is None else min(best, t)
+        return round(best, 3)
+    except Exception as ex:  # capture not possible on this path: report it, do not fail the bench
+        torch.cuda.synchronize()
+        return f"capture failed: {type(ex).__name__}"
+
+
 def run_config1(args, dev) -> dict:
     """one conv, 1x56x56x64, 3x3 pad 1, K = 64, bias + per-channel requant to int8.
     Also the reference-API drop-in (launch_fprop_nhwc_qi32, float codes, U8 zero points) at the same
@@ -824,6 +855,7 @@ def run_config1(args, dev) -> dict:
     ms = statistics.median(_timed_ms(run, steps, flush, stream))
     hot = _timed_ms(lambda: [run() for _ in range(100)], 3, flush, stream)
     hot_us = min(hot) * 10.0
+    graph_us = _graph_us(run, dev)
     # drop-in: U8 float codes (x + 127 in [0, 254]), per-image zero point 91, filter zero point 37
     xf = (x.float() + 127.0).contiguous()
     wf = (wt.float() + 127.0).contiguous()
@@ -836,16 +868,21 @@ def run_config1(args, dev) -> dict:
     dpath = b2q.last_path()
     dms = statistics.median(_timed_ms(drop, steps, flush, stream))
     dhot = min(_timed_ms(lambda: [drop() for _ in range(100)], 3, flush, stream)) * 10.0
+    dgraph_us = _graph_us(drop, dev)
     peaks = load_peaks()
     ops = 2 * n * h * w * k * 9 * c
     nbytes = n * h * w * c + k * 9 * c + n * h * w * k + 8 * k
     rec = {"workload": "config1 conv 1x56x56x64 3x3/1 p1 K64, bias+per-channel requant int8",
            "value": round(1.0 / (ms * 1e-3), 1), "unit": "images/s", "ms_per_step": round(ms, 5), "steps": steps,
            "path": path, "tops": round(ops / ms / 1e9, 2), "back_to_back_us": round(hot_us, 2),
+           "graph_us": graph_us,
            "roofline": _roof(ops, nbytes, ms, peaks),
-           "note": "M = 3136 rows: 25 row tiles of 128 on 148 SMs; latency-bound (roof_ms is the tensor/HBM roof)",
+           "note": "M = 3136 rows: 28 row tiles on 148 SMs; latency-bound (roof_ms is the tensor/HBM roof). "
+                   "back_to_back_us: 100 calls from Python in a row (includes the host call path); graph_us: the "
+                   "same 100 calls captured once in a CUDA graph and replayed (device time per conv)",
            "dropin_qi32": {"entry": "launch_fprop_nhwc_qi32 (U8 float codes, zero points 91 / 37)", "path": dpath,
                            "ms_per_step": round(dms, 5), "back_to_back_us": round(dhot, 2),
+                           "graph_us": dgraph_us,
                            "roofline": _roof(ops, 4 * (n * h * w * c + k * 9 * c + n * h * w * k), dms, peaks)}}
     if not args.no_cpu_baseline:
         from oracle import oracle
