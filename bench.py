@@ -477,6 +477,63 @@ def run_reference_gpu(args) -> list[dict]:
                     "identical_int32": bool(torch.equal(y_ref, y_drop) and torch.equal(y_ref, y_s8))})
         del xf, wf, y_ref, y_drop, y_s8
         torch.cuda.empty_cache()
+    out += _reference_gpu_f32(ref, dev, stream, flush)
+    return out
+
+
+def _reference_gpu_f32(ref, dev, stream, flush) -> list[dict]:
+    """The reference's fp32 conv (fprop / bprop / grad) and fp32 bmm against this library's fp32
+    drop-ins on the same inputs: resnet_like_56x56 of the reference's conv_bench suite
+    (src/main.cpp:163-186) and BASELINE config 2's bmm shape in fp32.  Agreement is reported as the
+    largest |ours - reference| relative to the largest |reference|."""
+    import ctypes
+
+    import torch
+
+    import my_own_cnn_b200 as b2q
+
+    if not hasattr(ref, "refgpu_conv_f32"):
+        return []
+    ref.refgpu_conv_f32.argtypes = [ctypes.c_int] + [ctypes.c_void_p] * 3 + [ctypes.c_int] * 10
+    ref.refgpu_bmm_f32.argtypes = [ctypes.c_void_p] * 3 + [ctypes.c_int] * 6
+    out = []
+    n, h, w, c, k, r = 32, 56, 56, 64, 64, 3
+    p = b2q.Conv2DParams(1, 1, 1, 1, 1, 1, 1)
+    g = torch.Generator(device=dev).manual_seed(SEED)
+    x = torch.randn((n, h, w, c), device=dev, generator=g)
+    wt = torch.randn((k, r, r, c), device=dev, generator=g)
+    dy = torch.randn((n, h, w, k), device=dev, generator=g)
+    flops = 2.0 * n * h * w * k * r * r * c
+    for op, name, a, b, shape, ours in (
+            (0, "fprop", x, wt, (n, h, w, k), b2q.launch_fprop_nhwc),
+            (1, "bprop", dy, wt, (n, h, w, c), b2q.launch_bprop_nhwc),
+            (2, "grad", x, dy, (k, r, r, c), b2q.launch_grad_nhwc)):
+        y_ref = torch.empty(shape, device=dev)
+        y_me = torch.empty(shape, device=dev)
+        run_ref = lambda: ref.refgpu_conv_f32(op, a.data_ptr(), b.data_ptr(), y_ref.data_ptr(), n, h, w, c, r, r, k, 1,
+                                              1, 1)
+        run_me = lambda: ours(a, b, y_me, n, h, w, c, r, r, k, p)
+        run_ref(); run_me(); path = b2q.last_path()
+        t_ref = statistics.median(_timed_ms(run_ref, 3, flush, stream))
+        t_me = statistics.median(_timed_ms(run_me, 10, flush, stream))
+        rel = float((y_me - y_ref).abs().max() / y_ref.abs().max())
+        out.append({"impl": "reference-gpu", "case": f"fp32 {name} conv_bench resnet_like_56x56 (n32 56x56 C64 K64 3x3)",
+                    "reference_gpu_ms": round(t_ref, 4), "ours_ms": round(t_me, 4), "ours_path": path,
+                    "speedup": round(t_ref / t_me, 1), "ours_tflops": round(flops / t_me / 1e9, 1),
+                    "max_rel_diff": rel})
+    batch, M = 64, 1024
+    A = torch.randn((batch, M, M), device=dev, generator=g)
+    B = torch.randn((batch, M, M), device=dev, generator=g)
+    C_ref, C_me = torch.empty_like(A), torch.empty_like(A)
+    run_ref = lambda: ref.refgpu_bmm_f32(A.data_ptr(), B.data_ptr(), C_ref.data_ptr(), batch, M, M, M, 0, 0)
+    run_me = lambda: b2q.bmm_matmul(A, B, C_me, batch, M, M, M, 0, 0)
+    run_ref(); run_me(); path = b2q.last_path()
+    t_ref = statistics.median(_timed_ms(run_ref, 3, flush, stream))
+    t_me = statistics.median(_timed_ms(run_me, 10, flush, stream))
+    out.append({"impl": "reference-gpu", "case": "fp32 bmm_matmul batch 64 x 1024^3 NN", "reference_gpu_ms": round(t_ref, 4),
+                "ours_ms": round(t_me, 4), "ours_path": path, "speedup": round(t_ref / t_me, 1),
+                "ours_tflops": round(2.0 * batch * M ** 3 / t_me / 1e9, 1),
+                "max_rel_diff": float((C_me - C_ref).abs().max() / C_ref.abs().max())})
     return out
 
 

@@ -14,6 +14,14 @@
  *   b200q_block_fprop_nhwc_qi32  replaces conv_quant_detail::launch_block_fprop_nhwc_qi32_{u8,s5}
  *                                (src/conv_types.h:242-251, src/cuda_kernels.cu:1394-1461,1483-1497)
  *   b200q_bmm_matmul_i32         replaces bmm_matmul_i32 (bmm.h:69-74, bmm.cu:298-322)
+ *   b200q_conv_fprop_f32         replaces launch_fprop_nhwc / launch_block_fprop_nhwc
+ *                                (src/conv_types.h:287-299, src/cuda_kernels.cu:767-823, 939-998)
+ *   b200q_conv_bprop_f32         replaces launch_bprop_nhwc / launch_block_bprop_nhwc
+ *                                (src/conv_types.h:290-302, src/cuda_kernels.cu:825-872, 1000-1057)
+ *   b200q_conv_grad_f32          replaces launch_grad_nhwc / launch_block_grad_nhwc
+ *                                (src/conv_types.h:293-306, src/cuda_kernels.cu:874-937, 1059-1136)
+ *   b200q_bmm_f32                replaces bmm_matmul (bmm.h:36-39, bmm.cu:270-296); the layer API
+ *                                bmm_fprop / bmm_bprop* (bmm.h:41-66) is defined over it by the shim
  * New entry points (int8 storage, fused requantization; no reference counterpart):
  *   b200q_conv2d_s8, b200q_bmm_s8.
  * The C++ shim my_own_cnn_b200/shim/reference_shim.cpp defines the reference's
@@ -101,6 +109,40 @@ int b200q_block_fprop_nhwc_qi32(int qtype, const float* d_x, const float* d_w, i
 int b200q_bmm_matmul_i32(const int32_t* A, const int32_t* B, int32_t* C, int batch, int M, int N,
                          int K, int trans_a, int trans_b, void* stream);
 
+/* ---- fp32 drop-ins (tensor cores, 3 x TF32 split products) ----
+ * All tensors fp32 in the reference's layouts: x / dx [n,h,w,c], y / dy [n,ho,wo,k],
+ * w / dw [k, block_by, block_bx, r, s, c/groups] (block_by = block_bx = 1: the regular KRSC filter).
+ * Each operand is split as hi + lo (hi = the value rounded to TF32's 10-bit mantissa, lo = the exact
+ * remainder) and the products hi*hi + hi*lo + lo*hi are summed in fp32 by kind::tf32 tcgen05 MMAs,
+ * so results agree with an fp32 loop to about 1e-6 of sum(|x||w|) per output (the tests bound the
+ * difference to an exact float64 sum by 1e-5 * sum(|x||w|)).  Summation order differs from the
+ * reference's loops, so results are not bit-identical to them.  Inputs are assumed finite.
+ * Workspace: a per-(device, stream) grow-only buffer holding the split operands.  Groups with
+ * (c/groups) * (k/groups) <= 16 (depthwise and the like) run on CUDA-core fp32 kernels instead:
+ * a GEMM per group would have 1-4 rows or columns. */
+
+/* y = conv(x, w) (+ bias of the output block).  d_bias: NULL or [k * block_by * block_bx];
+ * bias_mode 0 = one bias per (k, block), 1 = one per k shared by all blocks, at index
+ * k * block_by * block_bx (BlockBiasMode, src/conv_types.h:36-39, 184-188). */
+int b200q_conv_fprop_f32(const float* d_x, const float* d_w, const float* d_bias, int bias_mode, float* d_y, int n,
+                         int h, int w, int c, int r, int s, int k, const b200q_conv_params* p, int block_by,
+                         int block_bx, void* stream);
+
+/* dx = data gradient of the conv for dy (n, h, w, c are dx's dimensions, as in the reference). */
+int b200q_conv_bprop_f32(const float* d_dy, const float* d_w, float* d_dx, int n, int h, int w, int c, int r, int s,
+                         int k, const b200q_conv_params* p, int block_by, int block_bx, void* stream);
+
+/* dw = filter gradient; d_dbias (NULL or [k * block_by * block_bx]) receives the blocked bias
+ * gradient with the reference's rule (src/cpu_ref.cpp:318-371): dy summed over the block's output
+ * pixels whose tap (0, 0) input lies inside the image. */
+int b200q_conv_grad_f32(const float* d_x, const float* d_dy, float* d_dw, float* d_dbias, int bias_mode, int n, int h,
+                        int w, int c, int r, int s, int k, const b200q_conv_params* p, int block_by, int block_bx,
+                        void* stream);
+
+/* Row-major fp32 batched GEMM, C_b = op(A_b) @ op(B_b), layouts as bmm.h:9-29. */
+int b200q_bmm_f32(const float* A, const float* B, float* C, int batch, int M, int N, int K, int trans_a, int trans_b,
+                  void* stream);
+
 /* ---- new int8 entry points ---- */
 
 /* int8 NHWC conv: d_x [n,h,w,c] int8, d_w [k,r,s,c/groups] int8, zero points 0,
@@ -184,7 +226,9 @@ int b200q_device_error(void);
  * (256-row tiles, one M = 256 MMA per K slice across a cluster of two CTAs), 9 tcgen05 row-tile
  * 3x3 conv (one input-window load per tile serves all nine taps), 10 tcgen05 row tiles over a
  * space-to-depth copy of a stride-2 low-channel input (network stems; the input and weights are
- * rearranged into the stream's workspace). */
+ * rearranged into the stream's workspace), 11 tcgen05 quantized-int32 drop-in (raw 8-bit codes and
+ * zero-point correction terms), 12 CUDA-core depthwise with TMA-staged tiles, 13 tcgen05 fp32
+ * (3 x TF32 split GEMM), 14 CUDA-core fp32 (groups of a few channels, e.g. depthwise). */
 int b200q_last_path(void);
 
 /* 0 = automatic dispatch (default); 1 = force the CUDA-core kernels (cross-checks). */

@@ -35,6 +35,8 @@ PATH_NAMES = {
     10: "tcgen05-s2d",
     11: "tcgen05-qi32",
     12: "cuda-core-depthwise-tma",
+    13: "tcgen05-f32",
+    14: "cuda-core-f32",
 }
 
 
@@ -88,6 +90,10 @@ def lib() -> ctypes.CDLL:
         "b200q_fill_i32_uniform": [vp, c_size_t, c_uint64, c_uint64, c_int32, c_int32, vp],
         "b200q_fill_s8_table": [vp, c_size_t, c_uint64, c_uint64, vp, vp],
         "b200q_selftest_wait_timeout": [c_longlong],
+        "b200q_conv_fprop_f32": [vp, vp, vp, i, vp, i, i, i, i, i, i, i, pconv, i, i, vp],
+        "b200q_conv_bprop_f32": [vp, vp, vp, i, i, i, i, i, i, i, pconv, i, i, vp],
+        "b200q_conv_grad_f32": [vp, vp, vp, vp, i, i, i, i, i, i, i, i, pconv, i, i, vp],
+        "b200q_bmm_f32": [vp, vp, vp, i, i, i, i, i, i, vp],
     }
     for name, args in sig.items():
         f = getattr(L, name)
@@ -129,5 +135,6 @@ EXPORTED_SYMBOLS = [
     "b200q_device_error", "b200q_last_path", "b200q_set_path_policy", "b200q_tc_launch_count",
     "b200q_fill_s8_uniform", "b200q_fill_i32_uniform", "b200q_fill_s8_table",
     "b200q_selftest_wait_timeout", "b200q_conv2d_s8_packed_noalloc", "b200q_noalloc_scratch_bytes",
+    "b200q_conv_fprop_f32", "b200q_conv_bprop_f32", "b200q_conv_grad_f32", "b200q_bmm_f32",
     "b200q_conv2d_s8_add", "b200q_maxpool_s8", "b200q_global_avgpool_s8", "b200q_conv2d_s8_plan",
 ]

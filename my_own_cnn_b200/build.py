@@ -9,6 +9,8 @@ written next to the sources, so the built files travel with the source tree:
   reference headers (src/conv_types.h, src/nnalgebra_quantization.h, bmm.h) at build time
 * ``oracle/_ref/quant_conv_test_b200``       -- the reference's unmodified quant_conv_test.cu
   linked against the shim instead of the reference kernels (drop-in proof)
+* ``oracle/_ref/conv_bench_b200``            -- the reference's own fp32 conv_bench driver, unmodified,
+  linked against the shim (its fp32 launchers come from this library)
 * ``oracle/_ref/qconv_bench_b200``           -- shim/qconv_bench.cu, the reference's conv_bench
   driver pattern for the quantized path, with the reference's src/bench.cpp, src/cuda_utils.cpp and
   src/cpu_ref.cpp compiled from their sources
@@ -30,6 +32,7 @@ LIB = PKG / "libb200q.so"
 SHIM_LIB = PKG / "libb200q_refshim.so"
 REF_TEST_BIN = ROOT / "oracle" / "_ref" / "quant_conv_test_b200"
 QCONV_BENCH_BIN = ROOT / "oracle" / "_ref" / "qconv_bench_b200"
+CONV_BENCH_BIN = ROOT / "oracle" / "_ref" / "conv_bench_b200"
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-Wall"]
@@ -96,6 +99,15 @@ def build_reference_shim(ref_root: str | os.PathLike | None = None, force: bool 
         _run([_nvcc(), *ARCH, "-O2", "-std=c++17", *inc, "-o", str(QCONV_BENCH_BIN), str(bench_src),
               str(ref / "src" / "bench.cpp"), str(ref / "src" / "cuda_utils.cpp"),
               str(ref / "src" / "cpu_ref.cpp"),
+              "-L", str(PKG), "-lb200q_refshim", "-lb200q",
+              "-Xlinker", "-rpath,$ORIGIN/../../my_own_cnn_b200"])
+    # The reference's own fp32 conv_bench driver (src/main.cpp, bench.cpp, verify.cpp, cpu_ref.cpp,
+    # cudnn_ref.cpp without cuDNN), unmodified, linked against the shim instead of the reference's
+    # src/cuda_kernels.cu and bmm.cu.
+    if force or _stale(CONV_BENCH_BIN, [SHIM_LIB]):
+        srcs = [str(ref / "src" / f) for f in ("main.cpp", "bench.cpp", "verify.cpp", "cpu_ref.cpp", "cudnn_ref.cpp",
+                                               "cuda_utils.cpp")]
+        _run([_nvcc(), *ARCH, "-O2", "-std=c++17", *inc, "-o", str(CONV_BENCH_BIN), *srcs,
               "-L", str(PKG), "-lb200q_refshim", "-lb200q",
               "-Xlinker", "-rpath,$ORIGIN/../../my_own_cnn_b200"])
     return True

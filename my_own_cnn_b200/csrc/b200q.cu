@@ -31,6 +31,7 @@
 #include "tc_gemm.cuh"
 #include "qi32_tc.cuh"
 #include "dw_tma.cuh"
+#include "f32_tc.cuh"
 
 namespace b200q {
 namespace {
@@ -98,10 +99,15 @@ int device_state(DeviceState** out) {
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(tc_gemm_s8_kernel)");
     e = cudaFuncSetAttribute(tc_gemm_s8_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(tc_gemm_s8_pair_kernel)");
-    e = cudaFuncSetAttribute(dw_tma_s8_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(dw_tma_s8_kernel<1>)");
-    e = cudaFuncSetAttribute(dw_tma_s8_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(dw_tma_s8_kernel<2>)");
+    {
+      const void* dw_kernels[6] = {(const void*)dw_tma_s8_kernel<1, 0>, (const void*)dw_tma_s8_kernel<1, 1>,
+                                   (const void*)dw_tma_s8_kernel<1, 2>, (const void*)dw_tma_s8_kernel<2, 0>,
+                                   (const void*)dw_tma_s8_kernel<2, 1>, (const void*)dw_tma_s8_kernel<2, 2>};
+      for (const void* k : dw_kernels) {
+        e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(dw_tma_s8_kernel)");
+      }
+    }
     if (!g_encode_tiled) {
       cudaDriverEntryPointQueryResult q;
       void* fn = nullptr;
@@ -354,7 +360,7 @@ int launch_tc(const DeviceState& st, const CUtensorMap& ma, const CUtensorMap& m
   // Resident B for a single N tile whose K blocks fit in 64 KiB (narrow layers, 3x3 convs with
   // few output channels): the weights are loaded once per CTA instead of once per 128-row tile.
   const long long b_all = static_cast<long long>(a.num_kb) * a.BN * a.BK;
-  a.b_res = a.mode == 2 || (!a.pair && g_b_resident && a.n_tiles == 1 && !a.b_batched && a.b_major == 0 &&
+  a.b_res = a.mode == 2 || (!a.pair && !a.tf32 && g_b_resident && a.n_tiles == 1 && !a.b_batched && a.b_major == 0 &&
                             b_all <= 64 * 1024);
   const int b_rows = a.pair ? a.BN / 2 : a.BN;  // B rows per stage held by this CTA
   const int stage_bytes = (a.mode == 2 ? a.rt_stage : kTcBM * a.BK) + (a.b_res ? 0 : b_rows * a.BK);
@@ -396,8 +402,10 @@ int launch_tc(const DeviceState& st, const CUtensorMap& ma, const CUtensorMap& m
   if (a.nacc < 2) a.nacc = 2;
   a.tmem_cols = static_cast<uint32_t>(a.nacc * a.BN);
   const uint32_t sgn = a.ab_unsigned ? 0u : 1u;       // kind::i8 operand type: 0 = u8, 1 = s8
-  a.idesc = (2u << 4)                                   // D = s32
-            | (sgn << 7) | (sgn << 10)                  // A, B type
+  const uint32_t dfmt = a.tf32 ? 1u : 2u;               // D = f32 (kind::tf32) or s32 (kind::i8)
+  const uint32_t abfmt = a.tf32 ? 2u : sgn;             // kind::tf32 operand format: 2 = TF32
+  a.idesc = (dfmt << 4)
+            | (abfmt << 7) | (abfmt << 10)              // A, B type
             | (static_cast<uint32_t>(a.a_major) << 15)  // A major
             | (static_cast<uint32_t>(a.b_major) << 16)  // B major
             | (static_cast<uint32_t>(a.BN >> 3) << 17)  // N
@@ -668,6 +676,163 @@ int noalloc_scratch(int8_t** out) {
     g_noalloc_ptr[dev] = static_cast<int8_t*>(ptr);
   }
   *out = g_noalloc_ptr[dev];
+  return B200Q_OK;
+}
+
+// ------------------------------------------------------------------ fp32 (3 x TF32 split) paths
+int f32_pack(const DeviceState& st, const float* src, float* dst, const F32Pack& q, cudaStream_t stream) {
+  const long long tiles = static_cast<long long>(q.batch) * ((q.rows + 31) / 32) * (q.kp / 32);
+  const long long cap = static_cast<long long>(st.sms) * 16;
+  const int grid = static_cast<int>(tiles < 1 ? 1 : (tiles < cap ? tiles : cap));
+  f32_pack_kernel<<<grid, 256, 0, stream>>>(src, dst, q);
+  return check_launch("f32_pack_kernel launch");
+}
+
+// C[b][m][n] = sum over the packed reduction of A'[b][m][.] * B'[b][n][.] (3 x kp fp32 per row),
+// fp32 accumulators written bit for bit at C + b * bstride + m * ldc + n.
+int f32_gemm(const DeviceState& st, const float* ap, const float* bp, float* c, int batch, int M, int N, int kp,
+             long long ldc, long long bstride, cudaStream_t stream) {
+  TcArgs a{};
+  a.mode = 0;
+  a.tf32 = 1;
+  a.BK = 128;
+  a.BN = pick_bn(N, 0);
+  a.M = M;
+  a.N = N;
+  a.batch = batch;
+  a.b_batched = batch > 1;
+  a.num_kb = 3 * kp / 32;
+  a.epi = Epilogue{kOutS32, 0, 0, 0, nullptr, nullptr, nullptr, 0.0f};
+  a.out = c;
+  a.ldc = ldc;
+  a.batch_stride = bstride;
+  a.vec_ok = N % 4 == 0 && ldc % 4 == 0 && bstride % 4 == 0 && aligned16(c);
+  const uint64_t row_bytes = 12ull * kp;
+  CUtensorMap ma, mb;
+  int rc = encode_tiled_3d(&ma, ap, row_bytes, static_cast<uint64_t>(M), static_cast<uint64_t>(batch), 128, kTcBM, 128);
+  if (rc) return rc;
+  rc = encode_tiled_3d(&mb, bp, row_bytes, static_cast<uint64_t>(N), static_cast<uint64_t>(batch), 128, a.BN, 128);
+  if (rc) return rc;
+  return launch_tc(st, ma, mb, a, stream);
+}
+
+F32Pack f32_conv_pack(const ConvGeom& g, int mode, int rows, int cols, int batch, int lo_mask, int chunk) {
+  F32Pack q{};
+  q.mode = mode;
+  q.rows = rows;
+  q.cols = cols;
+  q.kp = (cols + 31) / 32 * 32;
+  q.lo_mask = lo_mask;
+  q.batch = batch;
+  q.g = g;
+  q.T = g.r * g.s * g.cg;
+  q.nblk = g.by * g.bx;
+  q.mb = g.n * g.bho * g.bwo;
+  q.chunk = chunk;
+  return q;
+}
+
+bool f32_sizes_ok(const ConvGeom& g) {
+  const long long mb = static_cast<long long>(g.n) * g.bho * g.bwo;
+  const long long T = static_cast<long long>(g.r) * g.s * g.cg;
+  return mb < (1ll << 30) && T < (1 << 24) && static_cast<long long>(g.by) * g.bx * g.groups < (1 << 16);
+}
+
+int f32_fprop(const DeviceState& st, const float* x, const float* w, const float* bias, int bias_mode, float* y,
+              const ConvGeom& g, cudaStream_t stream) {
+  const int G = g.groups, nblk = g.by * g.bx, Gp = nblk * G;
+  const int mb = g.n * g.bho * g.bwo, T = g.r * g.s * g.cg;
+  const F32Pack qa = f32_conv_pack(g, kPackIm2colRows, mb, T, Gp, 4, mb);
+  const F32Pack qb = f32_conv_pack(g, kPackWRows, g.kg, T, Gp, 2, mb);
+  // Without blocks or bias the GEMM writes y directly: row m of group grp at y + m * K + grp * Kg.
+  const bool direct = nblk == 1 && !bias;
+  const size_t a_bytes = round256(static_cast<size_t>(Gp) * mb * 3 * qa.kp * 4);
+  const size_t b_bytes = round256(static_cast<size_t>(Gp) * g.kg * 3 * qb.kp * 4);
+  const size_t c_bytes = direct ? 0 : round256(static_cast<size_t>(Gp) * mb * g.kg * 4);
+  void* ws = nullptr;
+  int rc = get_workspace(a_bytes + b_bytes + c_bytes, stream, &ws);
+  if (rc) return rc;
+  float* ap = static_cast<float*>(ws);
+  float* bp = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + a_bytes);
+  float* cp = direct ? y : reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + a_bytes + b_bytes);
+  if ((rc = f32_pack(st, x, ap, qa, stream))) return rc;
+  if ((rc = f32_pack(st, w, bp, qb, stream))) return rc;
+  if (direct)
+    rc = f32_gemm(st, ap, bp, cp, G, mb, g.kg, qa.kp, g.k, g.kg, stream);
+  else
+    rc = f32_gemm(st, ap, bp, cp, Gp, mb, g.kg, qa.kp, g.kg, static_cast<long long>(mb) * g.kg, stream);
+  if (rc) return rc;
+  if (!direct) {
+    const size_t total = static_cast<size_t>(g.n) * g.ho * g.wo * g.k;
+    f32_fprop_scatter_kernel<<<grid_for(total, 256, st.sms), 256, 0, stream>>>(cp, y, g, mb, bias, bias_mode);
+    if ((rc = check_launch("f32_fprop_scatter_kernel launch"))) return rc;
+  }
+  g_last_path = 13;
+  return B200Q_OK;
+}
+
+int f32_bprop(const DeviceState& st, const float* dy, const float* w, float* dx, const ConvGeom& g,
+              cudaStream_t stream) {
+  const int G = g.groups, nblk = g.by * g.bx, Gp = nblk * G;
+  const int mb = g.n * g.bho * g.bwo, T = g.r * g.s * g.cg;
+  const F32Pack qa = f32_conv_pack(g, kPackDyRows, mb, g.kg, Gp, 4, mb);
+  const F32Pack qb = f32_conv_pack(g, kPackWCols, T, g.kg, Gp, 2, mb);
+  const size_t a_bytes = round256(static_cast<size_t>(Gp) * mb * 3 * qa.kp * 4);
+  const size_t b_bytes = round256(static_cast<size_t>(Gp) * T * 3 * qb.kp * 4);
+  const size_t c_bytes = round256(static_cast<size_t>(Gp) * mb * T * 4);
+  void* ws = nullptr;
+  int rc = get_workspace(a_bytes + b_bytes + c_bytes, stream, &ws);
+  if (rc) return rc;
+  float* ap = static_cast<float*>(ws);
+  float* bp = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + a_bytes);
+  float* col = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + a_bytes + b_bytes);
+  if ((rc = f32_pack(st, dy, ap, qa, stream))) return rc;
+  if ((rc = f32_pack(st, w, bp, qb, stream))) return rc;
+  if ((rc = f32_gemm(st, ap, bp, col, Gp, mb, T, qa.kp, T, static_cast<long long>(mb) * T, stream))) return rc;
+  const size_t total = static_cast<size_t>(g.n) * g.h * g.w * g.c;
+  f32_col2im_kernel<<<grid_for(total, 256, st.sms), 256, 0, stream>>>(col, dx, g, mb, T);
+  if ((rc = check_launch("f32_col2im_kernel launch"))) return rc;
+  g_last_path = 13;
+  return B200Q_OK;
+}
+
+int f32_grad(const DeviceState& st, const float* x, const float* dy, float* dw, float* dbias, int bias_mode,
+             const ConvGeom& g, cudaStream_t stream) {
+  const int G = g.groups, nblk = g.by * g.bx, Gp = nblk * G;
+  const int mb = g.n * g.bho * g.bwo, T = g.r * g.s * g.cg;
+  // The reduction runs over the block's output pixels: split it so that every SM has output tiles.
+  const long long tiles = static_cast<long long>(Gp) * ((g.kg + kTcBM - 1) / kTcBM) * ((T + 255) / 256);
+  long long splits = (2ll * st.sms + tiles - 1) / tiles;
+  const long long max_splits = (mb + 511) / 512;
+  if (splits > max_splits) splits = max_splits;
+  if (splits < 1) splits = 1;
+  const int chunk = static_cast<int>(((mb + splits - 1) / splits + 31) / 32 * 32);
+  splits = (mb + chunk - 1) / chunk;
+  const int bt = static_cast<int>(splits) * Gp;
+  const F32Pack qa = f32_conv_pack(g, kPackDyCols, g.kg, chunk, bt, 4, chunk);
+  const F32Pack qb = f32_conv_pack(g, kPackIm2colCols, T, chunk, bt, 2, chunk);
+  const size_t a_bytes = round256(static_cast<size_t>(bt) * g.kg * 3 * qa.kp * 4);
+  const size_t b_bytes = round256(static_cast<size_t>(bt) * T * 3 * qb.kp * 4);
+  const size_t c_bytes = round256(static_cast<size_t>(bt) * g.kg * T * 4);
+  void* ws = nullptr;
+  int rc = get_workspace(a_bytes + b_bytes + c_bytes, stream, &ws);
+  if (rc) return rc;
+  float* ap = static_cast<float*>(ws);
+  float* bp = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + a_bytes);
+  float* cp = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + a_bytes + b_bytes);
+  if ((rc = f32_pack(st, dy, ap, qa, stream))) return rc;
+  if ((rc = f32_pack(st, x, bp, qb, stream))) return rc;
+  if ((rc = f32_gemm(st, ap, bp, cp, bt, g.kg, T, qa.kp, T, static_cast<long long>(g.kg) * T, stream))) return rc;
+  const size_t total = static_cast<size_t>(g.k) * nblk * T;
+  f32_grad_reduce_kernel<<<grid_for(total, 256, st.sms), 256, 0, stream>>>(cp, dw, g, nblk, T,
+                                                                           static_cast<int>(splits));
+  if ((rc = check_launch("f32_grad_reduce_kernel launch"))) return rc;
+  if (dbias) {
+    const int entries = g.k * nblk;
+    f32_dbias_kernel<<<entries < st.sms * 8 ? entries : st.sms * 8, 256, 0, stream>>>(dy, dbias, g, bias_mode);
+    if ((rc = check_launch("f32_dbias_kernel launch"))) return rc;
+  }
+  g_last_path = 13;
   return B200Q_OK;
 }
 
@@ -1110,14 +1275,19 @@ static int conv2d_s8_impl(const int8_t* d_x, const int8_t* d_w, const int32_t* d
     if (rc) return rc;
     const size_t smem = static_cast<size_t>(dp.stages) * dp.stage + 1024;
     int per_sm = static_cast<int>((kSmemLimit + 1024) / (smem + 1024));
-    if (per_sm > 3) per_sm = 3;
+    if (per_sm > 2) per_sm = 2;
     if (per_sm < 1) per_sm = 1;
     const int grid = dp.total < st->sms * per_sm ? dp.total : st->sms * per_sm;
     g_last_path = 12;
-    if (g.stride_h == 1)
-      dw_tma_s8_kernel<1><<<grid, 256, smem, cs>>>(mx, static_cast<int8_t*>(d_y), d_w, g, e, dp);
-    else
-      dw_tma_s8_kernel<2><<<grid, 256, smem, cs>>>(mx, static_cast<int8_t*>(d_y), d_w, g, e, dp);
+    const int cl = (e.zp == 0 && e.lo == -128 && e.hi == 127) ? 1 : (e.zp == 0 && e.lo == 0 && e.hi <= 127) ? 2 : 0;
+    int8_t* yo = static_cast<int8_t*>(d_y);
+#define B200Q_DW(S, CL) dw_tma_s8_kernel<S, CL><<<grid, kDwThreads, smem, cs>>>(mx, yo, d_w, g, e, dp)
+    if (g.stride_h == 1) {
+      if (cl == 1) B200Q_DW(1, 1); else if (cl == 2) B200Q_DW(1, 2); else B200Q_DW(1, 0);
+    } else {
+      if (cl == 1) B200Q_DW(2, 1); else if (cl == 2) B200Q_DW(2, 2); else B200Q_DW(2, 0);
+    }
+#undef B200Q_DW
     return check_launch("dw_tma_s8_kernel launch");
   }
   const size_t total = static_cast<size_t>(M) * k;
@@ -1400,6 +1570,130 @@ int b200q_fill_s8_table(int8_t* d_out, size_t count, uint64_t seed, uint64_t ten
   const uint64_t key = mix64(seed * 0x9E3779B97F4A7C15ull ^ mix64(tensor_id + 0x632BE59BD9B4E019ull));
   fill_s8_table_kernel<<<grid_for(count, 256, st->sms), 256, 0, as_stream(stream)>>>(d_out, count, key, d_table);
   return check_launch("fill_s8_table_kernel launch");
+}
+
+// Groups of a few channels (depthwise and the like) run on CUDA cores: a tensor-core GEMM per group
+// would have 1-4 rows or columns (env B200Q_F32_DIRECT=0 keeps them on the GEMM route; the forced
+// CUDA-core policy sends every fp32 conv here, for cross-checks).
+static bool f32_use_direct(const ConvGeom& g) {
+  static const bool on = [] {
+    const char* v = getenv("B200Q_F32_DIRECT");
+    return !(v && v[0] == '0');
+  }();
+  return g_policy.load() == 1 || (on && static_cast<long long>(g.cg) * g.kg <= 16);
+}
+
+static int f32_conv_common(const void* a, const void* b, const void* out, int n, int h, int w, int c, int r, int s,
+                           int k, const b200q_conv_params* p, int by, int bx, ConvGeom* g, DeviceState** st) {
+  int rc = conv_geom(n, h, w, c, r, s, k, p, by, bx, g);
+  if (rc) return rc;
+  if (!a || !b || !out) return fail(B200Q_ERR_INVALID_ARG, "null tensor pointer");
+  if (!f32_sizes_ok(*g)) return fail(B200Q_ERR_UNSUPPORTED, "fp32 conv too large for one batched GEMM");
+  return device_state(st);
+}
+
+int b200q_conv_fprop_f32(const float* d_x, const float* d_w, const float* d_bias, int bias_mode, float* d_y, int n,
+                         int h, int w, int c, int r, int s, int k, const b200q_conv_params* p, int block_by,
+                         int block_bx, void* stream) {
+  ConvGeom g;
+  DeviceState* st = nullptr;
+  int rc = f32_conv_common(d_x, d_w, d_y, n, h, w, c, r, s, k, p, block_by, block_bx, &g, &st);
+  if (rc) return rc;
+  if (bias_mode != 0 && bias_mode != 1) return fail(B200Q_ERR_INVALID_ARG, "bad bias mode %d", bias_mode);
+  if (f32_use_direct(g)) {
+    const size_t total = static_cast<size_t>(g.n) * g.ho * g.wo * g.k;
+    f32_direct_fprop_kernel<<<grid_for(total, 256, st->sms), 256, 0, as_stream(stream)>>>(d_x, d_w, d_y, g, d_bias,
+                                                                                        bias_mode);
+    g_last_path = 14;
+    return check_launch("f32_direct_fprop_kernel launch");
+  }
+  return f32_fprop(*st, d_x, d_w, d_bias, bias_mode, d_y, g, as_stream(stream));
+}
+
+int b200q_conv_bprop_f32(const float* d_dy, const float* d_w, float* d_dx, int n, int h, int w, int c, int r, int s,
+                         int k, const b200q_conv_params* p, int block_by, int block_bx, void* stream) {
+  ConvGeom g;
+  DeviceState* st = nullptr;
+  int rc = f32_conv_common(d_dy, d_w, d_dx, n, h, w, c, r, s, k, p, block_by, block_bx, &g, &st);
+  if (rc) return rc;
+  if (f32_use_direct(g)) {
+    const size_t total = static_cast<size_t>(g.n) * g.h * g.w * g.c;
+    f32_direct_bprop_kernel<<<grid_for(total, 256, st->sms), 256, 0, as_stream(stream)>>>(d_dy, d_w, d_dx, g);
+    g_last_path = 14;
+    return check_launch("f32_direct_bprop_kernel launch");
+  }
+  return f32_bprop(*st, d_dy, d_w, d_dx, g, as_stream(stream));
+}
+
+int b200q_conv_grad_f32(const float* d_x, const float* d_dy, float* d_dw, float* d_dbias, int bias_mode, int n, int h,
+                        int w, int c, int r, int s, int k, const b200q_conv_params* p, int block_by, int block_bx,
+                        void* stream) {
+  ConvGeom g;
+  DeviceState* st = nullptr;
+  int rc = f32_conv_common(d_x, d_dy, d_dw, n, h, w, c, r, s, k, p, block_by, block_bx, &g, &st);
+  if (rc) return rc;
+  if (bias_mode != 0 && bias_mode != 1) return fail(B200Q_ERR_INVALID_ARG, "bad bias mode %d", bias_mode);
+  if (f32_use_direct(g)) {
+    cudaStream_t cs = as_stream(stream);
+    const long long total = static_cast<long long>(g.k) * g.by * g.bx * g.r * g.s * g.cg;
+    const int grid = static_cast<int>(total < st->sms * 16ll ? total : st->sms * 16ll);
+    f32_direct_grad_kernel<<<grid, 256, 0, cs>>>(d_x, d_dy, d_dw, g);
+    rc = check_launch("f32_direct_grad_kernel launch");
+    if (rc) return rc;
+    if (d_dbias) {
+      const int entries = g.k * g.by * g.bx;
+      f32_dbias_kernel<<<entries < st->sms * 8 ? entries : st->sms * 8, 256, 0, cs>>>(d_dy, d_dbias, g, bias_mode);
+      rc = check_launch("f32_dbias_kernel launch");
+      if (rc) return rc;
+    }
+    g_last_path = 14;
+    return B200Q_OK;
+  }
+  return f32_grad(*st, d_x, d_dy, d_dw, d_dbias, bias_mode, g, as_stream(stream));
+}
+
+int b200q_bmm_f32(const float* A, const float* B, float* C, int batch, int M, int N, int K, int trans_a, int trans_b,
+                  void* stream) {
+  if (batch < 0 || M < 0 || N < 0 || K < 0) return fail(B200Q_ERR_INVALID_ARG, "negative bmm dimension");
+  if (batch == 0 || M == 0 || N == 0) return B200Q_OK;
+  if (!C || (K > 0 && (!A || !B))) return fail(B200Q_ERR_INVALID_ARG, "null bmm pointer");
+  if (M >= (1 << 30) || N >= (1 << 30) || K >= (1 << 28) || batch >= (1 << 24))
+    return fail(B200Q_ERR_UNSUPPORTED, "bmm too large");
+  DeviceState* st = nullptr;
+  int rc = device_state(&st);
+  if (rc) return rc;
+  cudaStream_t cs = as_stream(stream);
+  if (K == 0) {
+    cudaError_t e = cudaMemsetAsync(C, 0, static_cast<size_t>(batch) * M * N * sizeof(float), cs);
+    return e == cudaSuccess ? B200Q_OK : cuda_fail(e, "cudaMemsetAsync(bmm C)");
+  }
+  F32Pack qa{}, qb{};
+  qa.mode = qb.mode = kPackMat;
+  qa.rows = M; qb.rows = N;
+  qa.cols = qb.cols = K;
+  qa.kp = qb.kp = (K + 31) / 32 * 32;
+  qa.lo_mask = 4; qb.lo_mask = 2;
+  qa.batch = qb.batch = batch;
+  // A [b][M][K] (or [b][K][M] transposed), B [b][K][N] (or [b][N][K] transposed): logical rows are
+  // the output rows / columns, logical columns the reduction
+  qa.sb = static_cast<long long>(M) * K;
+  qa.sr = trans_a ? 1 : K;
+  qa.sc = trans_a ? M : 1;
+  qb.sb = static_cast<long long>(K) * N;
+  qb.sr = trans_b ? K : 1;
+  qb.sc = trans_b ? 1 : N;
+  const size_t a_bytes = round256(static_cast<size_t>(batch) * M * 3 * qa.kp * 4);
+  const size_t b_bytes = round256(static_cast<size_t>(batch) * N * 3 * qb.kp * 4);
+  void* ws = nullptr;
+  rc = get_workspace(a_bytes + b_bytes, cs, &ws);
+  if (rc) return rc;
+  float* ap = static_cast<float*>(ws);
+  float* bp = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + a_bytes);
+  if ((rc = f32_pack(*st, A, ap, qa, cs))) return rc;
+  if ((rc = f32_pack(*st, B, bp, qb, cs))) return rc;
+  if ((rc = f32_gemm(*st, ap, bp, C, batch, M, N, qa.kp, N, static_cast<long long>(M) * N, cs))) return rc;
+  g_last_path = 13;
+  return B200Q_OK;
 }
 
 }  // extern "C"

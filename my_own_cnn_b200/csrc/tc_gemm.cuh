@@ -69,6 +69,7 @@ struct TcArgs {
   int rt_wide;  // window map in 8-byte elements {2 * W, H, N} (one channel plane): rows of whole pixels
   float hi_f;   // float(epi.hi), for the float-domain clamp of quant4_s8<2>
   int ab_unsigned;  // both operands unsigned 8-bit (the quantized-int32 drop-in's U8 codes)
+  int tf32;         // fp32 operands, kind::tf32 MMAs, fp32 accumulators copied out bit for bit
 };
 
 constexpr int kTcMaxAcc = 8;
@@ -652,7 +653,7 @@ __device__ __forceinline__ bool rowtile_pair_loop(const TcArgs& a, uint32_t tmem
 }
 
 // resident (K block kb of B at kb * stage_b) rather than in the ring.
-template <int KS, bool BRES>
+template <int KS, bool BRES, bool TF32 = false>
 __device__ __forceinline__ bool gemm_mma_loop(const TcArgs& a, uint32_t tmem_base, uint64_t a_desc0, uint64_t b_desc0,
                                               uint32_t sa16, uint32_t sb16, uint32_t as16, uint32_t bs16,
                                               uint32_t full0, uint32_t empty0, uint32_t accf0, uint32_t acce0) {
@@ -675,9 +676,14 @@ __device__ __forceinline__ bool gemm_mma_loop(const TcArgs& a, uint32_t tmem_bas
       const uint64_t ad = a_desc0 + a_off;
       const uint64_t bd = b_desc0 + (BRES ? bres_off : b_off);
 #pragma unroll
-      for (int j = 0; j < KS; ++j)
-        tc_mma_i8_elect(d_tmem, ad + static_cast<uint64_t>(j * as16), bd + static_cast<uint64_t>(j * bs16), idesc,
-                        (kb != 0 || j != 0) ? 1u : 0u);
+      for (int j = 0; j < KS; ++j) {
+        if constexpr (TF32)
+          tc_mma_tf32_elect(d_tmem, ad + static_cast<uint64_t>(j * as16), bd + static_cast<uint64_t>(j * bs16), idesc,
+                            (kb != 0 || j != 0) ? 1u : 0u);
+        else
+          tc_mma_i8_elect(d_tmem, ad + static_cast<uint64_t>(j * as16), bd + static_cast<uint64_t>(j * bs16), idesc,
+                          (kb != 0 || j != 0) ? 1u : 0u);
+      }
       tc_commit_elect(empty0 + 8 * stage);
       bres_off += sb16;
       a_off += sa16;
@@ -910,7 +916,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const uint32_t sa16 = stage_a >> 4, sb16 = stage_b >> 4, as16 = a_step >> 4, bs16 = b_step >> 4;
 #define B200Q_GEMM_MMA(KS, BRES)                                                                              \
   ok = gemm_mma_loop<KS, BRES>(a, tmem_base, a_desc0, b_desc0, sa16, sb16, as16, bs16, full0, empty0, accf0, acce0)
-        if (a.b_res) {
+        if (a.tf32) {
+          // fp32 GEMMs (3 x TF32 split operands): tiled mode, 128-byte K blocks, B in the ring
+          ok = gemm_mma_loop<4, false, true>(a, tmem_base, a_desc0, b_desc0, sa16, sb16, as16, bs16, full0, empty0,
+                                             accf0, acce0);
+        } else if (a.b_res) {
           if (ksteps == 4) B200Q_GEMM_MMA(4, true);
           else if (ksteps == 2) B200Q_GEMM_MMA(2, true);
           else B200Q_GEMM_MMA(1, true);

@@ -254,3 +254,18 @@ def cpu_threads() -> int:
         return len(os.sched_getaffinity(0))
     except AttributeError:
         return os.cpu_count() or 1
+
+
+def ref_conv_f32(a: ConvArgs, op: int, blocked: bool, in_a: np.ndarray, in_b: np.ndarray, out_shape,
+                 bias: np.ndarray | None = None, bias_mode: int = 0) -> np.ndarray:
+    """The reference's own fp32 CPU loops (src/cpu_ref.cpp:116-371): op 0 fprop (x, w) -> y,
+    1 bprop (dy, w) -> dx, 2 grad (x, dy) -> dw.  For blocked grad, `bias` receives dbias."""
+    in_a = np.ascontiguousarray(in_a, dtype=np.float32)
+    in_b = np.ascontiguousarray(in_b, dtype=np.float32)
+    out = np.zeros(out_shape, dtype=np.float32)
+    bptr = None if bias is None else _p(bias)
+    lib_ = ref_lib()
+    lib_.ref_conv_f32.argtypes = [ctypes.c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int]
+    if lib_.ref_conv_f32(ctypes.byref(a), op, int(blocked), _p(in_a), _p(in_b), _p(out), bptr, bias_mode):
+        raise RuntimeError("reference rejected the shape")
+    return out

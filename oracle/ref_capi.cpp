@@ -5,7 +5,8 @@
 // into oracle/_ref/libref_oracle.so.  Nothing from the reference is copied:
 // this file only builds the reference's tensor structs from flat buffers and
 // calls cpu_fprop_nhwc_qi32 / cpu_block_fprop_nhwc_qi32
-// (conv_types.h:255-285, cpu_ref.cpp:36-112, exports cpu_ref.cpp:371-401).
+// (conv_types.h:255-285, cpu_ref.cpp:36-112, exports cpu_ref.cpp:371-401) and the fp32
+// cpu_{,block_}{fprop,bprop,grad}_nhwc (conv_types.h:204-210, cpu_ref.cpp:116-371).
 #include <cstring>
 #include <exception>
 #include <thread>
@@ -129,6 +130,66 @@ int ref_fprop_qi32_threaded(const Args* a, int kind, const float* x, const float
   for (int v : rc)
     if (v) return v;
   return 0;
+}
+
+// The reference's fp32 CPU loops.  op 0 = fprop (a = x, b = w, out = y), 1 = bprop (a = dy,
+// b = w, out = dx), 2 = grad (a = x, b = dy, out = dw).  Blocked when a->by * a->bx > 1 or
+// blocked != 0; bias / dbias (K * By * Bx floats, may be null) with bias_mode as BlockBiasMode.
+int ref_conv_f32(const Args* a, int op, int blocked, const float* in_a, const float* in_b, float* out,
+                 float* bias, int bias_mode) {
+  try {
+    const Conv2DParams p = to_params(*a);
+    const int cg = a->c / a->groups;
+    TensorNHWC x(a->n, a->h, a->w, a->c);
+    FilterKRSC wshape(a->r, a->s, cg, a->k);
+    const ConvShape sh = infer_conv_shape(x, wshape, p);
+    TensorNHWC y(a->n, sh.ho, sh.wo, a->k);
+    BlockConv2DParams bp;
+    bp.conv = p;
+    bp.block_by = a->by;
+    bp.block_bx = a->bx;
+    const BlockBiasMode mode = bias_mode ? BlockBiasMode::Shared : BlockBiasMode::PerBlock;
+    if (!blocked) {
+      FilterKRSC w(a->r, a->s, cg, a->k);
+      if (op == 0) {
+        std::memcpy(x.ptr(), in_a, x.elements() * sizeof(float));
+        std::memcpy(w.ptr(), in_b, w.elements() * sizeof(float));
+        cpu_fprop_nhwc(x, w, p, y);
+        std::memcpy(out, y.ptr(), y.elements() * sizeof(float));
+      } else if (op == 1) {
+        std::memcpy(y.ptr(), in_a, y.elements() * sizeof(float));
+        std::memcpy(w.ptr(), in_b, w.elements() * sizeof(float));
+        cpu_bprop_nhwc(y, w, p, x);
+        std::memcpy(out, x.ptr(), x.elements() * sizeof(float));
+      } else {
+        std::memcpy(x.ptr(), in_a, x.elements() * sizeof(float));
+        std::memcpy(y.ptr(), in_b, y.elements() * sizeof(float));
+        cpu_grad_nhwc(x, y, p, w);
+        std::memcpy(out, w.ptr(), w.elements() * sizeof(float));
+      }
+    } else {
+      BlockFilterKByBxRSC w(a->k, a->by, a->bx, a->r, a->s, cg);
+      if (op == 0) {
+        std::memcpy(x.ptr(), in_a, x.elements() * sizeof(float));
+        std::memcpy(w.ptr(), in_b, w.elements() * sizeof(float));
+        cpu_block_fprop_nhwc(x, w, bp, y, bias, mode);
+        std::memcpy(out, y.ptr(), y.elements() * sizeof(float));
+      } else if (op == 1) {
+        std::memcpy(y.ptr(), in_a, y.elements() * sizeof(float));
+        std::memcpy(w.ptr(), in_b, w.elements() * sizeof(float));
+        cpu_block_bprop_nhwc(y, w, bp, x);
+        std::memcpy(out, x.ptr(), x.elements() * sizeof(float));
+      } else {
+        std::memcpy(x.ptr(), in_a, x.elements() * sizeof(float));
+        std::memcpy(y.ptr(), in_b, y.elements() * sizeof(float));
+        cpu_block_grad_nhwc(x, y, bp, w, bias, mode);
+        std::memcpy(out, w.ptr(), w.elements() * sizeof(float));
+      }
+    }
+    return 0;
+  } catch (const std::exception&) {
+    return 1;
+  }
 }
 
 }  // extern "C"

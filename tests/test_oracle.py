@@ -180,3 +180,42 @@ def test_pool_oracles_against_numpy():
     s = x.astype(np.int32).sum(axis=(1, 2))
     want = np.clip(np.rint(s.astype(np.float32) / np.float32(99)), -128, 127).astype(np.int8)
     np.testing.assert_array_equal(a, want)
+
+
+@pytest.mark.parametrize("case", [
+    # n, h, w, c, k, r, s, pad_h, pad_w, sh, sw, dh, dw, groups, by, bx
+    (2, 7, 6, 4, 6, 3, 2, 1, 0, 1, 1, 1, 1, 2, 1, 1),
+    (1, 9, 9, 6, 4, 3, 3, 2, 2, 2, 2, 2, 2, 1, 1, 1),
+    (2, 6, 6, 4, 5, 3, 3, 1, 1, 1, 1, 1, 1, 1, 2, 3),
+    (2, 8, 8, 6, 6, 3, 3, 1, 1, 1, 1, 1, 1, 3, 2, 2),
+])
+@pytest.mark.parametrize("mode", [0, 1])
+def test_f32_restatement_matches_reference_cpu(case, mode):
+    """oracle/f32_oracle.py (float64) against the reference's own fp32 loops (src/cpu_ref.cpp:116-371):
+    equal within fp32 rounding of the reference's sums, dbias included."""
+    from oracle import f32_oracle
+
+    if not oracle.ref_available():
+        pytest.skip("reference oracle not built")
+    n, h, w, c, k, r, s, ph, pw, sh, sw, dh, dw, G, by, bx = case
+    prm = (ph, pw, sh, sw, dh, dw, G)
+    blocked = by * bx > 1
+    rng = np.random.default_rng(sum(case) + mode)
+    ho, wo = f32_oracle.out_hw(h, w, r, s, ph, pw, sh, sw, dh, dw)
+    x = rng.standard_normal((n, h, w, c)).astype(np.float32)
+    wt = rng.standard_normal((k, by, bx, r, s, c // G) if blocked else (k, r, s, c // G)).astype(np.float32)
+    dy = rng.standard_normal((n, ho, wo, k)).astype(np.float32)
+    bias = rng.standard_normal(k * by * bx).astype(np.float32) if blocked else None
+    a = oracle.conv_args(n, h, w, c, r, s, k, *prm, by, bx)
+    ye, yb = f32_oracle.fprop(x, wt, prm, by, bx, bias, mode)
+    y = oracle.ref_conv_f32(a, 0, blocked, x, wt, (n, ho, wo, k), None if bias is None else bias.copy(), mode)
+    assert (np.abs(y - ye) <= 1e-5 * yb + 1e-6).all()
+    dxe, dxb = f32_oracle.bprop(dy, wt, (n, h, w, c), prm, by, bx)
+    dx = oracle.ref_conv_f32(a, 1, blocked, dy, wt, (n, h, w, c))
+    assert (np.abs(dx - dxe) <= 1e-5 * dxb + 1e-6).all()
+    dwe, dwb, dbe = f32_oracle.grad(x, dy, r, s, prm, by, bx, mode)
+    db = np.zeros(k * by * bx, np.float32)
+    dwr = oracle.ref_conv_f32(a, 2, blocked, x, dy, dwe.shape, db if blocked else None, mode)
+    assert (np.abs(dwr - dwe) <= 1e-5 * dwb + 1e-6).all()
+    if blocked:
+        np.testing.assert_allclose(db, dbe, rtol=1e-5, atol=1e-4)
