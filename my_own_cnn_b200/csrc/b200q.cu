@@ -346,7 +346,8 @@ bool want_pair(int sms, const TcArgs& a) {
   return n_tiles >= 2 && pair_tiles >= sms;
 }
 
-int launch_tc(const DeviceState& st, const CUtensorMap& ma, const CUtensorMap& mb, TcArgs a, cudaStream_t stream) {
+int launch_tc(const DeviceState& st, const CUtensorMap& ma, const CUtensorMap& mb, TcArgs a, cudaStream_t stream,
+              const CUtensorMap* ma2 = nullptr) {
   // 4-byte outputs go through shared memory and TMA stores when the row pitch allows a tensor map.
   CUtensorMap mc = ma;  // unused placeholder when tma_store == 0
   a.tma_store = 0;
@@ -423,7 +424,7 @@ int launch_tc(const DeviceState& st, const CUtensorMap& ma, const CUtensorMap& m
     g_tc_launches.fetch_add(1, std::memory_order_relaxed);
     return check_launch("tc_gemm_s8_pair_kernel launch");
   }
-  tc_gemm_s8_kernel<<<grid, kTcThreads, smem, stream>>>(ma, mb, mc, a);
+  tc_gemm_s8_kernel<<<grid, kTcThreads, smem, stream>>>(ma, mb, mc, a, ma2 ? *ma2 : ma);
   g_tc_launches.fetch_add(1, std::memory_order_relaxed);
   return check_launch("tc_gemm_s8_kernel launch");
 }
@@ -738,8 +739,74 @@ bool f32_sizes_ok(const ConvGeom& g) {
   return mb < (1ll << 30) && T < (1 << 24) && static_cast<long long>(g.by) * g.bx * g.groups < (1 << 16);
 }
 
+// Whether a regular fp32 conv of this geometry (input x of g.c channels) can run through the
+// im2col TMA: groups == 1, no blocks, 16-byte pixel rows and pointers, the im2col corner limits,
+// and at least 128 KiB of input (smaller im2col maps take the packed route).
+bool f32_im2col_ok(const ConvGeom& g, const void* x, const void* y) {
+  const bool corners_ok = g.pad_w <= 127 && g.pad_h <= 127 && g.pad_w - (g.s - 1) * g.dil_w >= -128 &&
+                          g.pad_h - (g.r - 1) * g.dil_h >= -128 && (g.s - 1) * g.dil_w <= 255 &&
+                          (g.r - 1) * g.dil_h <= 255 && g.stride_h <= 8 && g.stride_w <= 8;
+  const long long M = static_cast<long long>(g.n) * g.ho * g.wo;
+  const size_t x_bytes = static_cast<size_t>(g.n) * g.h * g.w * g.c * 4;
+  return g.groups == 1 && g.by == 1 && g.bx == 1 && g.c % 4 == 0 && aligned16(x) && aligned16(y) && corners_ok &&
+         x_bytes >= (128u << 10) && M < (1ll << 31) && g.k <= 65535;
+}
+
+// fp32 conv of x [n,h,w,c] with KRSC weights (flip = 0) or with the data-gradient filter of a
+// stride-1 conv (flip = 1, see f32_pack_taps_kernel), written to y [n,ho,wo,k] directly.
+int f32_conv_im2col(const DeviceState& st, const float* x, const float* w, float* y, const ConvGeom& g, int flip,
+                    cudaStream_t stream) {
+  const int cpad = (g.c + 31) / 32 * 32;
+  const int L = g.r * g.s * cpad;
+  const size_t x_elems = static_cast<size_t>(g.n) * g.h * g.w * g.c;
+  const size_t x_bytes = round256(x_elems * 4);
+  const size_t b_bytes = round256(static_cast<size_t>(g.k) * 3 * L * 4);
+  void* ws = nullptr;
+  int rc = get_workspace(2 * x_bytes + b_bytes, stream, &ws);
+  if (rc) return rc;
+  float* xhi = static_cast<float*>(ws);
+  float* xlo = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + x_bytes);
+  float* bp = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + 2 * x_bytes);
+  f32_split_kernel<<<grid_for(x_elems / 4, 256, st.sms), 256, 0, stream>>>(
+      reinterpret_cast<const float4*>(x), reinterpret_cast<float4*>(xhi), reinterpret_cast<float4*>(xlo), x_elems / 4);
+  if ((rc = check_launch("f32_split_kernel launch"))) return rc;
+  f32_pack_taps_kernel<<<grid_for(static_cast<size_t>(g.k) * 3 * L, 256, st.sms), 256, 0, stream>>>(
+      w, bp, g.k, g.r, g.s, g.c, cpad, flip);
+  if ((rc = check_launch("f32_pack_taps_kernel launch"))) return rc;
+  TcArgs a{};
+  a.mode = 1;
+  a.tf32 = 1;
+  a.BK = 128;
+  a.cchunks = cpad / 32;
+  a.kb_third = g.r * g.s * a.cchunks;
+  a.num_kb = 3 * a.kb_third;
+  a.BN = pick_bn(g.k, 0);
+  a.M = g.n * g.ho * g.wo;
+  a.N = g.k;
+  a.batch = 1;
+  a.epi = Epilogue{kOutS32, 0, 0, 0, nullptr, nullptr, nullptr, 0.0f};
+  a.out = y;
+  a.ldc = g.k;
+  a.vec_ok = g.k % 4 == 0;
+  a.Ho = g.ho; a.Wo = g.wo; a.S = g.s;
+  a.stride_h = g.stride_h; a.stride_w = g.stride_w;
+  a.pad_h = g.pad_h; a.pad_w = g.pad_w;
+  a.dil_h = g.dil_h; a.dil_w = g.dil_w;
+  // the fp32 tensor as bytes: 4 * c byte channels per pixel, 128-byte (32-float) channel boxes
+  ConvGeom gb = g;
+  gb.c = 4 * g.c;
+  CUtensorMap ma, ma2, mb;
+  if ((rc = encode_im2col(&ma, reinterpret_cast<const int8_t*>(xhi), gb, 128))) return rc;
+  if ((rc = encode_im2col(&ma2, reinterpret_cast<const int8_t*>(xlo), gb, 128))) return rc;
+  if ((rc = encode_tiled_3d(&mb, bp, 12ull * L, static_cast<uint64_t>(g.k), 1, 128, a.BN, 128))) return rc;
+  if ((rc = launch_tc(st, ma, mb, a, stream, &ma2))) return rc;
+  g_last_path = 13;
+  return B200Q_OK;
+}
+
 int f32_fprop(const DeviceState& st, const float* x, const float* w, const float* bias, int bias_mode, float* y,
               const ConvGeom& g, cudaStream_t stream) {
+  if (!bias && f32_im2col_ok(g, x, y)) return f32_conv_im2col(st, x, w, y, g, 0, stream);
   const int G = g.groups, nblk = g.by * g.bx, Gp = nblk * G;
   const int mb = g.n * g.bho * g.bwo, T = g.r * g.s * g.cg;
   const F32Pack qa = f32_conv_pack(g, kPackIm2colRows, mb, T, Gp, 4, mb);
@@ -773,6 +840,16 @@ int f32_fprop(const DeviceState& st, const float* x, const float* w, const float
 
 int f32_bprop(const DeviceState& st, const float* dy, const float* w, float* dx, const ConvGeom& g,
               cudaStream_t stream) {
+  // Stride 1: dx is the conv of dy with the flipped, transposed filter and padding dil * (R - 1) - pad.
+  if (g.stride_h == 1 && g.stride_w == 1 && g.groups == 1 && g.by == 1 && g.bx == 1) {
+    ConvGeom gb = g;
+    gb.h = g.ho; gb.w = g.wo; gb.c = g.k;
+    gb.ho = g.h; gb.wo = g.w; gb.k = g.c;
+    gb.pad_h = g.dil_h * (g.r - 1) - g.pad_h;
+    gb.pad_w = g.dil_w * (g.s - 1) - g.pad_w;
+    gb.cg = gb.c; gb.kg = gb.k; gb.bho = gb.ho; gb.bwo = gb.wo;
+    if (gb.pad_h >= 0 && gb.pad_w >= 0 && f32_im2col_ok(gb, dy, dx)) return f32_conv_im2col(st, dy, w, dx, gb, 1, stream);
+  }
   const int G = g.groups, nblk = g.by * g.bx, Gp = nblk * G;
   const int mb = g.n * g.bho * g.bwo, T = g.r * g.s * g.cg;
   const F32Pack qa = f32_conv_pack(g, kPackDyRows, mb, g.kg, Gp, 4, mb);

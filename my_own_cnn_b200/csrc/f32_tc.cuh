@@ -288,6 +288,51 @@ __global__ void __launch_bounds__(256) f32_dbias_kernel(const float* __restrict_
   }
 }
 
+// ---- fp32 convs through the im2col TMA (groups == 1, no blocks): the input is split once into hi
+// and lo copies (which stay in L2 for typical sizes) and the tensor core reads the taps straight
+// from them, three passes over the taps ([hi | hi | lo] against packed weights [hi | lo | hi]).
+
+__global__ void f32_split_kernel(const float4* __restrict__ x, float4* __restrict__ hi, float4* __restrict__ lo,
+                                 size_t n4) {
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n4;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const float4 v = __ldg(x + i);
+    float4 h, l;
+    tf32_split(v.x, h.x, l.x);
+    tf32_split(v.y, h.y, l.y);
+    tf32_split(v.z, h.z, l.z);
+    tf32_split(v.w, h.w, l.w);
+    hi[i] = h;
+    lo[i] = l;
+  }
+}
+
+// Packed weights for the im2col-TMA conv: row k' of 3 x L floats, L = R * S * cpad (channels padded
+// to cpad, a multiple of 32 = one 128-byte K block), thirds [hi | lo | hi].  flip = 0: the conv's
+// own KRSC filter (k' = k, channel c); flip = 1: the data-gradient filter of a stride-1 conv,
+// w'[k'][r][s][c] = w[c][R-1-r][S-1-s][k'] with w in KRSC of shape [cin_t][R][S][kout_t] terms.
+__global__ void f32_pack_taps_kernel(const float* __restrict__ w, float* __restrict__ dst, int kout, int r, int s,
+                                     int cin, int cpad, int flip) {
+  const int L = r * s * cpad;
+  const size_t total = static_cast<size_t>(kout) * 3 * L;
+  for (size_t idx = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; idx < total;
+       idx += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const int j = static_cast<int>(idx % (3 * L));
+    const int kp = static_cast<int>(idx / (3 * L));
+    const int third = j / L, jj = j - third * L;
+    const int tap = jj / cpad, c = jj - tap * cpad;
+    float v = 0.0f;
+    if (c < cin) {
+      const int rr = tap / s, ss = tap - rr * s;
+      v = flip ? __ldg(w + ((static_cast<size_t>(c) * r + (r - 1 - rr)) * s + (s - 1 - ss)) * kout + kp)
+               : __ldg(w + ((static_cast<size_t>(kp) * r + rr) * s + ss) * cin + c);
+    }
+    float hi, lo;
+    tf32_split(v, hi, lo);
+    dst[idx] = third == 1 ? lo : hi;
+  }
+}
+
 // ---- direct CUDA-core kernels for groups of a few channels (depthwise and the like), where a GEMM
 // per group would have 1-4 rows or columns.  The loops are the reference's (src/cpu_ref.cpp:116-371)
 // with fp32 fused multiply-adds.

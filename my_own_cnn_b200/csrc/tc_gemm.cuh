@@ -21,8 +21,12 @@
 
 namespace b200q {
 
-constexpr int kTcThreads = 320;  // producer warp, MMA warp, 8 epilogue warps
-constexpr int kTcEpiWarps = 8;
+#ifndef B200Q_EPI_PER_QUARTER
+#define B200Q_EPI_PER_QUARTER 2
+#endif
+constexpr int kTcEpiPerQuarter = B200Q_EPI_PER_QUARTER;  // epilogue warps per TMEM lane quarter
+constexpr int kTcEpiWarps = 4 * kTcEpiPerQuarter;
+constexpr int kTcThreads = 64 + 32 * kTcEpiWarps;  // producer warp, MMA warp, epilogue warps
 constexpr int kTcBM = 128;
 
 struct TcArgs {
@@ -70,6 +74,7 @@ struct TcArgs {
   float hi_f;   // float(epi.hi), for the float-domain clamp of quant4_s8<2>
   int ab_unsigned;  // both operands unsigned 8-bit (the quantized-int32 drop-in's U8 codes)
   int tf32;         // fp32 operands, kind::tf32 MMAs, fp32 accumulators copied out bit for bit
+  int kb_third;     // fp32 im2col convs: K blocks per third of the split reduction (0 otherwise)
 };
 
 constexpr int kTcMaxAcc = 8;
@@ -101,7 +106,8 @@ __device__ __forceinline__ uint32_t pack4_sat_s8(int a, int b, int c, int d) {
 // CL selects how the clamp is done: 0 in integers (any bounds and zero point); 1 by the
 // saturating pack alone (the default range [-128, 127], zero point 0); 2 in floats before the
 // conversion (zero point 0 and lo = 0, the ReLU / ReLU6 forms: max(NaN, 0) = 0 matches
-// rint_sat(NaN) = 0, and integer bounds commute with rounding), the upper bound 127 by the pack.
+// rint_sat(NaN) = 0, and integer bounds commute with rounding), the upper bound 127 by the pack;
+// 4 as 2 when hi >= 127 (plain ReLU): only the lower bound in floats, the pack does the rest.
 template <int CL>
 __device__ __forceinline__ uint32_t quant4_s8(const TcArgs& a, float f0, float f1, float f2, float f3) {
   const Epilogue& e = a.epi;
@@ -109,6 +115,9 @@ __device__ __forceinline__ uint32_t quant4_s8(const TcArgs& a, float f0, float f
     const float hi = a.hi_f;
     f0 = fminf(fmaxf(f0, 0.0f), hi); f1 = fminf(fmaxf(f1, 0.0f), hi);
     f2 = fminf(fmaxf(f2, 0.0f), hi); f3 = fminf(fmaxf(f3, 0.0f), hi);
+  }
+  if constexpr (CL == 4) {  // ReLU with upper bound >= 127: the saturating pack is the upper clamp
+    f0 = fmaxf(f0, 0.0f); f1 = fmaxf(f1, 0.0f); f2 = fmaxf(f2, 0.0f); f3 = fmaxf(f3, 0.0f);
   }
   int r0 = __float2int_rn(f0), r1 = __float2int_rn(f1), r2 = __float2int_rn(f2), r3 = __float2int_rn(f3);
   if constexpr (CL == 0) {
@@ -432,7 +441,7 @@ __device__ __forceinline__ void epilogue_role_t(const TcArgs& a, const CUtensorM
   const int row = rank * kTcBM + q * 32 + lane;
   int buf = 0;
   uint32_t acc_ph = 0;
-  int sel = half;  // this warp's chunks in the current tile: sel, sel + 2, ...
+  int sel = half;  // this warp's chunks in the current tile: sel, sel + E, ... (E warps per quarter)
   // Tile coordinates advance by `nunits` tiles per iteration as mixed-radix counters (batch item,
   // M tile, N tile; for row tiles image and block of output rows): no integer division per tile.
   TileWalk tw(unit, nunits, a.batch, a.m_tiles, a.n_tiles);
@@ -442,7 +451,8 @@ __device__ __forceinline__ void epilogue_role_t(const TcArgs& a, const CUtensorM
   // Row tile: TMEM row -> (tile row ti, column wo) at pitch P; pitch padding and rows past the
   // tile or the image are not stored.
   const int ti = rt ? row / a.rt_P : 0, two = rt ? row - ti * a.rt_P : 0;
-  for (int tile = unit; tile < a.total_tiles; tile += nunits, sel ^= 1, tw.next(), rw.next()) {
+  for (int tile = unit; tile < a.total_tiles;
+       tile += nunits, sel = (sel + 1 == kTcEpiPerQuarter ? 0 : sel + 1), tw.next(), rw.next()) {
     const int b = tw.b, mt = tw.mt, nt = tw.nt;
     int m = mt * TM + row;
     const int n0 = nt * a.BN;
@@ -456,7 +466,7 @@ __device__ __forceinline__ void epilogue_role_t(const TcArgs& a, const CUtensorM
     // Chunks holding columns < N; the two warps of a lane quarter swap parities every tile, so an
     // odd chunk count (N <= 32, N = 96, ...) is shared evenly over two tiles.
     const int nvalid = (min(a.BN, a.N - n0) + 31) >> 5;
-    const int nmine = (nvalid - sel + 1) >> 1;
+    const int nmine = nvalid > sel ? (nvalid - sel + kTcEpiPerQuarter - 1) / kTcEpiPerQuarter : 0;
     if (!mbar_wait_bounded(accf0 + 8 * buf, acc_ph, a.wait_limit, a.err, kDevErrTimeoutEpilogue)) break;
     tc_fence_after();
     const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(buf * a.BN);
@@ -465,7 +475,7 @@ __device__ __forceinline__ void epilogue_role_t(const TcArgs& a, const CUtensorM
     const int mrow0 = mt * TM + rank * kTcBM + q * 32;
     for (int i = 0; i < nmine; ++i) {
       uint32_t va[32];
-      const int ca = sel + 2 * i;
+      const int ca = sel + kTcEpiPerQuarter * i;
       tmem_ld_32x32b_x32(tbase + ca * 32, va);
       tmem_ld_wait();
       emit_chunk<KIND, TMA, CL, RES>(a, tmC, va, b, m, mrow0, row_off, n0 + ca * 32, lane, sbufs, sb, bias, scale,
@@ -498,7 +508,9 @@ __device__ __forceinline__ void epilogue_role(const TcArgs& a, const CUtensorMap
   epilogue_role_t<KIND, TMA, CL, PAIR, RES>(a, tmC, tmem_base, accf0, acce0, warp, lane, bias, scale, has_bias, \
                                             sbufs)
 #define B200Q_EPI_CL(TMA, RES)     \
-  if (cl == 1)                     \
+  if (cl == 4)                     \
+    B200Q_EPI(TMA, 4, RES);        \
+  else if (cl == 1)                \
     B200Q_EPI(TMA, 1, RES);        \
   else if (cl == 2)                \
     B200Q_EPI(TMA, 2, RES);        \
@@ -510,7 +522,7 @@ __device__ __forceinline__ void epilogue_role(const TcArgs& a, const CUtensorMap
     else
       B200Q_EPI(false, 0, false);
   } else {
-    const int cl = a.default_clamp ? 1 : (a.epi.zp == 0 && a.epi.lo == 0) ? 2 : 0;
+    const int cl = a.default_clamp ? 1 : (a.epi.zp == 0 && a.epi.lo == 0) ? (a.epi.hi >= 127 ? 4 : 2) : 0;
     if (a.epi.res) {
       if (a.tma_store) {
         B200Q_EPI_CL(true, true);
@@ -706,7 +718,8 @@ __device__ __forceinline__ bool gemm_mma_loop(const TcArgs& a, uint32_t tmem_bas
 
 __global__ void __launch_bounds__(kTcThreads, 1)
     tc_gemm_s8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                      const __grid_constant__ CUtensorMap tmC, const TcArgs a) {
+                      const __grid_constant__ CUtensorMap tmC, const TcArgs a,
+                      const __grid_constant__ CUtensorMap tmA2) {
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte alignment by pointer arithmetic on the shared window (an integer round trip would
   // turn every later access through these pointers into a generic load / store).
@@ -750,6 +763,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     fence_mbar_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    if (a.kb_third) tma_prefetch_desc(&tmA2);
   }
   if (warp == 1) {
     tmem_alloc(smem_u32(tmem_slot), a.tmem_cols);
@@ -836,11 +850,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           const uint32_t dA = smem_u32(sA + stage * stage_a);
           const uint32_t dB = smem_u32(sB + stage * stage_b);
           if (a.mode == 1) {
-            const int tap = kb / a.cchunks;
-            const int cc = kb - tap * a.cchunks;
+            // fp32 (tf32 split) convs walk the taps three times: thirds 0 and 1 read the hi copy
+            // of the input (tmA), third 2 the lo copy (tmA2)
+            const int third = a.kb_third ? kb / a.kb_third : 0;
+            const int kk = kb - third * a.kb_third;
+            const int tap = kk / a.cchunks;
+            const int cc = kk - tap * a.cchunks;
             const int r = tap / a.S;
             const int s = tap - r * a.S;
-            tma_load_im2col_4d(dA, &tmA, fb, cc * a.BK, wbase, hbase, img,
+            tma_load_im2col_4d(dA, third == 2 ? &tmA2 : &tmA, fb, cc * a.BK, wbase, hbase, img,
                                static_cast<uint16_t>(s * a.dil_w), static_cast<uint16_t>(r * a.dil_h));
           } else if (a.a_major == 0) {
             tma_load_3d(dA, &tmA, fb, kb * a.BK, m0, b);

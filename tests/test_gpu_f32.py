@@ -49,6 +49,11 @@ CASES = [
     (2, 12, 12, 32, 32, 3, 3, 1, 1, 2, 2, 1, 1, 32),     # depthwise, stride 2
     (3, 9, 9, 256, 96, 1, 1, 0, 0, 1, 1, 1, 1, 1),       # pointwise, K = 96
     (1, 23, 23, 3, 64, 7, 7, 3, 3, 2, 2, 1, 1, 1),       # stem
+    # inputs >= 128 KiB with C % 4 == 0: im2col TMA over hi / lo copies (fprop; bprop when stride 1)
+    (4, 28, 28, 64, 96, 3, 3, 1, 1, 2, 2, 1, 1, 1),      # stride 2
+    (2, 32, 32, 48, 64, 5, 5, 2, 2, 1, 1, 1, 1, 1),      # 5x5
+    (2, 40, 40, 32, 32, 3, 3, 2, 2, 1, 1, 2, 2, 1),      # dilation 2
+    (2, 40, 40, 36, 40, 3, 3, 1, 0, 1, 1, 1, 1, 1),      # C = 36 (channel padding to 64), asymmetric pad
 ]
 
 
