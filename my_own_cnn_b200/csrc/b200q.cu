@@ -162,6 +162,8 @@ int make_epilogue(const b200q_epilogue* epi, const int32_t* bias, const float* s
   out->scale = scale;
   out->res = nullptr;
   out->res_scale = 0.0f;
+  out->rowterm = nullptr;
+  out->rowzx = nullptr;
   return B200Q_OK;
 }
 
@@ -474,7 +476,7 @@ int qi32_tensor_core(const DeviceState& st, int qtype, const float* x, const flo
   const bool in_place = q.gcount == 1;  // the GEMM writes y directly; the fixup corrects in place
   const size_t a_bytes = round256(static_cast<size_t>(arows) * q.kp);
   const size_t b_bytes = round256(static_cast<size_t>(brows) * q.kp);
-  const size_t rt_bytes = round256(static_cast<size_t>(arows) * 4);
+  const size_t rt_bytes = round256(static_cast<size_t>(arows) * 4) * 2;  // row terms, then row zero points
   const size_t cs_bytes = round256(static_cast<size_t>(brows) * 4);
   const size_t c_bytes = in_place ? 0 : round256(static_cast<size_t>(arows) * g.kg * 4);
   void* ws = nullptr;
@@ -484,6 +486,7 @@ int qi32_tensor_core(const DeviceState& st, int qtype, const float* x, const flo
   uint32_t* a_buf = reinterpret_cast<uint32_t*>(base);
   uint32_t* b_buf = reinterpret_cast<uint32_t*>(base + a_bytes);
   int32_t* rowterm = reinterpret_cast<int32_t*>(base + a_bytes + b_bytes);
+  int32_t* rowzx = reinterpret_cast<int32_t*>(base + a_bytes + b_bytes + rt_bytes / 2);
   int32_t* colsum = reinterpret_cast<int32_t*>(base + a_bytes + b_bytes + rt_bytes);
   int32_t* cbuf = in_place ? y : reinterpret_cast<int32_t*>(base + a_bytes + b_bytes + rt_bytes + cs_bytes);
   int* flag = reinterpret_cast<int*>(base + a_bytes + b_bytes + rt_bytes + cs_bytes + c_bytes);
@@ -492,7 +495,7 @@ int qi32_tensor_core(const DeviceState& st, int qtype, const float* x, const flo
   const uint8_t* iq = static_cast<const uint8_t*>(in_qp);
   const uint8_t* fq = static_cast<const uint8_t*>(f_qp);
   qi32_pack_rows_kernel<<<grid_for(static_cast<size_t>(arows) * 32, 256, st.sms), 256, 0, stream>>>(
-      x, a_buf, rowterm, g, q, iq, fq, flag);
+      x, a_buf, rowterm, rowzx, g, q, iq, fq, flag);
   rc = check_launch("qi32_pack_rows_kernel launch");
   if (rc) return rc;
   qi32_pack_filter_kernel<<<grid_for(static_cast<size_t>(brows) * 32, 256, st.sms), 256, 0, stream>>>(
@@ -509,6 +512,11 @@ int qi32_tensor_core(const DeviceState& st, int qtype, const float* x, const flo
   a.b_batched = q.gcount > 1;
   a.num_kb = q.kp / a.BK;
   a.epi = Epilogue{kOutS32, 0, 0, 0, nullptr, nullptr, nullptr, 0.0f};
+  if (in_place) {  // one block, one group: the correction goes into the GEMM epilogue
+    a.epi.bias = colsum;
+    a.epi.rowterm = rowterm;
+    a.epi.rowzx = rowzx;
+  }
   a.out = cbuf;
   a.ldc = g.kg;
   a.batch_stride = static_cast<long long>(q.mb) * g.kg;
@@ -526,12 +534,13 @@ int qi32_tensor_core(const DeviceState& st, int qtype, const float* x, const flo
   if (rc) return rc;
   const size_t total = static_cast<size_t>(g.n) * g.ho * g.wo * g.k;
   const bool v4 = g.kg % 4 == 0 && aligned16(y) && aligned16(cbuf);
+  const int fused = in_place ? 1 : 0;
   if (v4)
     qi32_fixup_kernel<4><<<grid_for(total / 4, 256, st.sms), 256, 0, stream>>>(cbuf, y, rowterm, colsum, g, q, iq, fq,
-                                                                              flag, x, w);
+                                                                              flag, x, w, fused);
   else
     qi32_fixup_kernel<1><<<grid_for(total, 256, st.sms), 256, 0, stream>>>(cbuf, y, rowterm, colsum, g, q, iq, fq,
-                                                                          flag, x, w);
+                                                                          flag, x, w, fused);
   rc = check_launch("qi32_fixup_kernel launch");
   if (rc) return rc;
   g_last_path = 11;
@@ -547,7 +556,9 @@ int qi32_common(int qtype, const float* x, const float* w, int32_t* y, const Con
   DeviceState* st = nullptr;
   int rc = device_state(&st);
   if (rc) return rc;
-  if (g_policy.load() == 0) {
+  // Groups of a few channels (depthwise and the like: (c/groups) * (k/groups) <= 16) stay on the
+  // direct kernel: a GEMM per group would have 1-4 rows or columns.
+  if (g_policy.load() == 0 && static_cast<long long>(g.cg) * g.kg > 16) {
     rc = qi32_tensor_core(*st, qtype, x, w, y, g, in_qp, f_qp, as_stream(stream));
     if (rc != B200Q_ERR_UNSUPPORTED) return rc;
   }
@@ -739,16 +750,16 @@ bool f32_sizes_ok(const ConvGeom& g) {
   return mb < (1ll << 30) && T < (1 << 24) && static_cast<long long>(g.by) * g.bx * g.groups < (1 << 16);
 }
 
-// Whether a regular fp32 conv of this geometry (input x of g.c channels) can run through the
-// im2col TMA: groups == 1, no blocks, 16-byte pixel rows and pointers, the im2col corner limits,
-// and at least 128 KiB of input (smaller im2col maps take the packed route).
+// Whether an fp32 conv of this geometry (input x of g.c channels) can run through the im2col TMA:
+// no blocks, 16-byte group channel starts and pointers, the im2col corner limits, and at least
+// 128 KiB of input (smaller im2col maps take the packed route).  Groups are batch items.
 bool f32_im2col_ok(const ConvGeom& g, const void* x, const void* y) {
   const bool corners_ok = g.pad_w <= 127 && g.pad_h <= 127 && g.pad_w - (g.s - 1) * g.dil_w >= -128 &&
                           g.pad_h - (g.r - 1) * g.dil_h >= -128 && (g.s - 1) * g.dil_w <= 255 &&
                           (g.r - 1) * g.dil_h <= 255 && g.stride_h <= 8 && g.stride_w <= 8;
   const long long M = static_cast<long long>(g.n) * g.ho * g.wo;
   const size_t x_bytes = static_cast<size_t>(g.n) * g.h * g.w * g.c * 4;
-  return g.groups == 1 && g.by == 1 && g.bx == 1 && g.c % 4 == 0 && aligned16(x) && aligned16(y) && corners_ok &&
+  return g.by == 1 && g.bx == 1 && g.cg % 4 == 0 && aligned16(x) && aligned16(y) && corners_ok &&
          x_bytes >= (128u << 10) && M < (1ll << 31) && g.k <= 65535;
 }
 
@@ -756,7 +767,7 @@ bool f32_im2col_ok(const ConvGeom& g, const void* x, const void* y) {
 // stride-1 conv (flip = 1, see f32_pack_taps_kernel), written to y [n,ho,wo,k] directly.
 int f32_conv_im2col(const DeviceState& st, const float* x, const float* w, float* y, const ConvGeom& g, int flip,
                     cudaStream_t stream) {
-  const int cpad = (g.c + 31) / 32 * 32;
+  const int cpad = (g.cg + 31) / 32 * 32;
   const int L = g.r * g.s * cpad;
   const size_t x_elems = static_cast<size_t>(g.n) * g.h * g.w * g.c;
   const size_t x_bytes = round256(x_elems * 4);
@@ -771,7 +782,7 @@ int f32_conv_im2col(const DeviceState& st, const float* x, const float* w, float
       reinterpret_cast<const float4*>(x), reinterpret_cast<float4*>(xhi), reinterpret_cast<float4*>(xlo), x_elems / 4);
   if ((rc = check_launch("f32_split_kernel launch"))) return rc;
   f32_pack_taps_kernel<<<grid_for(static_cast<size_t>(g.k) * 3 * L, 256, st.sms), 256, 0, stream>>>(
-      w, bp, g.k, g.r, g.s, g.c, cpad, flip);
+      w, bp, g.k, g.r, g.s, g.cg, cpad, flip, g.kg);
   if ((rc = check_launch("f32_pack_taps_kernel launch"))) return rc;
   TcArgs a{};
   a.mode = 1;
@@ -780,14 +791,17 @@ int f32_conv_im2col(const DeviceState& st, const float* x, const float* w, float
   a.cchunks = cpad / 32;
   a.kb_third = g.r * g.s * a.cchunks;
   a.num_kb = 3 * a.kb_third;
-  a.BN = pick_bn(g.k, 0);
+  a.BN = pick_bn(g.kg, 0);
   a.M = g.n * g.ho * g.wo;
-  a.N = g.k;
-  a.batch = 1;
+  a.N = g.kg;
+  a.batch = g.groups;  // group b: channels from b * cg, filter rows b * kg.., output columns b * kg..
+  a.b_batched = g.groups > 1;
+  a.grp_bytes = 4 * g.cg;
+  a.batch_stride = g.kg;
   a.epi = Epilogue{kOutS32, 0, 0, 0, nullptr, nullptr, nullptr, 0.0f};
   a.out = y;
   a.ldc = g.k;
-  a.vec_ok = g.k % 4 == 0;
+  a.vec_ok = g.kg % 4 == 0 && g.k % 4 == 0;
   a.Ho = g.ho; a.Wo = g.wo; a.S = g.s;
   a.stride_h = g.stride_h; a.stride_w = g.stride_w;
   a.pad_h = g.pad_h; a.pad_w = g.pad_w;
@@ -798,7 +812,9 @@ int f32_conv_im2col(const DeviceState& st, const float* x, const float* w, float
   CUtensorMap ma, ma2, mb;
   if ((rc = encode_im2col(&ma, reinterpret_cast<const int8_t*>(xhi), gb, 128))) return rc;
   if ((rc = encode_im2col(&ma2, reinterpret_cast<const int8_t*>(xlo), gb, 128))) return rc;
-  if ((rc = encode_tiled_3d(&mb, bp, 12ull * L, static_cast<uint64_t>(g.k), 1, 128, a.BN, 128))) return rc;
+  if ((rc = encode_tiled_3d(&mb, bp, 12ull * L, static_cast<uint64_t>(g.kg), static_cast<uint64_t>(g.groups), 128,
+                            a.BN, 128)))
+    return rc;
   if ((rc = launch_tc(st, ma, mb, a, stream, &ma2))) return rc;
   g_last_path = 13;
   return B200Q_OK;
@@ -841,13 +857,13 @@ int f32_fprop(const DeviceState& st, const float* x, const float* w, const float
 int f32_bprop(const DeviceState& st, const float* dy, const float* w, float* dx, const ConvGeom& g,
               cudaStream_t stream) {
   // Stride 1: dx is the conv of dy with the flipped, transposed filter and padding dil * (R - 1) - pad.
-  if (g.stride_h == 1 && g.stride_w == 1 && g.groups == 1 && g.by == 1 && g.bx == 1) {
+  if (g.stride_h == 1 && g.stride_w == 1 && g.by == 1 && g.bx == 1) {
     ConvGeom gb = g;
     gb.h = g.ho; gb.w = g.wo; gb.c = g.k;
     gb.ho = g.h; gb.wo = g.w; gb.k = g.c;
     gb.pad_h = g.dil_h * (g.r - 1) - g.pad_h;
     gb.pad_w = g.dil_w * (g.s - 1) - g.pad_w;
-    gb.cg = gb.c; gb.kg = gb.k; gb.bho = gb.ho; gb.bwo = gb.wo;
+    gb.cg = g.kg; gb.kg = g.cg; gb.bho = gb.ho; gb.bwo = gb.wo;
     if (gb.pad_h >= 0 && gb.pad_w >= 0 && f32_im2col_ok(gb, dy, dx)) return f32_conv_im2col(st, dy, w, dx, gb, 1, stream);
   }
   const int G = g.groups, nblk = g.by * g.bx, Gp = nblk * G;
@@ -1158,7 +1174,7 @@ static int conv2d_s8_impl(const int8_t* d_x, const int8_t* d_w, const int32_t* d
   int rc = conv_geom(n, h, w, c, r, s, k, p, 1, 1, &g);
   if (rc) return rc;
   if (!d_x || !d_w || !d_y) return fail(B200Q_ERR_INVALID_ARG, "null tensor pointer");
-  Epilogue e;
+  Epilogue e{};
   rc = make_epilogue(epi, d_bias, d_scale, &e);
   if (rc) return rc;
   if (d_res) {
@@ -1453,7 +1469,7 @@ int b200q_bmm_s8(const int8_t* A, const int8_t* B, const int32_t* d_bias, const 
   if (batch < 0 || M < 0 || N < 0 || K < 0) return fail(B200Q_ERR_INVALID_ARG, "negative bmm dimension");
   if (batch == 0 || M == 0 || N == 0) return B200Q_OK;
   if (!A || !B || !C) return fail(B200Q_ERR_INVALID_ARG, "null bmm pointer");
-  Epilogue e;
+  Epilogue e{};
   int rc = make_epilogue(epi, d_bias, d_col_scale, &e);
   if (rc) return rc;
   DeviceState* st = nullptr;
@@ -1561,7 +1577,7 @@ int b200q_conv2d_s8_packed_noalloc(const int8_t* d_x, const int8_t* d_w, const i
   if (rc) return rc;
   if (!d_x || !d_w || !d_y) return fail(B200Q_ERR_INVALID_ARG, "null tensor pointer");
   if (g.groups != 1) return fail(B200Q_ERR_UNSUPPORTED, "the fixed-scratch conv supports groups == 1 only");
-  Epilogue e;
+  Epilogue e{};
   rc = make_epilogue(epi, d_bias, d_scale, &e);
   if (rc) return rc;
   if (!aligned16(d_y) || (d_bias && !aligned16(d_bias)) || (d_scale && !aligned16(d_scale)))

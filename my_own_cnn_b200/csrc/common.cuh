@@ -24,6 +24,10 @@ struct Epilogue {
   const float* scale;   // required for S8 / F32
   const int8_t* res;    // int8 residual with the output's layout (S8 outputs only), or null
   float res_scale;
+  // int32 outputs only: per-row terms, t = acc + rowterm[m] - rowzx[m] * bias[col] instead of
+  // acc + bias[col] (the quantized-int32 drop-in's zero-point correction; null otherwise)
+  const int32_t* rowterm;
+  const int32_t* rowzx;
 };
 
 // Requantize one int32 value (bias already added, wrapping):

@@ -307,12 +307,14 @@ __global__ void f32_split_kernel(const float4* __restrict__ x, float4* __restric
   }
 }
 
-// Packed weights for the im2col-TMA conv: row k' of 3 x L floats, L = R * S * cpad (channels padded
-// to cpad, a multiple of 32 = one 128-byte K block), thirds [hi | lo | hi].  flip = 0: the conv's
-// own KRSC filter (k' = k, channel c); flip = 1: the data-gradient filter of a stride-1 conv,
-// w'[k'][r][s][c] = w[c][R-1-r][S-1-s][k'] with w in KRSC of shape [cin_t][R][S][kout_t] terms.
+// Packed weights for the im2col-TMA conv: row k' of 3 x L floats, L = R * S * cpad (the group's
+// cin channels padded to cpad, a multiple of 32 = one 128-byte K block), thirds [hi | lo | hi].
+// flip = 0: the conv's own filter [kout][R][S][cin] (row k', channel c).  flip = 1: the data-gradient
+// filter of a stride-1 conv: row k' is input channel k' of the forward conv, in group
+// grp = k' / kout_g; its channel c is the forward conv's output channel grp * cin + c, and
+// w'[k'][r][s][c] = w[grp * cin + c][R-1-r][S-1-s][k' - grp * kout_g] (forward filter [K][R][S][kout_g]).
 __global__ void f32_pack_taps_kernel(const float* __restrict__ w, float* __restrict__ dst, int kout, int r, int s,
-                                     int cin, int cpad, int flip) {
+                                     int cin, int cpad, int flip, int kout_g) {
   const int L = r * s * cpad;
   const size_t total = static_cast<size_t>(kout) * 3 * L;
   for (size_t idx = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; idx < total;
@@ -324,8 +326,13 @@ __global__ void f32_pack_taps_kernel(const float* __restrict__ w, float* __restr
     float v = 0.0f;
     if (c < cin) {
       const int rr = tap / s, ss = tap - rr * s;
-      v = flip ? __ldg(w + ((static_cast<size_t>(c) * r + (r - 1 - rr)) * s + (s - 1 - ss)) * kout + kp)
-               : __ldg(w + ((static_cast<size_t>(kp) * r + rr) * s + ss) * cin + c);
+      if (flip) {
+        const int grp = kp / kout_g;
+        v = __ldg(w + ((static_cast<size_t>(grp * cin + c) * r + (r - 1 - rr)) * s + (s - 1 - ss)) * kout_g +
+                  (kp - grp * kout_g));
+      } else {
+        v = __ldg(w + ((static_cast<size_t>(kp) * r + rr) * s + ss) * cin + c);
+      }
     }
     float hi, lo;
     tf32_split(v, hi, lo);

@@ -18,6 +18,9 @@
 //   qi32_pack_filter_kernel  float weights -> 8-bit rows [G'][Kg][Kp] and their sums  sum b_j;
 //   tc_gemm_s8_kernel        C[G'][Mb][Kg] = A . B^T  (int32 out, unsigned or signed operands);
 //   qi32_fixup_kernel        y[n,ho,wo,k] = C + rowterm - zx * colsum, scattered to NHWC.
+// A regular conv (one block, one group) takes the correction in the GEMM's int32 epilogue instead
+// (Epilogue::rowterm / rowzx, the column sums as its bias) and writes y directly; the fixup kernel
+// then only runs the out-of-range fallback, returning at once when the flag is clear.
 // Codes whose truncated value does not fit the 8-bit operand type (U8 outside [0, 255], S5
 // outside [-128, 127]) set a device flag in the pack kernels; the fixup kernel then computes every
 // output directly on CUDA cores (qi32_direct), so out-of-range inputs still give the reference's
@@ -79,7 +82,8 @@ struct Qi32Pack {
 // One warp per packed row (gp, mb): gp = block * groups + group, mb = (image, row, column) inside
 // the output block.  Each lane builds 4-byte words of the row; the row sum is reduced over the warp.
 __global__ void __launch_bounds__(256) qi32_pack_rows_kernel(const float* __restrict__ x, uint32_t* __restrict__ a,
-                                                             int32_t* __restrict__ rowterm, ConvGeom g, Qi32Pack q,
+                                                             int32_t* __restrict__ rowterm, int32_t* __restrict__ rowzx,
+                                                             ConvGeom g, Qi32Pack q,
                                                              const uint8_t* __restrict__ in_qp,
                                                              const uint8_t* __restrict__ f_qp, int* __restrict__ flag) {
   const int lane = threadIdx.x & 31;
@@ -141,9 +145,11 @@ __global__ void __launch_bounds__(256) qi32_pack_rows_kernel(const float* __rest
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xFFFFFFFFu, sum, o);
-    if (lane == 0)
+    if (lane == 0) {
       rowterm[row] = static_cast<int32_t>(static_cast<uint32_t>(q.T) * static_cast<uint32_t>(zx) * static_cast<uint32_t>(zf) -
                                           static_cast<uint32_t>(zf) * sum);
+      rowzx[row] = zx;
+    }
   }
   if (__any_sync(0xFFFFFFFFu, bad) && lane == 0) atomicOr(flag, 1);
 }
@@ -200,10 +206,13 @@ __global__ void __launch_bounds__(256) qi32_fixup_kernel(const int32_t* src, int
                                                          const int32_t* __restrict__ colsum, ConvGeom g, Qi32Pack q,
                                                          const uint8_t* __restrict__ in_qp,
                                                          const uint8_t* __restrict__ f_qp, const int* __restrict__ flag,
-                                                         const float* __restrict__ x, const float* __restrict__ w) {
+                                                         const float* __restrict__ x, const float* __restrict__ w,
+                                                         int fused) {
   const size_t total = static_cast<size_t>(g.n) * g.ho * g.wo * g.k;
   const size_t items = total / V;
   const bool direct = *flag != 0;
+  // fused: the GEMM epilogue already applied the correction; only the out-of-range fallback is left
+  if (fused && !direct) return;
   const int zf = load_zp(f_qp, 0, q.qp_stride, q.qp_signed);
   for (size_t it = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; it < items;
        it += static_cast<size_t>(gridDim.x) * blockDim.x) {

@@ -75,6 +75,7 @@ struct TcArgs {
   int ab_unsigned;  // both operands unsigned 8-bit (the quantized-int32 drop-in's U8 codes)
   int tf32;         // fp32 operands, kind::tf32 MMAs, fp32 accumulators copied out bit for bit
   int kb_third;     // fp32 im2col convs: K blocks per third of the split reduction (0 otherwise)
+  int grp_bytes;    // fp32 im2col convs: bytes between the channel starts of consecutive groups (batch items)
 };
 
 constexpr int kTcMaxAcc = 8;
@@ -473,13 +474,31 @@ __device__ __forceinline__ void epilogue_role_t(const TcArgs& a, const CUtensorM
     const size_t row_off =
         (!PAIR && a.mode == 2) ? rt_off : static_cast<size_t>(b) * a.batch_stride + static_cast<size_t>(m) * a.ldc;
     const int mrow0 = mt * TM + rank * kTcBM + q * 32;
+    // int32 outputs with per-row terms: t = acc + rowterm[m] - rowzx[m] * bias[col] (one load per row and tile)
+    int32_t rterm = 0, rzx = 0;
+    const bool rowmode = KIND == kOutS32 && a.epi.rowterm != nullptr;
+    if (rowmode && m < a.M) {
+      rterm = __ldg(a.epi.rowterm + m);
+      rzx = __ldg(a.epi.rowzx + m);
+    }
     for (int i = 0; i < nmine; ++i) {
       uint32_t va[32];
       const int ca = sel + kTcEpiPerQuarter * i;
       tmem_ld_32x32b_x32(tbase + ca * 32, va);
       tmem_ld_wait();
+      if constexpr (KIND == kOutS32) {
+        if (rowmode) {
+          const int nc = n0 + ca * 32;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const int32_t bj = (nc + j < a.N) ? bias[nc + j] : 0;
+            va[j] = static_cast<uint32_t>(va[j]) + static_cast<uint32_t>(rterm) -
+                    static_cast<uint32_t>(rzx) * static_cast<uint32_t>(bj);
+          }
+        }
+      }
       emit_chunk<KIND, TMA, CL, RES>(a, tmC, va, b, m, mrow0, row_off, n0 + ca * 32, lane, sbufs, sb, bias, scale,
-                                 has_bias);
+                                 has_bias && !rowmode);
     }
     tc_fence_before();
     __syncwarp();
@@ -858,7 +877,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             const int cc = kk - tap * a.cchunks;
             const int r = tap / a.S;
             const int s = tap - r * a.S;
-            tma_load_im2col_4d(dA, third == 2 ? &tmA2 : &tmA, fb, cc * a.BK, wbase, hbase, img,
+            // grouped fp32 convs: batch item b is group b, whose channels start grp_bytes later
+            tma_load_im2col_4d(dA, third == 2 ? &tmA2 : &tmA, fb, cc * a.BK + b * a.grp_bytes, wbase, hbase, img,
                                static_cast<uint16_t>(s * a.dil_w), static_cast<uint16_t>(r * a.dil_h));
           } else if (a.a_major == 0) {
             tma_load_3d(dA, &tmA, fb, kb * a.BK, m0, b);

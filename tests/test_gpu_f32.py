@@ -54,6 +54,8 @@ CASES = [
     (2, 32, 32, 48, 64, 5, 5, 2, 2, 1, 1, 1, 1, 1),      # 5x5
     (2, 40, 40, 32, 32, 3, 3, 2, 2, 1, 1, 2, 2, 1),      # dilation 2
     (2, 40, 40, 36, 40, 3, 3, 1, 0, 1, 1, 1, 1, 1),      # C = 36 (channel padding to 64), asymmetric pad
+    (2, 28, 28, 64, 64, 3, 3, 1, 1, 1, 1, 1, 1, 4),      # groups 4 on the im2col route (group = batch item)
+    (2, 24, 24, 72, 48, 3, 3, 1, 1, 1, 1, 1, 1, 2),      # groups 2, 36 channels per group
 ]
 
 
