@@ -90,6 +90,10 @@ typedef struct b200q_epilogue {
  * d_in_qp: device array of n qparams (per image), d_f_qp: device pointer to one qparams,
  * of the struct type selected by qtype.
  * y = sum over valid taps of (x - zp_in[img]) * (w - zp_f), int32 wrapping.
+ * Runs on tcgen05 tensor cores (raw 8-bit codes, zero points restored by per-row / per-column terms;
+ * codes outside the 8-bit range fall back to a direct computation on the device), except groups of
+ * (c/groups) * (k/groups) <= 16 channel pairs, which run on a direct CUDA-core kernel.  Uses the
+ * stream's workspace for the 8-bit operands.
  * Replaces conv_quant_detail::launch_fprop_nhwc_qi32_{u8,s5} (src/conv_types.h:232-241). */
 int b200q_fprop_nhwc_qi32(int qtype, const float* d_x, const float* d_w, int32_t* d_y, int n, int h,
                           int w, int c, int r, int s, int k, const b200q_conv_params* p,
