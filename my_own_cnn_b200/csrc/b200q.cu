@@ -322,6 +322,13 @@ const int g_pair_min_k = [] {
   return v ? atoi(v) : 2048;
 }();
 
+// Row groups per space-to-depth row tile (env B200Q_RT_GROUPS, for A/B timing; 1 = one group).
+const int g_rt_groups = [] {
+  const char* v = getenv("B200Q_RT_GROUPS");
+  const int n = v ? atoi(v) : 4;
+  return n < 1 ? 1 : (n > 8 ? 8 : n);
+}();
+
 // Space-to-depth stem switch (env B200Q_S2D=0 keeps low-channel stride-2 convs on the packed
 // path, for A/B timing).
 const bool g_s2d = [] {
@@ -395,15 +402,17 @@ int launch_tc(const DeviceState& st, const CUtensorMap& ma, const CUtensorMap& m
   if (stages < 2) return fail(B200Q_ERR_UNSUPPORTED, "tile does not fit shared memory");
   a.stages = stages;
   const int tile_m = a.pair ? 2 * kTcBM : kTcBM;
-  a.m_tiles = a.mode == 2 ? a.n_img * ((a.Ho + a.rt_T - 1) / a.rt_T) : (a.M + tile_m - 1) / tile_m;
+  if (a.rt_G < 1) a.rt_G = 1;
+  a.m_tiles = a.mode == 2 ? a.n_img * ((a.Ho + a.rt_T * a.rt_G - 1) / (a.rt_T * a.rt_G)) : (a.M + tile_m - 1) / tile_m;
   const long long total = static_cast<long long>(a.batch) * a.m_tiles * a.n_tiles;
   if (total > 0x7FFFFFFFll) return fail(B200Q_ERR_UNSUPPORTED, "too many tiles");
   a.total_tiles = static_cast<int>(total);
   // As many accumulator buffers as the 512 TMEM columns hold: short reductions finish a tile
   // every few hundred cycles, and the MMA warp must not wait for the epilogue's turnaround.
-  a.nacc = g_nacc_max < 512 / a.BN ? g_nacc_max : 512 / a.BN;
-  if (a.nacc < 2) a.nacc = 2;
-  a.tmem_cols = static_cast<uint32_t>(a.nacc * a.BN);
+  a.acc_cols = a.BN * a.rt_G;
+  a.nacc = g_nacc_max < 512 / a.acc_cols ? g_nacc_max : 512 / a.acc_cols;
+  if (a.nacc < 2) return fail(B200Q_ERR_UNSUPPORTED, "accumulator does not fit tensor memory twice");
+  a.tmem_cols = static_cast<uint32_t>(a.nacc * a.acc_cols);
   const uint32_t sgn = a.ab_unsigned ? 0u : 1u;       // kind::i8 operand type: 0 = u8, 1 = s8
   const uint32_t dfmt = a.tf32 ? 1u : 2u;               // D = f32 (kind::tf32) or s32 (kind::i8)
   const uint32_t abfmt = a.tf32 ? 2u : sgn;             // kind::tf32 operand format: 2 = TF32
@@ -1246,9 +1255,16 @@ static int conv2d_s8_impl(const int8_t* d_x, const int8_t* d_w, const int32_t* d
       a.rt_x0 = xoff;
       a.rt_y0 = yoff;
       a.rt_plane = 16;  // K-direction core-matrix stride: one pixel
-      // Window rows: the last tap slice of the tile's last accumulator row reads pixel
-      // (r2 - 1) * P + s2 - 1 + 127, which must stay inside the box.
-      const int rows = ((r2 - 1) * P + s2 - 1 + 128 + P - 1) / P;
+      // Row groups: up to g_rt_groups groups of rt_T output rows per tile (one window, one TMEM
+      // buffer of BN columns per group, two buffers in tensor memory).
+      a.rt_G = g_rt_groups;
+      if (a.rt_G > 256 / bn) a.rt_G = 256 / bn;
+      const int row_blocks = (g.ho + a.rt_T - 1) / a.rt_T;
+      if (a.rt_G > row_blocks) a.rt_G = row_blocks;
+      if (a.rt_G < 1) a.rt_G = 1;
+      // Window rows: the last tap slice of the last group's last accumulator row reads pixel
+      // (rt_G - 1) * rt_T * P + (r2 - 1) * P + s2 - 1 + 127, which must stay inside the box.
+      const int rows = ((a.rt_G - 1) * a.rt_T * P + (r2 - 1) * P + s2 - 1 + 128 + P - 1) / P;
       a.rt_box = rows * P * 16;
       a.rt_stage = (a.rt_box + 1023) / 1024 * 1024;
       CUtensorMap ma, mb;

@@ -71,6 +71,10 @@ struct TcArgs {
   // matrix stride is one pixel (rt_plane = 16), so the second half of the slice is the next pixel.
   int rt_pairs, rt_R, rt_S;
   int rt_wide;  // window map in 8-byte elements {2 * W, H, N} (one channel plane): rows of whole pixels
+  // Row groups (tap-pair row tiles): a tile is rt_G groups of rt_T output rows sharing one window;
+  // group j accumulates into TMEM columns [j * BN, (j + 1) * BN) of the buffer, from the window
+  // started j * rt_T rows lower.  acc_cols = BN * rt_G columns per accumulator buffer.
+  int rt_G, acc_cols;
   float hi_f;   // float(epi.hi), for the float-domain clamp of quant4_s8<2>
   int ab_unsigned;  // both operands unsigned 8-bit (the quantized-int32 drop-in's U8 codes)
   int tf32;         // fp32 operands, kind::tf32 MMAs, fp32 accumulators copied out bit for bit
@@ -447,7 +451,8 @@ __device__ __forceinline__ void epilogue_role_t(const TcArgs& a, const CUtensorM
   // M tile, N tile; for row tiles image and block of output rows): no integer division per tile.
   TileWalk tw(unit, nunits, a.batch, a.m_tiles, a.n_tiles);
   const bool rt = !PAIR && a.mode == 2;
-  const int rblocks = rt ? (a.Ho + a.rt_T - 1) / a.rt_T : 1;
+  const int rt_tb = a.rt_T * a.rt_G;  // output rows per tile
+  const int rblocks = rt ? (a.Ho + rt_tb - 1) / rt_tb : 1;
   TileWalk rw(rt ? unit : 0, nunits, 1 << 30, rblocks, 1);  // (image, row block) of mode-2 tiles
   // Row tile: TMEM row -> (tile row ti, column wo) at pitch P; pitch padding and rows past the
   // tile or the image are not stored.
@@ -458,19 +463,22 @@ __device__ __forceinline__ void epilogue_role_t(const TcArgs& a, const CUtensorM
     int m = mt * TM + row;
     const int n0 = nt * a.BN;
     size_t rt_off = 0;
+    int rt_img = 0, rt_ho0 = 0;
     if (rt) {
-      const int img = rw.b, ho0 = rw.mt * a.rt_T;
-      const bool valid = ti < a.rt_T && ho0 + ti < a.Ho && two < a.Wo;
+      rt_img = rw.b;
+      rt_ho0 = rw.mt * rt_tb;
+      const bool valid = ti < a.rt_T && rt_ho0 + ti < a.Ho && two < a.Wo;
       m = valid ? 0 : a.M;
-      rt_off = (static_cast<size_t>(img * a.Ho + ho0 + ti) * a.Wo + two) * a.ldc;
+      rt_off = (static_cast<size_t>(rt_img * a.Ho + rt_ho0 + ti) * a.Wo + two) * a.ldc;
     }
-    // Chunks holding columns < N; the two warps of a lane quarter swap parities every tile, so an
-    // odd chunk count (N <= 32, N = 96, ...) is shared evenly over two tiles.
-    const int nvalid = (min(a.BN, a.N - n0) + 31) >> 5;
+    // Chunks holding columns < N (times the row groups); the warps of a lane quarter rotate through
+    // them every tile, so an odd chunk count (N <= 32, N = 96, ...) is shared evenly over tiles.
+    const int ncols = (min(a.BN, a.N - n0) + 31) >> 5;
+    const int nvalid = ncols * a.rt_G;
     const int nmine = nvalid > sel ? (nvalid - sel + kTcEpiPerQuarter - 1) / kTcEpiPerQuarter : 0;
     if (!mbar_wait_bounded(accf0 + 8 * buf, acc_ph, a.wait_limit, a.err, kDevErrTimeoutEpilogue)) break;
     tc_fence_after();
-    const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(buf * a.BN);
+    const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(buf * a.acc_cols);
     const size_t row_off =
         (!PAIR && a.mode == 2) ? rt_off : static_cast<size_t>(b) * a.batch_stride + static_cast<size_t>(m) * a.ldc;
     const int mrow0 = mt * TM + rank * kTcBM + q * 32;
@@ -483,8 +491,20 @@ __device__ __forceinline__ void epilogue_role_t(const TcArgs& a, const CUtensorM
     }
     for (int i = 0; i < nmine; ++i) {
       uint32_t va[32];
-      const int ca = sel + kTcEpiPerQuarter * i;
-      tmem_ld_32x32b_x32(tbase + ca * 32, va);
+      int ca = sel + kTcEpiPerQuarter * i;
+      int tcol = ca * 32;  // TMEM column of the chunk
+      int m_c = m;
+      size_t off_c = row_off;
+      if (a.rt_G > 1) {
+        // row group j = ca / ncols: TMEM columns j * BN.., output rows j * rt_T lower
+        const int j = ca / ncols;
+        ca -= j * ncols;
+        tcol = j * a.BN + ca * 32;
+        const int ho = rt_ho0 + j * a.rt_T + ti;
+        m_c = (ti < a.rt_T && ho < a.Ho && two < a.Wo) ? 0 : a.M;
+        off_c = (static_cast<size_t>(rt_img * a.Ho + ho) * a.Wo + two) * a.ldc;
+      }
+      tmem_ld_32x32b_x32(tbase + tcol, va);
       tmem_ld_wait();
       if constexpr (KIND == kOutS32) {
         if (rowmode) {
@@ -497,7 +517,7 @@ __device__ __forceinline__ void epilogue_role_t(const TcArgs& a, const CUtensorM
           }
         }
       }
-      emit_chunk<KIND, TMA, CL, RES>(a, tmC, va, b, m, mrow0, row_off, n0 + ca * 32, lane, sbufs, sb, bias, scale,
+      emit_chunk<KIND, TMA, CL, RES>(a, tmC, va, b, m_c, mrow0, off_c, n0 + ca * 32, lane, sbufs, sb, bias, scale,
                                  has_bias && !rowmode);
     }
     tc_fence_before();
@@ -613,7 +633,7 @@ __device__ __forceinline__ bool rowtile_mma_loop(const TcArgs& a, uint32_t tmem_
                                                    kDevErrTimeoutMma)))
       return false;
     tc_fence_after();
-    const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * a.BN);
+    const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * a.acc_cols);
     if (!__all_sync(0xFFFFFFFFu, mbar_wait_bounded(full0 + 8 * stage, ph, a.wait_limit, a.err, kDevErrTimeoutMma)))
       return false;
     const uint64_t ad_s = rt_desc0 + ((stage * stage_a) >> 4);
@@ -657,18 +677,22 @@ __device__ __forceinline__ bool rowtile_pair_loop(const TcArgs& a, uint32_t tmem
                                                    kDevErrTimeoutMma)))
       return false;
     tc_fence_after();
-    const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * a.BN);
+    const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * a.acc_cols);
     if (!__all_sync(0xFFFFFFFFu, mbar_wait_bounded(full0 + 8 * stage, ph, a.wait_limit, a.err, kDevErrTimeoutMma)))
       return false;
     const uint64_t ad_s = rt_desc0 + ((stage * stage_a) >> 4);
+    for (int gj = 0; gj < a.rt_G; ++gj) {  // row group gj: window rows gj * rt_T lower, TMEM columns gj * BN
+      const uint64_t ad_g = ad_s + static_cast<uint64_t>(gj * a.rt_T) * P;
+      const uint32_t d_g = d_tmem + static_cast<uint32_t>(gj * a.BN);
 #pragma unroll
-    for (int r = 0; r < R; ++r)
+      for (int r = 0; r < R; ++r)
 #pragma unroll
-      for (int sp = 0; sp < S / 2; ++sp) {
-        const int kb = r * (S / 2) + sp;
-        tc_mma_i8_elect(d_tmem, ad_s + static_cast<uint64_t>(r * P + 2 * sp), b_desc0 + static_cast<uint64_t>(kb * bstep),
-                        idesc, kb != 0 ? 1u : 0u);
-      }
+        for (int sp = 0; sp < S / 2; ++sp) {
+          const int kb = r * (S / 2) + sp;
+          tc_mma_i8_elect(d_g, ad_g + static_cast<uint64_t>(r * P + 2 * sp), b_desc0 + static_cast<uint64_t>(kb * bstep),
+                          idesc, kb != 0 ? 1u : 0u);
+        }
+    }
     tc_commit_elect(empty0 + 8 * stage);
     if (++stage == a.stages) {
       stage = 0;
@@ -697,7 +721,7 @@ __device__ __forceinline__ bool gemm_mma_loop(const TcArgs& a, uint32_t tmem_bas
                                                    kDevErrTimeoutMma)))
       return false;
     tc_fence_after();
-    const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * a.BN);
+    const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * a.acc_cols);
     uint32_t bres_off = 0;
     for (int kb = 0; kb < num_kb; ++kb) {
       // The TMA completion on the mbarrier orders the tiles for the tensor core; a tcgen05
@@ -823,11 +847,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
       // Row tiles: one window load per tile (all taps, all channels); tiles enumerate
       // (image, block of rt_T output rows).
+      const int rt_tb = a.rt_T * a.rt_G;  // output rows per tile
       TileWalk rw(a.mode == 2 ? static_cast<int>(blockIdx.x) : 0, gridDim.x, 1 << 30,
-                  a.mode == 2 ? (a.Ho + a.rt_T - 1) / a.rt_T : 1, 1);
+                  a.mode == 2 ? (a.Ho + rt_tb - 1) / rt_tb : 1, 1);
       for (int tile = blockIdx.x; tile < a.total_tiles && ok && a.mode == 2; tile += gridDim.x, rw.next()) {
         const int img = rw.b;
-        const int ho0 = rw.mt * a.rt_T;
+        const int ho0 = rw.mt * rt_tb;
         if (!mbar_wait_bounded(empty0 + 8 * stage, ph ^ 1u, a.wait_limit, a.err, kDevErrTimeoutProducer)) {
           ok = false;
           break;
@@ -1101,7 +1126,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
           break;
         }
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * a.BN);
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * a.acc_cols);
         for (int kb = 0; kb < a.num_kb; ++kb) {
           if (!__all_sync(0xFFFFFFFFu,
                           mbar_wait_bounded(full0 + 8 * stage, ph, a.wait_limit, a.err, kDevErrTimeoutMma))) {
