@@ -322,10 +322,11 @@ const int g_pair_min_k = [] {
   return v ? atoi(v) : 2048;
 }();
 
-// Row groups per space-to-depth row tile (env B200Q_RT_GROUPS, for A/B timing; 1 = one group).
+// Row groups per space-to-depth row tile, at most (env B200Q_RT_GROUPS, for A/B timing; 1 = one
+// group; the tensor-memory cap 256 / BN applies: 4 groups of 64 columns, 8 of 32).
 const int g_rt_groups = [] {
   const char* v = getenv("B200Q_RT_GROUPS");
-  const int n = v ? atoi(v) : 4;
+  const int n = v ? atoi(v) : 8;
   return n < 1 ? 1 : (n > 8 ? 8 : n);
 }();
 
@@ -1210,7 +1211,8 @@ static int conv2d_s8_impl(const int8_t* d_x, const int8_t* d_w, const int32_t* d
     const int yoff = -((g.pad_h + 1) / 2), xoff = -((g.pad_w + 1) / 2);
     const int r2 = route.s2d_r2, s2 = route.s2d_s2;
     const int P = g.wo + s2 - 1;
-    const int bn = pick_bn(k, 0);
+    // 32-column tiles for stems of at most 32 output channels (twice the row groups in tensor memory)
+    const int bn = (k <= 32 && g_rt_groups > 4) ? 32 : pick_bn(k, 0);
     {
       const int h2 = (h + 1) / 2, w2 = (w + 1) / 2;
       const size_t xs_bytes = (static_cast<size_t>(n) * h2 * w2 * 16 + 1023) / 1024 * 1024;
