@@ -1263,6 +1263,9 @@ static int conv2d_s8_impl(const int8_t* d_x, const int8_t* d_w, const int32_t* d
       if (a.rt_G > 256 / bn) a.rt_G = 256 / bn;
       const int row_blocks = (g.ho + a.rt_T - 1) / a.rt_T;
       if (a.rt_G > row_blocks) a.rt_G = row_blocks;
+      // keep at least one tile per SM
+      while (a.rt_G > 1 && static_cast<long long>(n) * ((g.ho + a.rt_T * a.rt_G - 1) / (a.rt_T * a.rt_G)) < st->sms)
+        --a.rt_G;
       if (a.rt_G < 1) a.rt_G = 1;
       // Window rows: the last tap slice of the last group's last accumulator row reads pixel
       // (rt_G - 1) * rt_T * P + (r2 - 1) * P + s2 - 1 + 127, which must stay inside the box.
@@ -1303,16 +1306,34 @@ static int conv2d_s8_impl(const int8_t* d_x, const int8_t* d_w, const int32_t* d
     a.rt_T = 128 / rt_P;
     a.rt_x0 = -1;
     a.rt_y0 = -1;
-    // T + 3 window rows: the right-border tap of the last output row reads index (T + 2) * P, the
-    // zero column of one more row (without it that read would reach the next channel plane).
-    a.rt_plane = (a.rt_T + 3) * rt_P * 16;
+    // Row groups: as many groups of rt_T rows as keep two accumulator buffers in tensor memory and
+    // the resident weights plus two window stages in shared memory.
+    {
+      const int max_g = g_rt_groups < 256 / a.BN ? g_rt_groups : 256 / a.BN;
+      const int row_blocks = (g.ho + a.rt_T - 1) / a.rt_T;
+      a.rt_G = 1;
+      for (int gg = max_g < row_blocks ? max_g : row_blocks; gg > 1; --gg) {
+        // keep at least one tile per SM (BASELINE config 1 is a single image: 28 tiles of 2 rows)
+        if (static_cast<long long>(n) * ((g.ho + a.rt_T * gg - 1) / (a.rt_T * gg)) < st->sms) continue;
+        const long long stage = ((a.rt_T * gg + 3) * static_cast<long long>(rt_P) * c + (2 * rt_P + 2 + 128) * 16 +
+                                 1023) / 1024 * 1024;
+        if (9ll * c * a.BN + 2 * stage + kSmemReserve + 8 * 1024 <= kSmemLimit) {
+          a.rt_G = gg;
+          break;
+        }
+      }
+    }
+    // rt_T * rt_G + 3 window rows: the right-border tap of the last output row reads index
+    // (rows - 1) * P, the zero column of one more row (without it that read would reach the next
+    // channel plane).
+    a.rt_plane = (a.rt_T * a.rt_G + 3) * rt_P * 16;
     a.rt_box = a.rt_plane * (c / 16);
     // tap offsets read up to 2P + 2 pixels past a tile's 128 rows: slack after the last plane
     a.rt_stage = (a.rt_box + (2 * rt_P + 2 + 128) * 16 + 1023) / 1024 * 1024;
     CUtensorMap ma, mb;
     rc = encode_tiled_3d(&mb, d_w, static_cast<uint64_t>(9 * c), static_cast<uint64_t>(k), 1, a.BK, a.BN, a.BK);
     if (rc) return rc;
-    rc = encode_rowtile(&ma, d_x, g.n, g.h, g.w, c, a.rt_P, a.rt_T + 3);
+    rc = encode_rowtile(&ma, d_x, g.n, g.h, g.w, c, a.rt_P, a.rt_T * a.rt_G + 3);
     if (rc) return rc;
     g_last_path = 9;
     return launch_tc(*st, ma, mb, a, cs);

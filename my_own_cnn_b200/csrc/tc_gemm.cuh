@@ -637,13 +637,17 @@ __device__ __forceinline__ bool rowtile_mma_loop(const TcArgs& a, uint32_t tmem_
     if (!__all_sync(0xFFFFFFFFu, mbar_wait_bounded(full0 + 8 * stage, ph, a.wait_limit, a.err, kDevErrTimeoutMma)))
       return false;
     const uint64_t ad_s = rt_desc0 + ((stage * stage_a) >> 4);
+    for (int gj = 0; gj < a.rt_G; ++gj) {  // row group gj: window rows gj * rt_T lower, TMEM columns gj * BN
+      const uint64_t ad_g = ad_s + static_cast<uint64_t>(gj * a.rt_T) * P;
+      const uint32_t d_g = d_tmem + static_cast<uint32_t>(gj * a.BN);
 #pragma unroll
-    for (int tap = 0; tap < 9; ++tap) {
-      const uint64_t at = ad_s + static_cast<uint64_t>((tap / 3) * P + (tap % 3));
+      for (int tap = 0; tap < 9; ++tap) {
+        const uint64_t at = ad_g + static_cast<uint64_t>((tap / 3) * P + (tap % 3));
 #pragma unroll
-      for (int j = 0; j < KS; ++j)
-        tc_mma_i8_elect(d_tmem, at + static_cast<uint64_t>(j * pl2),
-                        b_desc0 + static_cast<uint64_t>(tap * bstep + j * 2), idesc, (tap | j) != 0 ? 1u : 0u);
+        for (int j = 0; j < KS; ++j)
+          tc_mma_i8_elect(d_g, at + static_cast<uint64_t>(j * pl2),
+                          b_desc0 + static_cast<uint64_t>(tap * bstep + j * 2), idesc, (tap | j) != 0 ? 1u : 0u);
+      }
     }
     tc_commit_elect(empty0 + 8 * stage);
     if (++stage == a.stages) {
