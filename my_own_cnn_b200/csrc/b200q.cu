@@ -203,13 +203,13 @@ int encode_out_4b(CUtensorMap* map, void* base, uint64_t n, uint64_t m, uint64_t
 
 // int8 output [batch][M][N] as a 3-D map with 32 x 32 boxes and the 32-byte swizzle of the
 // epilogue's staging buffers.
-int encode_out_1b(CUtensorMap* map, void* base, uint64_t n, uint64_t m, uint64_t batch) {
+int encode_out_1b(CUtensorMap* map, void* base, uint64_t n, uint64_t m, uint64_t batch, bool wide = false) {
   cuuint64_t dims[3] = {n, m, batch};
   cuuint64_t strides[2] = {n, n * m};
-  cuuint32_t box[3] = {32, 32, 1};
+  cuuint32_t box[3] = {wide ? 128u : 32u, 32, 1};
   cuuint32_t es[3] = {1, 1, 1};
   CUresult r = g_encode_tiled(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, base, dims, strides, box, es,
-                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_32B,
+                              CU_TENSOR_MAP_INTERLEAVE_NONE, wide ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_32B,
                               CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(B200Q_ERR_CUDA, "cuTensorMapEncodeTiled (int8 output) failed (%d)", (int)r);
   return B200Q_OK;
@@ -275,6 +275,13 @@ int pick_bn(int n, int mn_major_b) {
 }
 
 // int8 TMA-store epilogue switch (env B200Q_S8_TMA_STORE=0 turns it off, for A/B timing).
+// Wide int8 TMA stores (TcArgs::wide_store): env B200Q_S8_WIDE = 0 off, 1 reductions < 128 only,
+// 2 every eligible GEMM.
+const int g_s8_wide = [] {
+  const char* v = getenv("B200Q_S8_WIDE");
+  return v ? atoi(v) : 1;
+}();
+
 const bool g_s8_tma_store = [] {
   const char* v = getenv("B200Q_S8_TMA_STORE");
   return !(v && v[0] == '0');
@@ -384,18 +391,28 @@ int launch_tc(const DeviceState& st, const CUtensorMap& ma, const CUtensorMap& m
               (!a.epi.res || reinterpret_cast<uintptr_t>(a.epi.res) % 8 == 0);
   // int8 outputs: TMA stores when the row pitch allows a map and every 32-column chunk can read
   // its bias / scale (staged columns are zero-padded to a multiple of 32).  GEMMs with a reduction
-  // shorter than 128 keep direct stores: there the epilogue alone sets the pace and the staging
-  // round trip measured slower.
-  if (a.mode != 2 && a.epi.out_kind == kOutS8 && g_s8_tma_store && a.num_kb * a.BK >= 128 && a.ldc == a.N &&
-      a.N % 16 == 0 &&
-      aligned16(a.out) &&
-      (a.stage_cols > 0 || a.N % 32 == 0) && a.vec_ok) {
+  // shorter than 128 are store-bound: they take the 128-byte-wide boxes (256-column tiles) or keep
+  // direct stores (32-byte boxes measured no faster there); longer reductions keep the 32-byte
+  // boxes, whose smaller staging leaves more ring stages.
+  const bool short_red = a.num_kb * a.BK < 128;
+  a.wide_store = 0;
+  if (a.mode != 2 && a.epi.out_kind == kOutS8 && g_s8_tma_store && !a.pair && kTcEpiPerQuarter == 2 &&
+      (g_s8_wide == 2 || (g_s8_wide == 1 && short_red)) && a.BN == 256 && a.N % 256 == 0 && a.ldc == a.N &&
+      aligned16(a.out) && a.stage_cols > 0 && a.vec_ok) {
+    const uint64_t rows = static_cast<uint64_t>(a.M);
+    int rc = encode_out_1b(&mc, a.out, static_cast<uint64_t>(a.N), rows, static_cast<uint64_t>(a.batch), true);
+    if (rc) return rc;
+    a.tma_store = 1;
+    a.wide_store = 1;
+  } else if (a.mode != 2 && a.epi.out_kind == kOutS8 && g_s8_tma_store && !short_red && a.ldc == a.N &&
+             a.N % 16 == 0 && aligned16(a.out) && (a.stage_cols > 0 || a.N % 32 == 0) && a.vec_ok) {
     const uint64_t rows = static_cast<uint64_t>(a.M);
     int rc = encode_out_1b(&mc, a.out, static_cast<uint64_t>(a.N), rows, static_cast<uint64_t>(a.batch));
     if (rc) return rc;
     a.tma_store = 1;
   }
-  const int stage_out = a.epi.out_kind == kOutS8 ? kEpiStageBytesS8 : kEpiStageBytes;
+  const int stage_out =
+      a.epi.out_kind == kOutS8 ? (a.wide_store ? kEpiStageBytesS8W : kEpiStageBytesS8) : kEpiStageBytes;
   const int epi_bytes = a.stage_cols * 8 + (a.tma_store ? 1024 + kTcEpiWarps * 2 * stage_out : 0);
   const int b_res_bytes = a.b_res ? static_cast<int>(b_all) : 0;
   int stages = (kSmemLimit - kSmemReserve - epi_bytes - b_res_bytes) / stage_bytes;

@@ -80,11 +80,16 @@ struct TcArgs {
   int tf32;         // fp32 operands, kind::tf32 MMAs, fp32 accumulators copied out bit for bit
   int kb_third;     // fp32 im2col convs: K blocks per third of the split reduction (0 otherwise)
   int grp_bytes;    // fp32 im2col convs: bytes between the channel starts of consecutive groups (batch items)
+  // int8 TMA stores of 32 rows x 128 columns: each epilogue warp takes 4 adjacent chunks of a
+  // 256-column tile and stores them with one 128-byte-wide box (SWIZZLE_128B map) instead of four
+  // 32-byte-wide ones (requires BN = 256, N % 256 == 0, two warps per lane quarter).
+  int wide_store;
 };
 
 constexpr int kTcMaxAcc = 8;
 constexpr int kEpiStageBytes = 32 * 128;   // one warp's 32 rows x 32 four-byte columns
 constexpr int kEpiStageBytesS8 = 32 * 32;  // one warp's 32 rows x 32 int8 columns
+constexpr int kEpiStageBytesS8W = 32 * 128;  // wide stores: 32 rows x 128 int8 columns
 
 __device__ __forceinline__ uint32_t kmajor_layout(int bk) {
   return bk == 128 ? 2u : (bk == 64 ? 4u : 6u);  // SWIZZLE_128B / 64B / 32B
@@ -352,10 +357,10 @@ __device__ __forceinline__ void stage_chunk_4b(const TcArgs& a, const uint32_t (
 // 32B-swizzled 1 KiB buffer (16-byte half h of row r at half h ^ ((r / 4) % 2), the layout of a
 // SWIZZLE_32B tensor map: conflict-free for one 16-byte store per lane) and leave with one TMA
 // store, which clips rows >= M and columns >= N.  The requantization is the one of store_chunk.
-template <int CL, bool RES>
+template <int CL, bool RES, bool WIDE>
 __device__ __forceinline__ void stage_chunk_s8(const TcArgs& a, const uint32_t (&v)[32], int n, int lane,
                                                uint8_t* sbuf, const int32_t* bias, const float* scale,
-                                               bool has_bias, const int8_t* rrow) {
+                                               bool has_bias, const int8_t* rrow, int slot) {
   const Epilogue& e = a.epi;
   const int4* bp = reinterpret_cast<const int4*>(bias + n);
   const float4* sp = reinterpret_cast<const float4*>(scale + n);
@@ -391,10 +396,21 @@ __device__ __forceinline__ void stage_chunk_s8(const TcArgs& a, const uint32_t (
     }
     packed[q] = quant4_s8<CL>(a, f0, f1, f2, f3);
   }
-  const int sw = (lane >> 2) & 1;
-  *reinterpret_cast<uint4*>(sbuf + lane * 32 + (sw << 4)) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
-  *reinterpret_cast<uint4*>(sbuf + lane * 32 + ((sw ^ 1) << 4)) =
-      make_uint4(packed[4], packed[5], packed[6], packed[7]);
+  if constexpr (WIDE) {
+    // 128-byte rows, SWIZZLE_128B: 16-byte unit j of row r at unit j ^ (r % 8); this chunk is
+    // units 2 * slot and 2 * slot + 1 of the row.
+    const int x = lane & 7;
+    *reinterpret_cast<uint4*>(sbuf + lane * 128 + (((2 * slot) ^ x) << 4)) =
+        make_uint4(packed[0], packed[1], packed[2], packed[3]);
+    *reinterpret_cast<uint4*>(sbuf + lane * 128 + (((2 * slot + 1) ^ x) << 4)) =
+        make_uint4(packed[4], packed[5], packed[6], packed[7]);
+  } else {
+    (void)slot;
+    const int sw = (lane >> 2) & 1;
+    *reinterpret_cast<uint4*>(sbuf + lane * 32 + (sw << 4)) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+    *reinterpret_cast<uint4*>(sbuf + lane * 32 + ((sw ^ 1) << 4)) =
+        make_uint4(packed[4], packed[5], packed[6], packed[7]);
+  }
 }
 
 // Epilogue role: 8 warps; warp w reads TMEM lanes 32*(w%4)..+31 (the hardware restricts a warp
@@ -402,19 +418,39 @@ __device__ __forceinline__ void stage_chunk_s8(const TcArgs& a, const uint32_t (
 // chunk % 2 == ((w-2)/4 + j) % 2.  Each chunk is loaded and processed in turn: overlapping the
 // next chunk's TMEM load with two register buffers measured slower (the extra register moves
 // cost more issue slots than the load latency it hid).
-template <int KIND, bool TMA, int CL, bool RES>
+template <int KIND, bool TMA, int CL, bool RES, bool WIDE>
 __device__ __forceinline__ void emit_chunk(const TcArgs& a, const CUtensorMap* tmC, const uint32_t (&v)[32], int b,
                                            int m, int mrow0, size_t row_off, int n, int lane, uint8_t* sbufs,
                                            int& sb, const int32_t* bias, const float* scale,
-                                           bool has_bias) {
+                                           bool has_bias, int slot) {
+  if constexpr (WIDE) {
+    // slot 0..3 of this warp's 128-column block (every chunk valid: N % 256 == 0)
+    uint8_t* buf = sbufs + sb * kEpiStageBytesS8W;
+    if (slot == 0) {
+      if (lane == 0) bulk_wait_group_read<1>();  // the store that used this buffer has read it
+      __syncwarp();
+    }
+    stage_chunk_s8<CL, RES, true>(a, v, n, lane, buf, bias, scale, has_bias,
+                                  RES && m < a.M ? a.epi.res + row_off + n : nullptr, slot);
+    if (slot == 3) {
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        tma_store_3d(tmC, smem_u32(buf), n - 96, mrow0, b);
+        bulk_commit_group();
+      }
+      sb ^= 1;
+    }
+    return;
+  }
   if (n >= a.N) return;
   if constexpr (TMA) {
     uint8_t* buf = sbufs + sb * (KIND == kOutS8 ? kEpiStageBytesS8 : kEpiStageBytes);
     if (lane == 0) bulk_wait_group_read<1>();  // the store that used this buffer has read it
     __syncwarp();
     if constexpr (KIND == kOutS8)
-      stage_chunk_s8<CL, RES>(a, v, n, lane, buf, bias, scale, has_bias,
-                               RES && m < a.M ? a.epi.res + row_off + n : nullptr);
+      stage_chunk_s8<CL, RES, false>(a, v, n, lane, buf, bias, scale, has_bias,
+                                      RES && m < a.M ? a.epi.res + row_off + n : nullptr, -1);
     else
       stage_chunk_4b<KIND>(a, v, n, lane, buf, bias, scale, has_bias);
     fence_proxy_async_smem();
@@ -431,7 +467,7 @@ __device__ __forceinline__ void emit_chunk(const TcArgs& a, const CUtensorMap* t
 
 // PAIR: the CTA is one half of a 2-SM pair (tiles of 2 x 128 rows; this CTA's TMEM holds rows
 // rank * 128 .. + 127 of each tile; the accumulator-empty barrier lives in the leader CTA).
-template <int KIND, bool TMA, int CL, bool PAIR, bool RES>
+template <int KIND, bool TMA, int CL, bool PAIR, bool RES, bool WIDE>
 __device__ __forceinline__ void epilogue_role_t(const TcArgs& a, const CUtensorMap* tmC, uint32_t tmem_base,
                                               uint32_t accf0, uint32_t acce0, int warp, int lane,
                                               const int32_t* bias, const float* scale, bool has_bias,
@@ -491,7 +527,7 @@ __device__ __forceinline__ void epilogue_role_t(const TcArgs& a, const CUtensorM
     }
     for (int i = 0; i < nmine; ++i) {
       uint32_t va[32];
-      int ca = sel + kTcEpiPerQuarter * i;
+      int ca = WIDE ? sel * 4 + i : sel + kTcEpiPerQuarter * i;
       int tcol = ca * 32;  // TMEM column of the chunk
       int m_c = m;
       size_t off_c = row_off;
@@ -517,8 +553,8 @@ __device__ __forceinline__ void epilogue_role_t(const TcArgs& a, const CUtensorM
           }
         }
       }
-      emit_chunk<KIND, TMA, CL, RES>(a, tmC, va, b, m_c, mrow0, off_c, n0 + ca * 32, lane, sbufs, sb, bias, scale,
-                                 has_bias && !rowmode);
+      emit_chunk<KIND, TMA, CL, RES, WIDE>(a, tmC, va, b, m_c, mrow0, off_c, n0 + ca * 32, lane, sbufs, sb, bias,
+                                           scale, has_bias && !rowmode, i);
     }
     tc_fence_before();
     __syncwarp();
@@ -543,18 +579,20 @@ __device__ __forceinline__ void epilogue_role(const TcArgs& a, const CUtensorMap
                                               uint8_t* sbufs) {
   // int8 outputs: one compiled variant per clamp form (quant4_s8's CL: the per-element branch
   // stays out of the unrolled loop) and per fused residual add.
-#define B200Q_EPI(TMA, CL, RES)                                                                                \
-  epilogue_role_t<KIND, TMA, CL, PAIR, RES>(a, tmC, tmem_base, accf0, acce0, warp, lane, bias, scale, has_bias, \
-                                            sbufs)
-#define B200Q_EPI_CL(TMA, RES)     \
-  if (cl == 4)                     \
-    B200Q_EPI(TMA, 4, RES);        \
-  else if (cl == 1)                \
-    B200Q_EPI(TMA, 1, RES);        \
-  else if (cl == 2)                \
-    B200Q_EPI(TMA, 2, RES);        \
-  else                             \
-    B200Q_EPI(TMA, 0, RES)
+#define B200Q_EPI_W(TMA, CL, RES, WIDE)                                                                    \
+  epilogue_role_t<KIND, TMA, CL, PAIR, RES, WIDE>(a, tmC, tmem_base, accf0, acce0, warp, lane, bias, scale, \
+                                                  has_bias, sbufs)
+#define B200Q_EPI(TMA, CL, RES) B200Q_EPI_W(TMA, CL, RES, false)
+#define B200Q_EPI_CLW(TMA, RES, WIDE)  \
+  if (cl == 4)                         \
+    B200Q_EPI_W(TMA, 4, RES, WIDE);    \
+  else if (cl == 1)                    \
+    B200Q_EPI_W(TMA, 1, RES, WIDE);    \
+  else if (cl == 2)                    \
+    B200Q_EPI_W(TMA, 2, RES, WIDE);    \
+  else                                 \
+    B200Q_EPI_W(TMA, 0, RES, WIDE)
+#define B200Q_EPI_CL(TMA, RES) B200Q_EPI_CLW(TMA, RES, false)
   if constexpr (KIND != kOutS8) {
     if (a.tma_store)
       B200Q_EPI(true, 0, false);
@@ -562,7 +600,13 @@ __device__ __forceinline__ void epilogue_role(const TcArgs& a, const CUtensorMap
       B200Q_EPI(false, 0, false);
   } else {
     const int cl = a.default_clamp ? 1 : (a.epi.zp == 0 && a.epi.lo == 0) ? (a.epi.hi >= 127 ? 4 : 2) : 0;
-    if (a.epi.res) {
+    if (!PAIR && kTcEpiPerQuarter == 2 && a.wide_store) {
+      if (a.epi.res) {
+        B200Q_EPI_CLW(true, true, !PAIR);
+      } else {
+        B200Q_EPI_CLW(true, false, !PAIR);
+      }
+    } else if (a.epi.res) {
       if (a.tma_store) {
         B200Q_EPI_CL(true, true);
       } else {
@@ -575,7 +619,9 @@ __device__ __forceinline__ void epilogue_role(const TcArgs& a, const CUtensorMap
     }
   }
 #undef B200Q_EPI_CL
+#undef B200Q_EPI_CLW
 #undef B200Q_EPI
+#undef B200Q_EPI_W
 }
 
 // Epilogue warps: stage bias / scale in shared memory when they fit, then drain the accumulators.
@@ -584,7 +630,9 @@ __device__ __forceinline__ void run_epilogue(const TcArgs& a, const CUtensorMap*
                                              uint32_t accf0, uint32_t acce0, int warp, int lane, int32_t* s_bias,
                                              float* s_scale, uint8_t* s_out) {
   const bool has_bias = a.epi.bias != nullptr;
-  uint8_t* sbufs = s_out + (warp - 2) * 2 * (a.epi.out_kind == kOutS8 ? kEpiStageBytesS8 : kEpiStageBytes);
+  uint8_t* sbufs = s_out + (warp - 2) * 2 *
+                              (a.epi.out_kind == kOutS8 ? (a.wide_store ? kEpiStageBytesS8W : kEpiStageBytesS8)
+                                                        : kEpiStageBytes);
   if (a.stage_cols > 0) {
     // Copy the per-column bias / scale into shared memory once per CTA (epilogue warps only).
     for (int i = threadIdx.x - 64; i < a.stage_cols; i += kTcEpiWarps * 32) {
