@@ -224,7 +224,8 @@ const char* b200q_last_error(void);
 int b200q_device_error(void);
 
 /* Which kernel family the last conv / bmm call on this thread dispatched to:
- * 1 tcgen05 im2col conv, 2 tcgen05 tiled GEMM, 3 CUDA-core generic, 4 CUDA-core depthwise,
+ * 1 tcgen05 im2col conv, 2 tcgen05 tiled GEMM (for both: GEMMs of at least 2^36 MACs first prepack
+ * their weights into per-stage images in the stream's workspace), 3 CUDA-core generic, 4 CUDA-core depthwise,
  * 5 CUDA-core quantized-int32 (drop-in), 6 CUDA-core int32 bmm, 7 tcgen05 GEMM over an im2col matrix
  * packed into the stream's workspace (low channel counts), 8 tcgen05 tiled GEMM on 2-SM pairs
  * (256-row tiles, one M = 256 MMA per K slice across a cluster of two CTAs), 9 tcgen05 row-tile
@@ -238,7 +239,8 @@ int b200q_last_path(void);
 /* 0 = automatic dispatch (default); 1 = force the CUDA-core kernels (cross-checks). */
 void b200q_set_path_policy(int policy);
 
-/* Number of tcgen05 kernel launches issued since load (for launch accounting). */
+/* Number of tcgen05 GEMM launches, and of the weight-prepack launches that feed them, issued since
+   load (for launch accounting). */
 long long b200q_tc_launch_count(void);
 
 /* ---- seeded synthetic data (counter-based splitmix64; the CPU oracle regenerates any slice) ---- */

@@ -355,6 +355,17 @@ const int g_nacc_max = [] {
 // for reductions of 2048 and more or 4-byte outputs (config 4b +16 %); equal or slower for int8
 // outputs of shorter reductions, where both CTAs' epilogues gate every accumulator buffer.  The
 // caller encodes the B map with BN / 2 rows per box when this holds.
+// Prepacked conv weights for long reductions (env B200Q_B_PREPACK=0: off; B200Q_PREPACK_MIN_KB:
+// the shortest reduction, in 128-byte K blocks, that takes it).
+const bool g_b_prepack = [] {
+  const char* v = getenv("B200Q_B_PREPACK");
+  return !(v && v[0] == '0');
+}();
+const int g_prepack_min_kb = [] {
+  const char* v = getenv("B200Q_PREPACK_MIN_KB");
+  return v ? atoi(v) : 8;
+}();
+
 bool want_pair(int sms, const TcArgs& a) {
   if (!g_pair || a.mode != 0 || a.a_major != 0 || a.b_major != 0 || a.conv_b || a.BN != 256) return false;
   if (a.num_kb * a.BK < g_pair_min_k && a.epi.out_kind == kOutS8) return false;
@@ -1401,6 +1412,30 @@ static int conv2d_s8_impl(const int8_t* d_x, const int8_t* d_w, const int32_t* d
       rc = encode_im2col(&ma, d_x, g, a.BK);
       if (rc) return rc;
       g_last_path = 1;
+    }
+    // Long reductions consume operands faster than the TMA splits a B box into 128-byte row
+    // requests: the weights go through one prepack pass into per-stage shared-memory images, then
+    // one bulk copy per stage (one-CTA tiles, 128-byte K blocks, weights not resident).  The pass
+    // costs a few microseconds, so only GEMMs of at least 2^36 MACs take it (config 4 layer 1:
+    // 0.161-0.164 -> 0.155 ms; ResNet-50's 13-30 GMAC layers measured 1.5 % slower with it).
+    const int n_tiles = (k + a.BN - 1) / a.BN;
+    const bool b_res_like = n_tiles == 1 && static_cast<long long>(a.num_kb) * a.BN * a.BK <= 64 * 1024;
+    const double macs = static_cast<double>(M) * k * a.num_kb * a.BK;
+    if (g_b_prepack && !a.pair && a.BK == 128 && a.num_kb >= g_prepack_min_kb && !b_res_like && aligned16(d_w) &&
+        macs >= 0x1p36) {
+      const long long units = static_cast<long long>(n_tiles) * a.num_kb * a.BN * 8;
+      void* ws = nullptr;
+      rc = get_workspace(static_cast<size_t>(units) * 16, cs, &ws);
+      if (rc) return rc;
+      const int threads = 256;
+      long long blocks = (units + threads - 1) / threads;
+      if (blocks > 8 * st->sms) blocks = 8 * st->sms;
+      pack_b_stages_kernel<<<static_cast<int>(blocks), threads, 0, cs>>>(d_w, static_cast<int8_t*>(ws), k, r * s, c,
+                                                                         a.cchunks, a.num_kb, a.BN, units);
+      g_tc_launches.fetch_add(1, std::memory_order_relaxed);
+      rc = check_launch("pack_b_stages_kernel launch");
+      if (rc) return rc;
+      a.b_packed = static_cast<const int8_t*>(ws);
     }
     return launch_tc(*st, ma, mb, a, cs);
   }

@@ -122,6 +122,14 @@ __device__ __forceinline__ void mbar_arrive_expect_tx_cluster_relaxed(uint32_t c
 }
 // Tiled TMA load into this CTA's shared memory whose completion is counted on a barrier of the
 // pair's leader CTA (cbar: cluster address).  No multicast.
+// Untiled bulk copy global -> this CTA's shared memory, completing on an mbarrier of this CTA
+// (addresses 16-byte aligned, size a multiple of 16).
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(bar)
+      : "memory");
+}
 __device__ __forceinline__ void tma_load_3d_pair(uint32_t dst, const CUtensorMap* map, uint32_t cbar, int c0, int c1,
                                                  int c2) {
   asm volatile(

@@ -84,6 +84,10 @@ struct TcArgs {
   // 256-column tile and stores them with one 128-byte-wide box (SWIZZLE_128B map) instead of four
   // 32-byte-wide ones (requires BN = 256, N % 256 == 0, two warps per lane quarter).
   int wide_store;
+  // Prepacked B (conv weights, 128-byte K blocks): stage image of (N tile nt, K block kb) at
+  // b_packed + (nt * num_kb + kb) * BN * 128, exactly the shared-memory bytes the tensor-map load
+  // would write (SWIZZLE_128B rows).  One bulk copy per stage instead of BN row requests.
+  const int8_t* b_packed;
 };
 
 constexpr int kTcMaxAcc = 8;
@@ -962,7 +966,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           } else {
             tma_load_3d(dA, &tmA, fb, m0, kb * a.BK, b);
           }
-          if (!a.b_res) load_b(dB, fb, kb, n0, a.b_batched ? b : 0);
+          if (a.b_packed)
+            bulk_load(dB, a.b_packed + (static_cast<size_t>(nt) * a.num_kb + kb) * stage_b, stage_b, fb);
+          else if (!a.b_res)
+            load_b(dB, fb, kb, n0, a.b_batched ? b : 0);
           issued_mask |= 1u << stage;
           last_ph = (last_ph & ~(1u << stage)) | (ph << stage);
           if (++stage == a.stages) {
@@ -1230,6 +1237,32 @@ __global__ void wait_timeout_probe_kernel(long long limit, int* err) {
     mbar_init(smem_u32(&bar), 1);
     fence_mbar_init();
     mbar_wait_bounded(smem_u32(&bar), 0, limit, err, kDevErrTimeoutProbe);
+  }
+}
+
+// Prepack conv weights w[N][taps][C] (int8, C % 16 == 0, 16-byte aligned) into the shared-memory
+// images of the B operand (BN rows x 128-byte K blocks, SWIZZLE_128B: 16-byte unit u of row r at
+// unit u ^ (r % 8)), one image per (N tile, K block), K block kb = tap * cchunks + cc covering
+// channels [cc * 128, cc * 128 + 128) of tap `tap`; rows past N and channels past C are zero, as
+// the tensor map's out-of-bounds fill gives.  One thread writes one 16-byte unit.
+__global__ void pack_b_stages_kernel(const int8_t* __restrict__ w, int8_t* __restrict__ out, int N, int taps, int C,
+                                     int cchunks, int num_kb, int BN, long long units) {
+  for (long long u = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; u < units;
+       u += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int pos = static_cast<int>(u & 7);
+    const long long rowi = u >> 3;  // (nt * num_kb + kb) * BN + row
+    const int row = static_cast<int>(rowi % BN);
+    const long long blk = rowi / BN;
+    const int kb = static_cast<int>(blk % num_kb);
+    const int nt = static_cast<int>(blk / num_kb);
+    const int unit = pos ^ (row & 7);
+    const int tap = kb / cchunks;
+    const int ch = (kb - tap * cchunks) * 128 + unit * 16;
+    const int n = nt * BN + row;
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    if (n < N && ch < C)
+      v = __ldg(reinterpret_cast<const uint4*>(w + (static_cast<size_t>(n) * taps + tap) * C + ch));
+    reinterpret_cast<uint4*>(out)[u] = v;
   }
 }
 

@@ -516,3 +516,31 @@ def test_cpp_qconv_bench_driver(cuda_lib, args):
     assert "gflops=" in proc.stdout
     if "qfprop" in args or "all" in args:
         assert "path 11" in proc.stdout, proc.stdout  # the drop-in ran on the tcgen05 route
+
+
+@pytest.mark.parametrize("shape", [
+    # n, h, w, c, r, k, pad: GEMMs of >= 2^36 MACs with 128-byte K blocks (prepacked weights)
+    (300, 14, 14, 1088, 1, 1024, 0),  # 1x1 tiled, C = 8.5 x 128 (last K block half zero)
+    (16, 56, 56, 320, 3, 512, 1),     # 3x3 im2col, C = 2.5 x 128 per tap
+])
+def test_prepacked_weights_long_reduction(cuda_lib, shape):
+    """Long-reduction convs whose weights go through the per-stage prepack (one bulk copy per
+    stage): int32 accumulators and int8 outputs of sampled images against the oracle."""
+    b2q = _b2q()
+    n, h, w, c, r, k, pad = shape
+    g = torch.Generator(device="cuda").manual_seed(sum(shape))
+    x = torch.randint(-128, 128, (n, h, w, c), dtype=torch.int8, device="cuda", generator=g)
+    wt = torch.randint(-128, 128, (k, r, r, c), dtype=torch.int8, device="cuda", generator=g)
+    bias = torch.randint(-2**15, 2**15, (k,), dtype=torch.int32, device="cuda", generator=g)
+    scale = torch.rand(k, device="cuda", generator=g) * 1e-5 + 1e-6
+    p = b2q.Conv2DParams(pad, pad, 1, 1, 1, 1, 1)
+    y32 = b2q.conv2d_s8(x, wt, None, None, p, b2q.Epilogue.int32())
+    y8 = b2q.conv2d_s8(x, wt, bias, scale, p, b2q.Epilogue.int8(relu=True))
+    torch.cuda.synchronize()
+    assert b2q.last_path() == ("tcgen05-tiled" if r == 1 else "tcgen05-im2col")
+    wh, bh, sh = wt.cpu().numpy(), bias.cpu().numpy(), scale.cpu().numpy()
+    for img in (0, n // 2, n - 1):
+        xh = x[img:img + 1].cpu().numpy()
+        acc = oracle.conv_s8(oracle.conv_args(1, h, w, c, r, r, k, pad, pad), xh, wh, threads=8)
+        np.testing.assert_array_equal(y32[img:img + 1].cpu().numpy(), acc)
+        np.testing.assert_array_equal(y8[img:img + 1].cpu().numpy(), oracle.requant_s8(acc, bh, sh, 0, 0, 127))
