@@ -366,9 +366,16 @@ const int g_prepack_min_kb = [] {
   return v ? atoi(v) : 8;
 }();
 
+// 2-SM tiles for batched GEMMs (bmm), either B layout (env B200Q_PAIR_BMM=0: off).
+const bool g_pair_bmm = [] {
+  const char* v = getenv("B200Q_PAIR_BMM");
+  return !(v && v[0] == '0');
+}();
+
 bool want_pair(int sms, const TcArgs& a) {
-  if (!g_pair || a.mode != 0 || a.a_major != 0 || a.b_major != 0 || a.conv_b || a.BN != 256) return false;
-  if (a.num_kb * a.BK < g_pair_min_k && a.epi.out_kind == kOutS8) return false;
+  if (!g_pair || a.mode != 0 || a.a_major != 0 || a.conv_b || a.BN != 256) return false;
+  if (a.b_major != 0 && !(g_pair_bmm && a.b_batched && a.BK == 128)) return false;
+  if (a.b_batched ? !g_pair_bmm : (a.num_kb * a.BK < g_pair_min_k && a.epi.out_kind == kOutS8)) return false;
   const long long n_tiles = (a.N + a.BN - 1) / a.BN;
   const long long pair_tiles = static_cast<long long>(a.batch) * ((a.M + 2 * kTcBM - 1) / (2 * kTcBM)) * n_tiles;
   return n_tiles >= 2 && pair_tiles >= sms;

@@ -1157,7 +1157,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
           else
             mbar_arrive_expect_tx_cluster_relaxed(fb, tx);
           tma_load_3d_pair(smem_u32(sA + stage * stage_a), &tmA, fb, kb * a.BK, m0, b);
-          tma_load_3d_pair(smem_u32(sB + stage * stage_b), &tmB, fb, kb * a.BK, nb0, bb);
+          if (a.b_major == 0)
+            tma_load_3d_pair(smem_u32(sB + stage * stage_b), &tmB, fb, kb * a.BK, nb0, bb);
+          else  // MN-major B (bmm NN): one 128-column box of BK K rows
+            tma_load_3d_pair(smem_u32(sB + stage * stage_b), &tmB, fb, nb0, kb * a.BK, bb);
           if (++stage == a.stages) {
             stage = 0;
             ph ^= 1u;
@@ -1176,7 +1179,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
       bool ok = true;
       const uint32_t layout = kmajor_layout(a.BK);
       const uint64_t a_desc0 = make_smem_desc(smem_u32(sA), 16u, 8u * a.BK, layout);
-      const uint64_t b_desc0 = make_smem_desc(smem_u32(sB), 16u, 8u * a.BK, layout);
+      // MN-major B: this CTA's 128 columns are one 128-byte swizzle atom wide, K rows 128 bytes
+      // apart (8-row groups 1024 bytes apart); a K = 32 slice is 32 rows = 4096 bytes on.
+      const bool bmn = a.b_major != 0;
+      const uint64_t b_desc0 = bmn ? make_smem_desc(smem_u32(sB), static_cast<uint32_t>(a.BK) * 128u, 1024u, 2u)
+                                   : make_smem_desc(smem_u32(sB), 16u, 8u * a.BK, layout);
       const int ksteps = a.BK / 32;
       for (int tile = unit; tile < a.total_tiles && ok; tile += nunits) {
         if (!__all_sync(0xFFFFFFFFu,
@@ -1194,7 +1201,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
           }
           const uint64_t ad_s = a_desc0 + ((stage * stage_a) >> 4);
           const uint64_t bd_s = b_desc0 + ((stage * stage_b) >> 4);
-          if (ksteps == 4) {
+          if (bmn) {
+            for (int j = 0; j < ksteps; ++j)
+              tc_mma_i8_pair_elect(d_tmem, ad_s + 2 * j, bd_s + 256 * j, a.idesc, (kb | j) != 0 ? 1u : 0u);
+          } else if (ksteps == 4) {
             tc_mma_i8_pair_kblock4(d_tmem, ad_s, bd_s, a.idesc, kb != 0 ? 1u : 0u);
           } else {
             for (int j = 0; j < ksteps; ++j)

@@ -350,7 +350,7 @@ def test_config2_bmm_full_size_sampled(cuda_lib):
     A = synth.fill_s8_uniform(torch.empty((batch, M, K), dtype=torch.int8, device="cuda"), 42, 101)
     B = synth.fill_s8_uniform(torch.empty((batch, K, N), dtype=torch.int8, device="cuda"), 42, 102)
     C = b2q.bmm_s8(A, B, 0, 0, b2q.Epilogue.int32())
-    assert b2q.last_path() == "tcgen05-tiled"
+    assert b2q.last_path() == "tcgen05-tiled-2sm"
     b2q.set_path_policy(1)
     try:
         C2 = b2q.bmm_s8(A, B, 0, 0, b2q.Epilogue.int32())
@@ -544,3 +544,26 @@ def test_prepacked_weights_long_reduction(cuda_lib, shape):
         acc = oracle.conv_s8(oracle.conv_args(1, h, w, c, r, r, k, pad, pad), xh, wh, threads=8)
         np.testing.assert_array_equal(y32[img:img + 1].cpu().numpy(), acc)
         np.testing.assert_array_equal(y8[img:img + 1].cpu().numpy(), oracle.requant_s8(acc, bh, sh, 0, 0, 127))
+
+
+@pytest.mark.parametrize("tb", [0, 1])
+def test_bmm_s8_2sm_tiles_both_b_layouts(cuda_lib, tb):
+    """bmm on 2-SM tiles with B stored [K][N] (MN-major operand) or [N][K] (K-major): every
+    int32 output against an exact product, int8 outputs against the oracle's requantization."""
+    b2q = _b2q()
+    batch, M, N, K = 40, 512, 768, 384
+    g = torch.Generator(device="cuda").manual_seed(77 + tb)
+    A = torch.randint(-128, 128, (batch, M, K), dtype=torch.int8, device="cuda", generator=g)
+    B = torch.randint(-128, 128, (batch, N, K) if tb else (batch, K, N), dtype=torch.int8, device="cuda", generator=g)
+    bias = torch.randint(-2**15, 2**15, (N,), dtype=torch.int32, device="cuda", generator=g)
+    scale = torch.rand(N, device="cuda", generator=g) * 1e-4 + 1e-6
+    C32 = b2q.bmm_s8(A, B, 0, tb, b2q.Epilogue.int32())
+    assert b2q.last_path() == "tcgen05-tiled-2sm"
+    C8 = b2q.bmm_s8(A, B, 0, tb, b2q.Epilogue.int8(), bias=bias, col_scale=scale)
+    assert b2q.last_path() == "tcgen05-tiled-2sm"
+    torch.cuda.synchronize()
+    Ah = A.cpu().numpy().astype(np.float64)
+    Bh = B.cpu().numpy().astype(np.float64)
+    want = np.matmul(Ah, np.swapaxes(Bh, 1, 2) if tb else Bh).astype(np.int64).astype(np.int32)
+    np.testing.assert_array_equal(C32.cpu().numpy(), want)
+    np.testing.assert_array_equal(C8.cpu().numpy(), oracle.requant_s8(want, bias.cpu().numpy(), scale.cpu().numpy()))
