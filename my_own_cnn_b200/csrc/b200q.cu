@@ -275,11 +275,16 @@ int pick_bn(int n, int mn_major_b) {
 }
 
 // int8 TMA-store epilogue switch (env B200Q_S8_TMA_STORE=0 turns it off, for A/B timing).
-// Wide int8 TMA stores (TcArgs::wide_store): env B200Q_S8_WIDE = 0 off, 1 reductions < 128 only,
-// 2 every eligible GEMM.
+// Wide int8 TMA stores (TcArgs::wide_store): env B200Q_S8_WIDE = 0 off, 1 reductions of at most
+// B200Q_S8_WIDE_MAX_RED bytes (default 256), 2 every eligible GEMM.
 const int g_s8_wide = [] {
   const char* v = getenv("B200Q_S8_WIDE");
   return v ? atoi(v) : 1;
+}();
+
+const int g_s8_wide_max_red = [] {
+  const char* v = getenv("B200Q_S8_WIDE_MAX_RED");
+  return v ? atoi(v) : 256;
 }();
 
 const bool g_s8_tma_store = [] {
@@ -415,7 +420,8 @@ int launch_tc(const DeviceState& st, const CUtensorMap& ma, const CUtensorMap& m
   const bool short_red = a.num_kb * a.BK < 128;
   a.wide_store = 0;
   if (a.mode != 2 && a.epi.out_kind == kOutS8 && g_s8_tma_store && !a.pair && kTcEpiPerQuarter == 2 &&
-      (g_s8_wide == 2 || (g_s8_wide == 1 && short_red)) && a.BN == 256 && a.N % 256 == 0 && a.ldc == a.N &&
+      (g_s8_wide == 2 || (g_s8_wide == 1 && a.num_kb * a.BK <= g_s8_wide_max_red)) && a.BN == 256 &&
+      a.N % 16 == 0 && a.ldc == a.N &&
       aligned16(a.out) && a.stage_cols > 0 && a.vec_ok) {
     const uint64_t rows = static_cast<uint64_t>(a.M);
     int rc = encode_out_1b(&mc, a.out, static_cast<uint64_t>(a.N), rows, static_cast<uint64_t>(a.batch), true);

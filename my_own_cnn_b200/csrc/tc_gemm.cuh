@@ -426,9 +426,10 @@ template <int KIND, bool TMA, int CL, bool RES, bool WIDE>
 __device__ __forceinline__ void emit_chunk(const TcArgs& a, const CUtensorMap* tmC, const uint32_t (&v)[32], int b,
                                            int m, int mrow0, size_t row_off, int n, int lane, uint8_t* sbufs,
                                            int& sb, const int32_t* bias, const float* scale,
-                                           bool has_bias, int slot) {
+                                           bool has_bias, int slot, bool last) {
   if constexpr (WIDE) {
-    // slot 0..3 of this warp's 128-column block (every chunk valid: N % 256 == 0)
+    // slot 0..3 of this warp's 128-column block; the box leaves after the warp's last valid chunk
+    // (the TMA store clips columns >= N, so unwritten slots past N never reach memory)
     uint8_t* buf = sbufs + sb * kEpiStageBytesS8W;
     if (slot == 0) {
       if (lane == 0) bulk_wait_group_read<1>();  // the store that used this buffer has read it
@@ -436,11 +437,11 @@ __device__ __forceinline__ void emit_chunk(const TcArgs& a, const CUtensorMap* t
     }
     stage_chunk_s8<CL, RES, true>(a, v, n, lane, buf, bias, scale, has_bias,
                                   RES && m < a.M ? a.epi.res + row_off + n : nullptr, slot);
-    if (slot == 3) {
+    if (last) {
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) {
-        tma_store_3d(tmC, smem_u32(buf), n - 96, mrow0, b);
+        tma_store_3d(tmC, smem_u32(buf), n - 32 * slot, mrow0, b);
         bulk_commit_group();
       }
       sb ^= 1;
@@ -515,7 +516,8 @@ __device__ __forceinline__ void epilogue_role_t(const TcArgs& a, const CUtensorM
     // them every tile, so an odd chunk count (N <= 32, N = 96, ...) is shared evenly over tiles.
     const int ncols = (min(a.BN, a.N - n0) + 31) >> 5;
     const int nvalid = ncols * a.rt_G;
-    const int nmine = nvalid > sel ? (nvalid - sel + kTcEpiPerQuarter - 1) / kTcEpiPerQuarter : 0;
+    const int nmine = WIDE ? max(0, min(4, nvalid - 4 * sel))
+                           : (nvalid > sel ? (nvalid - sel + kTcEpiPerQuarter - 1) / kTcEpiPerQuarter : 0);
     if (!mbar_wait_bounded(accf0 + 8 * buf, acc_ph, a.wait_limit, a.err, kDevErrTimeoutEpilogue)) break;
     tc_fence_after();
     const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(buf * a.acc_cols);
@@ -558,7 +560,7 @@ __device__ __forceinline__ void epilogue_role_t(const TcArgs& a, const CUtensorM
         }
       }
       emit_chunk<KIND, TMA, CL, RES, WIDE>(a, tmC, va, b, m_c, mrow0, off_c, n0 + ca * 32, lane, sbufs, sb, bias,
-                                           scale, has_bias && !rowmode, i);
+                                           scale, has_bias && !rowmode, i, i + 1 == nmine);
     }
     tc_fence_before();
     __syncwarp();

@@ -69,7 +69,8 @@ def _case(n, h, w, c, r, k, pad, stride, bias_hi, special=None, res_scale=None, 
     return b2q.last_path()
 
 
-@pytest.mark.parametrize("c,k", [(64, 256), (64, 64), (128, 96), (32, 48), (16, 256)])
+@pytest.mark.parametrize("c,k", [(64, 256), (64, 64), (128, 96), (32, 48), (16, 256), (64, 192), (128, 144),
+                                 (256, 400)])
 def test_pointwise_short_reduction(cuda_lib, c, k):
     assert _case(4, 28, 28, c, 1, k, 0, 1, 2**15, seed=c + k) == "tcgen05-tiled"
 
