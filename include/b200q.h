@@ -233,7 +233,9 @@ int b200q_device_error(void);
  * space-to-depth copy of a stride-2 low-channel input (network stems; the input and weights are
  * rearranged into the stream's workspace), 11 tcgen05 quantized-int32 drop-in (raw 8-bit codes and
  * zero-point correction terms), 12 CUDA-core depthwise with TMA-staged tiles, 13 tcgen05 fp32
- * (3 x TF32 split GEMM), 14 CUDA-core fp32 (groups of a few channels, e.g. depthwise). */
+ * (3 x TF32 split GEMM), 14 CUDA-core fp32 (groups of a few channels, e.g. depthwise), 15 tcgen05
+ * pixel-grouped 1x1 GEMM (G pixels per row against block-diagonal weights built in the stream's
+ * workspace, for layers with G * K <= 256 and G * C <= 256). */
 int b200q_last_path(void);
 
 /* 0 = automatic dispatch (default); 1 = force the CUDA-core kernels (cross-checks). */

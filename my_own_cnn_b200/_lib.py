@@ -37,6 +37,7 @@ PATH_NAMES = {
     12: "cuda-core-depthwise-tma",
     13: "tcgen05-f32",
     14: "cuda-core-f32",
+    15: "tcgen05-tiled-grouped",
 }
 
 

@@ -1124,7 +1124,20 @@ struct ConvRoute {
   int path;            // 10 s2d row tiles, 9 row tiles, 2 tiled, 1 im2col, 8 tiled 2-SM, 7 packed, 4 depthwise, 3 generic
   int s2d_r2, s2d_s2;  // path 10: taps of the stride-1 filter over the 2x2-block copy
   int tc_bk;           // paths 1 / 2 / 8: K block bytes per ring stage
+  int group;           // path 15: pixels per GEMM row
 };
+
+// Pixel grouping of a 1x1 conv (path 15): the largest G in {16, 8, 4, 2} with G * K <= 256,
+// G * C <= 256, G * C a multiple of 16 (TMA rows) and M % G == 0; 1 when none fits.
+static const bool g_group1x1 = [] {
+  const char* v = getenv("B200Q_GROUP1X1");
+  return !(v && v[0] == '0');
+}();
+static int pick_group(int c, int k, long long M) {
+  for (int G : {16, 8, 4, 2})
+    if (G * k <= 256 && G * c <= 256 && (G * c) % 16 == 0 && M % G == 0) return G;
+  return 1;
+}
 
 static int tc_pick_bk(int c) {
   // The K block (128 / 64 / 32 bytes of channels per ring stage) with the fewest blocks per tap,
@@ -1142,7 +1155,7 @@ static ConvRoute route_conv_s8(const ConvGeom& g, int h, int w, int c, int r, in
   const bool out_aligned = y_aligned && epi_aligned;
   (void)h;
   (void)w;
-  ConvRoute rt{3, 0, 0, 0};
+  ConvRoute rt{3, 0, 0, 0, 0};
   const bool auto_policy = g_policy.load() == 0;
   const long long M = static_cast<long long>(g.n) * g.ho * g.wo;
   const size_t x_bytes = static_cast<size_t>(g.n) * g.h * g.w * c;
@@ -1176,6 +1189,17 @@ static ConvRoute route_conv_s8(const ConvGeom& g, int h, int w, int c, int r, in
         g.pad_h == 1 && g.pad_w == 1 && g.dil_h == 1 && g.dil_w == 1 && (c == 32 || c == 64 || c == 128) &&
         k <= 256 && rt_P <= 128 && rt_fits && vec_ptrs && M < (1ll << 31)) {
       rt.path = 9;
+      return rt;
+    }
+  }
+  // Pixel-grouped 1x1 GEMM for narrow layers (G * K <= 256 and G * C <= 256: one N tile, resident
+  // block-diagonal weights): G times the outputs per tile, and TMA rows of G * C bytes.
+  if (g_group1x1 && auto_policy && g.groups == 1 && is_1x1_plain && vec_ptrs && M < (1ll << 31)) {
+    const int G = pick_group(c, k, M);
+    if (G > 1) {
+      rt.path = 15;
+      rt.group = G;
+      rt.tc_bk = tc_pick_bk(G * c);
       return rt;
     }
   }
@@ -1378,6 +1402,46 @@ static int conv2d_s8_impl(const int8_t* d_x, const int8_t* d_w, const int32_t* d
     rc = encode_rowtile(&ma, d_x, g.n, g.h, g.w, c, a.rt_P, a.rt_T * a.rt_G + 3);
     if (rc) return rc;
     g_last_path = 9;
+    return launch_tc(*st, ma, mb, a, cs);
+  }
+  if (route.path == 15) {
+    // G pixels per GEMM row: A = x as [M / G][G * C], B = block-diagonal weights in the stream's
+    // workspace, output rows [G * K] = G NHWC pixels (residual likewise).
+    const int G = route.group;
+    const int kg = G * k, cg = G * c;
+    const size_t wb = round256(static_cast<size_t>(kg) * cg), bb = round256(static_cast<size_t>(kg) * 4);
+    void* ws = nullptr;
+    rc = get_workspace(wb + 2 * bb, cs, &ws);
+    if (rc) return rc;
+    int8_t* wg = static_cast<int8_t*>(ws);
+    int32_t* bg = reinterpret_cast<int32_t*>(static_cast<char*>(ws) + wb);
+    float* sg = reinterpret_cast<float*>(static_cast<char*>(ws) + wb + bb);
+    group_weights_kernel<<<grid_for(static_cast<size_t>(kg) * cg, 256, st->sms), 256, 0, cs>>>(
+        d_w, wg, bg, sg, e.bias, e.scale, k, c, G);
+    g_tc_launches.fetch_add(1, std::memory_order_relaxed);
+    rc = check_launch("group_weights_kernel launch");
+    if (rc) return rc;
+    TcArgs a{};
+    a.mode = 0;
+    a.BK = route.tc_bk;
+    a.cchunks = (cg + a.BK - 1) / a.BK;
+    a.num_kb = a.cchunks;
+    a.BN = pick_bn(kg, 0);
+    a.M = static_cast<int>(M / G);
+    a.N = kg;
+    a.batch = 1;
+    a.epi = e;
+    if (e.bias) a.epi.bias = bg;
+    if (e.scale) a.epi.scale = sg;
+    a.out = d_y;
+    a.ldc = kg;
+    a.vec_ok = kg % 16 == 0;
+    CUtensorMap ma, mb;
+    rc = encode_tiled_3d(&ma, d_x, static_cast<uint64_t>(cg), static_cast<uint64_t>(a.M), 1, a.BK, kTcBM, a.BK);
+    if (rc) return rc;
+    rc = encode_tiled_3d(&mb, wg, static_cast<uint64_t>(cg), static_cast<uint64_t>(kg), 1, a.BK, a.BN, a.BK);
+    if (rc) return rc;
+    g_last_path = 15;
     return launch_tc(*st, ma, mb, a, cs);
   }
   if (route.path == 1 || route.path == 2 || route.path == 8) {

@@ -1278,4 +1278,26 @@ __global__ void pack_b_stages_kernel(const int8_t* __restrict__ w, int8_t* __res
   }
 }
 
+// Pixel-grouped 1x1 conv: G consecutive pixels are one GEMM row of G * C channels, and the
+// weights become the block-diagonal [G * K][G * C] matrix (block g maps pixel g's channels to its
+// K outputs), so the output rows [G * K] are the same bytes as G NHWC output pixels.  Also expands
+// bias / scale to G * K columns (entry j = entry j % K; null stays null).
+__global__ void group_weights_kernel(const int8_t* __restrict__ w, int8_t* __restrict__ wg, int32_t* __restrict__ bg,
+                                     float* __restrict__ sg, const int32_t* __restrict__ bias,
+                                     const float* __restrict__ scale, int K, int C, int G) {
+  const long long total = static_cast<long long>(G) * K * G * C;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long row = i / (static_cast<long long>(G) * C);
+    const int col = static_cast<int>(i - row * G * C);
+    const int gr = static_cast<int>(row / K), k = static_cast<int>(row - static_cast<long long>(gr) * K);
+    const int gc = col / C, c = col - gc * C;
+    wg[i] = gr == gc ? w[static_cast<size_t>(k) * C + c] : static_cast<int8_t>(0);
+    if (col == 0) {
+      if (bias) bg[row] = bias[k];
+      if (scale) sg[row] = scale[k];
+    }
+  }
+}
+
 }  // namespace b200q

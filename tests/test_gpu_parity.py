@@ -161,7 +161,9 @@ def test_conv_s8_tcgen05_pointwise(cuda_lib, shape):
     n, h, w, c, k = shape
     p = b2q.Conv2DParams(0, 0, 1, 1, 1, 1, 1)
     paths = _conv_case(n, h, w, c, 1, 1, k, p, seed=sum(shape))
-    assert paths == {"tcgen05-tiled"}, paths
+    # narrow layers whose rows group into G pixels (G * K <= 256, G * C <= 256, G | M) run pixel-grouped
+    grouped = any(g * k <= 256 and g * c <= 256 and (g * c) % 16 == 0 and (n * h * w) % g == 0 for g in (2, 4, 8, 16))
+    assert paths == {"tcgen05-tiled-grouped" if grouped else "tcgen05-tiled"}, paths
 
 
 @pytest.mark.parametrize("shape,groups,expect", [
@@ -172,7 +174,8 @@ def test_conv_s8_tcgen05_pointwise(cuda_lib, shape):
     ((3, 7, 7, 960, 3, 3, 960, 1, 1, 1), 960, "cuda-core-depthwise|cuda-core-depthwise-tma"),  # 7x7 stage
     ((1, 11, 13, 16, 3, 3, 16, 2, 1, 2), 16, "cuda-core-depthwise"),    # dilation 2: one pixel/thread
     ((2, 23, 23, 3, 7, 7, 64, 3, 2, 1), 1, "cuda-core-generic"),      # stem C = 3
-    ((1, 12, 12, 24, 1, 1, 40, 0, 1, 1), 1, "cuda-core-generic"),     # C % 32 != 0
+    ((1, 11, 13, 24, 1, 1, 40, 0, 1, 1), 1, "cuda-core-generic"),     # C % 16 != 0, odd M: no pixel grouping
+    ((1, 12, 12, 24, 1, 1, 40, 0, 1, 1), 1, "tcgen05-tiled-grouped"),  # C % 16 != 0: 4-pixel rows of 96 B
     ((2, 9, 9, 32, 3, 3, 64, 1, 1, 1), 2, "cuda-core-generic"),       # grouped
     ((1, 6, 6, 48, 3, 3, 64, 1, 1, 1), 1, "cuda-core-generic"),       # tiny tensor (36 output rows)
     ((2, 14, 14, 256, 3, 3, 256, 1, 1, 1), 1, "tcgen05-packed"),      # < 128 KiB: packed, not im2col

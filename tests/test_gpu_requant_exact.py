@@ -72,7 +72,9 @@ def _case(n, h, w, c, r, k, pad, stride, bias_hi, special=None, res_scale=None, 
 @pytest.mark.parametrize("c,k", [(64, 256), (64, 64), (128, 96), (32, 48), (16, 256), (64, 192), (128, 144),
                                  (256, 400)])
 def test_pointwise_short_reduction(cuda_lib, c, k):
-    assert _case(4, 28, 28, c, 1, k, 0, 1, 2**15, seed=c + k) == "tcgen05-tiled"
+    # narrow layers (G * K <= 256, G * C <= 256) run pixel-grouped, the others on plain tiles
+    grouped = any(g * k <= 256 and g * c <= 256 for g in (2, 4, 8, 16))
+    assert _case(4, 28, 28, c, 1, k, 0, 1, 2**15, seed=c + k) == ("tcgen05-tiled-grouped" if grouped else "tcgen05-tiled")
 
 
 def test_im2col_short_reduction(cuda_lib):
@@ -110,3 +112,30 @@ def test_bmm_short_reduction(cuda_lib):
         torch.cuda.synchronize()
         np.testing.assert_array_equal(y.cpu().numpy(), oracle.requant_s8(acc, bias, scale, zp, lo, hi),
                                       err_msg=name)
+
+
+@pytest.mark.parametrize("n,hw,c,k,expect", [
+    (4, 28, 32, 16, "tcgen05-tiled-grouped"),   # G = 8: rows of 256 channels, 128 outputs
+    (3, 30, 16, 96, "tcgen05-tiled-grouped"),   # G = 2 (MobileNetV2 g2b1.expand shape)
+    (2, 28, 64, 64, "tcgen05-tiled-grouped"),   # G = 4
+    (1, 7, 32, 16, "tcgen05-tiled"),            # M = 49: no G divides it
+])
+def test_pixel_grouped_pointwise(cuda_lib, n, hw, c, k, expect):
+    """1x1 convs of narrow layers as GEMMs over G-pixel rows with block-diagonal weights: every
+    epilogue form, int32 / fp32 outputs and the fused residual add against the oracle."""
+    b2q = _b2q()
+    assert _case(n, hw, hw, c, 1, k, 0, 1, 2**15, seed=c * k + n) == expect
+    _case(n, hw, hw, c, 1, k, 0, 1, 2**15, res_scale=0.5, seed=c * k + n + 1)
+    x = rng_s8(9, (n, hw, hw, c), -128, 127)
+    wt = rng_s8(10, (k, 1, 1, c), -128, 127)
+    bias = np.random.default_rng(11).integers(-2**20, 2**20, size=k).astype(np.int32)
+    scale = _scales(k, 12)
+    acc = oracle.conv_s8(oracle.conv_args(n, hw, hw, c, 1, 1, k, 0, 0), x, wt, threads=4)
+    d = lambda t: torch.from_numpy(t).cuda()
+    p = b2q.Conv2DParams(0, 0, 1, 1, 1, 1, 1)
+    y32 = b2q.conv2d_s8(d(x), d(wt), d(bias), None, p, b2q.Epilogue.int32())
+    yf = b2q.conv2d_s8(d(x), d(wt), d(bias), d(scale), p, b2q.Epilogue.fp32())
+    torch.cuda.synchronize()
+    assert b2q.last_path() == expect
+    np.testing.assert_array_equal(y32.cpu().numpy(), oracle.bias_add_i32(acc, bias))
+    np.testing.assert_allclose(yf.cpu().numpy(), oracle.dequant_f32(acc, bias, scale), rtol=1e-5, atol=0)

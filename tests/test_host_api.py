@@ -161,7 +161,8 @@ def test_conv_plan_dispatch_tables():
     """The host-side dispatch decision (b200q_conv2d_s8_plan, the same function the GPU dispatch
     uses) for the BASELINE workloads: network stems on space-to-depth row tiles, stride-1 3x3
     convs with C <= 128 on row tiles, other 3x3 convs on im2col, 1x1 convs tiled (config 4's long
-    reduction on 2-SM tiles), depthwise on CUDA cores, C = 24 expands packed."""
+    reduction on 2-SM tiles; narrow ones pixel-grouped: ResNet-50 s1b1.conv1, MobileNetV2
+    g1b1.project / g2b1.expand / g2b1.project), depthwise on CUDA cores, C = 24 expands packed."""
     from collections import Counter
 
     import my_own_cnn_b200 as b2q
@@ -171,8 +172,10 @@ def test_conv_plan_dispatch_tables():
     assert b2q.conv2d_s8_plan(1, 56, 56, 64, 3, 3, 64, P(), E.int8()) == "tcgen05-rowtile"   # config 1 / smoke
     assert b2q.conv2d_s8_plan(512, 14, 14, 1024, 1, 1, 2048, P(0, 0), E.int8()) == "tcgen05-tiled"
     assert b2q.conv2d_s8_plan(512, 14, 14, 2048, 1, 1, 512, P(0, 0), E.int8()) == "tcgen05-tiled-2sm"
-    want = {"resnet50": {"tcgen05-s2d": 1, "tcgen05-tiled": 33, "tcgen05-rowtile": 6, "tcgen05-im2col": 13},
-            "mobilenetv2": {"tcgen05-s2d": 1, "cuda-core-depthwise-tma": 17, "tcgen05-tiled": 32, "tcgen05-packed": 2}}
+    want = {"resnet50": {"tcgen05-s2d": 1, "tcgen05-tiled": 32, "tcgen05-tiled-grouped": 1, "tcgen05-rowtile": 6,
+                         "tcgen05-im2col": 13},
+            "mobilenetv2": {"tcgen05-s2d": 1, "cuda-core-depthwise-tma": 17, "tcgen05-tiled": 29,
+                            "tcgen05-tiled-grouped": 3, "tcgen05-packed": 2}}
     for net, batch in (("resnet50", 256), ("mobilenetv2", 512)):
         got = Counter(b2q.conv2d_s8_plan(batch, sp.h, sp.w, sp.c, sp.r, sp.r, sp.k, sp.params(), sp.epilogue())
                       for sp in nets.NETS[net]())
