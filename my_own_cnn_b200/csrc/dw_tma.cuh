@@ -123,6 +123,11 @@ __global__ void __launch_bounds__(kDwThreads, 2) dw_tma_s8_kernel(const __grid_c
   const int warp = tid >> 5;
   const uint32_t ring_u32 = smem_u32(ring);
   const uint32_t full0 = smem_u32(bars), empty0 = full0 + 64;
+  // A contiguous run of tiles per CTA (slab outermost): the CTA reloads its filter slab only at
+  // the run's slab boundaries instead of every few tiles of a grid-strided walk.
+  const int per_cta = (p.total + static_cast<int>(gridDim.x) - 1) / static_cast<int>(gridDim.x);
+  const int t_begin = min(p.total, static_cast<int>(blockIdx.x) * per_cta);
+  const int t_end = min(p.total, t_begin + per_cta);
   if (tid == 0) {
     for (int i = 0; i < p.stages; ++i) {
       mbar_init(full0 + 8 * i, 1);
@@ -136,7 +141,7 @@ __global__ void __launch_bounds__(kDwThreads, 2) dw_tma_s8_kernel(const __grid_c
     if ((tid & 31) == 0) {
       tma_prefetch_desc(&tmx);
       int it = 0;
-      for (int t = blockIdx.x; t < p.total; t += gridDim.x, ++it) {
+      for (int t = t_begin; t < t_end; ++t, ++it) {
         const int slot = it % p.stages;
         if (it >= p.stages &&
             !mbar_wait_bounded(empty0 + 8 * slot, static_cast<uint32_t>(((it / p.stages) - 1) & 1), p.wait_limit,
@@ -162,7 +167,7 @@ __global__ void __launch_bounds__(kDwThreads, 2) dw_tma_s8_kernel(const __grid_c
   int32_t bias[8];
   float scl[8];
   int it = 0;
-  for (int t = blockIdx.x; t < p.total; t += gridDim.x, ++it) {
+  for (int t = t_begin; t < t_end; ++t, ++it) {
     const int slot = it % p.stages;
     const DwTile d = dw_tile(p, g.n, t);
     if (active && d.slab != cur_slab) {
