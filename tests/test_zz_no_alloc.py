@@ -80,14 +80,16 @@ def test_noalloc_conv_rejects_requests_beyond_its_scratch(cuda_lib):
 
 
 def test_noalloc_conv_leaves_device_memory_unchanged(cuda_lib):
-    """After a first call (which looks up the array's address), further calls on a new stream take
-    no device memory: the free-memory figure of the device does not move."""
+    """After a first call (which looks up the array's address), further calls on another stream take
+    no device memory: the free-memory figure of the device does not move.  The stream is created
+    before the first figure is read: in a fresh process torch's first stream creation sets up its
+    stream pool, which takes device memory of its own."""
     cs = _case(17, (2, 96, 96, 3, 3, 3, 32), (1, 1, 2, 2, 1, 1, 1), (_lib.OUT_S8, 0, 0, 127), torch.int8)
     args = (cs["x"], cs["w"], cs["bias"], cs["scale"], cs["y_new"], cs["shape"], cs["params"], cs["epi"])
+    side = torch.cuda.Stream()
     assert _call("b200q_conv2d_s8_packed_noalloc", *args) == 0, _lib.lib().b200q_last_error()
     torch.cuda.synchronize()
     free0, _ = torch.cuda.mem_get_info()
-    side = torch.cuda.Stream()
     with torch.cuda.stream(side):
         for _ in range(3):
             assert _call("b200q_conv2d_s8_packed_noalloc", *args) == 0, _lib.lib().b200q_last_error()
