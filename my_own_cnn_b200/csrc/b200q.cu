@@ -454,7 +454,11 @@ int launch_tc(const DeviceState& st, const CUtensorMap& ma, const CUtensorMap& m
   a.acc_cols = a.BN * a.rt_G;
   a.nacc = g_nacc_max < 512 / a.acc_cols ? g_nacc_max : 512 / a.acc_cols;
   if (a.nacc < 2) return fail(B200Q_ERR_UNSUPPORTED, "accumulator does not fit tensor memory twice");
-  a.tmem_cols = static_cast<uint32_t>(a.nacc * a.acc_cols);
+  // tcgen05.alloc takes a power of two of at least 32 columns (row groups of 3, 5, 6 or 7 give
+  // buffers of 192, 320, ... columns): allocate the next power of two, at most the 512 columns.
+  uint32_t cols = 32;
+  while (cols < static_cast<uint32_t>(a.nacc * a.acc_cols)) cols <<= 1;
+  a.tmem_cols = cols;
   const uint32_t sgn = a.ab_unsigned ? 0u : 1u;       // kind::i8 operand type: 0 = u8, 1 = s8
   const uint32_t dfmt = a.tf32 ? 1u : 2u;               // D = f32 (kind::tf32) or s32 (kind::i8)
   const uint32_t abfmt = a.tf32 ? 2u : sgn;             // kind::tf32 operand format: 2 = TF32

@@ -266,6 +266,8 @@ def test_conv_s8_tcgen05_s2d_stem(cuda_lib, shape):
     (2, 28, 28, 128, 3, 3, 128, 1, 1, 1),  # ResNet stage-2 3x3: 144 KiB of resident weights, 2 stages
     (2, 7, 5, 64, 3, 3, 40, 1, 1, 1),      # N = 40 (scalar tail), tiny image
     (1, 6, 6, 64, 3, 3, 64, 1, 1, 1),      # 36 output pixels: one tile, 6 rows
+    (20, 56, 56, 64, 3, 3, 64, 1, 1, 1),   # 3 row groups per tile (4 would leave SMs idle): 384 -> 512 TMEM columns
+    (12, 56, 56, 64, 3, 3, 64, 1, 1, 1),   # 2 row groups per tile
 ])
 def test_conv_s8_tcgen05_rowtile(cuda_lib, shape):
     """3x3 stride-1 convs on row tiles (one window load per tile for all nine taps)."""
