@@ -792,7 +792,28 @@ def run_bmm(args, rank: int, world: int, local_rank: int) -> dict | None:
     torch.cuda.synchronize()
     t32 = sum(e[0].elapsed_time(e[1]) for e in ev) / args.steps
     t8 = sum(e[1].elapsed_time(e[2]) for e in ev) / args.steps
-    t32, t8 = max_over_ranks([t32, t8], device=dev)
+    # The reference's own entry (bmm_matmul_i32 on int32 operands holding the same int8 values):
+    # the tensor-core route (int8 copies + tcgen05 GEMM), and one call forced onto the CUDA-core kernel.
+    A32, B32 = A.to(torch.int32), B.to(torch.int32)
+    del flush
+    def time_i32(reps):
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(reps + 1)]
+        torch.cuda.synchronize()
+        evs[0].record(stream)
+        for i in range(reps):
+            b2q.bmm_matmul_i32(A32, B32, C32, batch, M, M, M, 0, 0)
+            evs[i + 1].record(stream)
+        torch.cuda.synchronize()
+        return sum(evs[i].elapsed_time(evs[i + 1]) for i in range(reps)) / reps
+    time_i32(3)
+    ti32 = time_i32(args.steps)
+    b2q.set_path_policy(1)
+    try:
+        ti32_cc = time_i32(1)
+    finally:
+        b2q.set_path_policy(0)
+    del A32, B32
+    t32, t8, ti32, ti32_cc = max_over_ranks([t32, t8, ti32, ti32_cc], device=dev)
     if rank != 0:
         return None
     peaks = load_peaks()
@@ -806,13 +827,19 @@ def run_bmm(args, rank: int, world: int, local_rank: int) -> dict | None:
             "int32_out": {"ms": round(t32, 4), "tops": round(ops / t32 / 1e9, 1),
                           "hbm_gbs": round(bytes32 / t32 / 1e6, 1), "hbm_frac": round(bytes32 / t32 / 1e6 / peaks["hbm_gbs"], 4)},
             "int8_out": {"ms": round(t8, 4), "tops": round(ops / t8 / 1e9, 1),
-                         "frac_of_int8_peak": round(ops / t8 / 1e9 / (2 * peaks["bf16_tflops"]), 4)}}
+                         "frac_of_int8_peak": round(ops / t8 / 1e9 / (2 * peaks["bf16_tflops"]), 4)},
+            "dropin_bmm_matmul_i32": {"ms": round(ti32, 4), "tops": round(ops / ti32 / 1e9, 1),
+                                      "cuda_core_ms": round(ti32_cc, 4),
+                                      "note": "int32 operands (int8 values): int8 copies + tcgen05 GEMM; "
+                                              "cuda_core_ms = the same call forced onto the CUDA-core kernel, "
+                                              "no L2 flush (inputs 512 MiB > L2)"}}
 
 
 # ------------------------------------------------------------- per-config sub-records (N = 1)
 
 SUB_KEEP = ("value", "unit", "ms_per_step", "steps", "warmup", "tops_per_gpu", "frac_of_int8_peak", "by_path",
             "roofline", "roofline_depthwise", "slowest_layers", "cpu_baseline", "int32_out", "int8_out", "config",
+            "dropin_bmm_matmul_i32",
             "gpu_launches", "clocks")
 
 

@@ -109,7 +109,12 @@ int b200q_block_fprop_nhwc_qi32(int qtype, const float* d_x, const float* d_w, i
                                 const void* d_in_qp, const void* d_f_qp, void* stream);
 
 /* Row-major int32 batched GEMM, C_b = op(A_b) @ op(B_b), int32 wrap-around.
- * Layouts as bmm.h:9-29.  Replaces bmm_matmul_i32 (bmm.h:69-74). */
+ * Layouts as bmm.h:9-29.  Replaces bmm_matmul_i32 (bmm.h:69-74).
+ * With 16-byte aligned A, B and C, K < 2^17 and the contiguous dimensions of A and B multiples of
+ * 16, the operands are first copied to int8 in the stream's workspace and multiplied by the
+ * tcgen05 GEMM (path 16); if any value lies outside [-128, 127] a device flag makes the CUDA-core
+ * kernel recompute C from the int32 operands, so every input gives the same C without a host
+ * round trip.  Other shapes run the CUDA-core kernel directly (path 6). */
 int b200q_bmm_matmul_i32(const int32_t* A, const int32_t* B, int32_t* C, int batch, int M, int N,
                          int K, int trans_a, int trans_b, void* stream);
 
@@ -235,7 +240,8 @@ int b200q_device_error(void);
  * zero-point correction terms), 12 CUDA-core depthwise with TMA-staged tiles, 13 tcgen05 fp32
  * (3 x TF32 split GEMM), 14 CUDA-core fp32 (groups of a few channels, e.g. depthwise), 15 tcgen05
  * pixel-grouped 1x1 GEMM (G pixels per row against block-diagonal weights built in the stream's
- * workspace, for layers with G * K <= 256 and G * C <= 256). */
+ * workspace, for layers with G * K <= 256 and G * C <= 256), 16 tcgen05 int32 bmm (operands copied
+ * to int8, CUDA-core recompute only when a value does not fit). */
 int b200q_last_path(void);
 
 /* 0 = automatic dispatch (default); 1 = force the CUDA-core kernels (cross-checks). */

@@ -38,6 +38,7 @@ PATH_NAMES = {
     13: "tcgen05-f32",
     14: "cuda-core-f32",
     15: "tcgen05-tiled-grouped",
+    16: "tcgen05-bmm-i32",
 }
 
 

@@ -1029,6 +1029,43 @@ int b200q_block_fprop_nhwc_qi32(int qtype, const float* d_x, const float* d_w, i
   return qi32_common(qtype, d_x, d_w, d_y, g, d_in_qp, d_f_qp, stream);
 }
 
+// tcgen05 batched GEMM over int8 operands in bmm.h's layouts (shapes checked by the caller:
+// 16-byte aligned pointers, the contiguous dimensions of A and B multiples of 16).
+static int bmm_s8_tcgen05(DeviceState& st, const int8_t* A, const int8_t* B, void* C, int batch, int M, int N,
+                          int K, bool ta, bool tb, const Epilogue& e, cudaStream_t cs) {
+  int rc = 0;
+  TcArgs a{};
+  a.mode = 0;
+  a.BK = 128;
+  a.a_major = ta ? 1 : 0;
+  a.b_major = tb ? 0 : 1;  // B stored [K][N] (no transpose) is N-contiguous = MN-major
+  a.BN = pick_bn(N, a.b_major);
+  a.M = M;
+  a.N = N;
+  a.batch = batch;
+  a.b_batched = 1;
+  a.num_kb = (K + a.BK - 1) / a.BK;
+  a.epi = e;
+  a.out = C;
+  a.ldc = N;
+  a.batch_stride = static_cast<long long>(M) * N;
+  a.vec_ok = N % 16 == 0;
+  CUtensorMap ma, mb;
+  if (!ta)
+    rc = encode_tiled_3d(&ma, A, (uint64_t)K, (uint64_t)M, (uint64_t)batch, a.BK, kTcBM, 128);
+  else
+    rc = encode_tiled_3d(&ma, A, (uint64_t)M, (uint64_t)K, (uint64_t)batch, kTcBM, a.BK, 128);
+  if (rc) return rc;
+  a.pair = want_pair(st.sms, a);
+  if (tb)
+    rc = encode_tiled_3d(&mb, B, (uint64_t)K, (uint64_t)N, (uint64_t)batch, a.BK, a.pair ? a.BN / 2 : a.BN, 128);
+  else
+    rc = encode_tiled_3d(&mb, B, (uint64_t)N, (uint64_t)K, (uint64_t)batch, 128, a.BK, 128);
+  if (rc) return rc;
+  g_last_path = a.pair ? 8 : 2;
+  return launch_tc(st, ma, mb, a, cs);
+}
+
 int b200q_bmm_matmul_i32(const int32_t* A, const int32_t* B, int32_t* C, int batch, int M, int N, int K,
                          int trans_a, int trans_b, void* stream) {
   if (batch < 0 || M < 0 || N < 0 || K < 0) return fail(B200Q_ERR_INVALID_ARG, "negative bmm dimension");
@@ -1038,17 +1075,46 @@ int b200q_bmm_matmul_i32(const int32_t* A, const int32_t* B, int32_t* C, int bat
   int rc = device_state(&st);
   if (rc) return rc;
   Epilogue e{kOutS32, 0, 0, 0, nullptr, nullptr};
+  cudaStream_t cs = as_stream(stream);
+  // Tensor-core route: operands whose values all fit int8 give the same C from an int8 GEMM with
+  // int32 accumulation (|a*b| <= 2^14, so sums of K <= 2^17 - 1 products cannot wrap).  The operands
+  // are copied to int8 on the device; a value outside [-128, 127] sets a flag, and the CUDA-core
+  // kernel below then runs (every block reads the flag and returns at once while it is clear).
+  const int* run_if = nullptr;
+  const bool ta = trans_a != 0, tb = trans_b != 0;
+  if (g_policy.load() == 0 && K > 0 && K < (1 << 17) && aligned16(A) && aligned16(B) && aligned16(C) &&
+      (ta ? M % 16 == 0 : K % 16 == 0) && (tb ? K % 16 == 0 : N % 16 == 0)) {
+    const size_t na = static_cast<size_t>(batch) * M * K, nb_ = static_cast<size_t>(batch) * K * N;
+    const size_t a_bytes = round256(na), b_bytes = round256(nb_);
+    void* ws = nullptr;
+    rc = get_workspace(a_bytes + b_bytes + 256, cs, &ws);
+    if (rc) return rc;
+    int8_t* a8 = static_cast<int8_t*>(ws);
+    int8_t* b8 = a8 + a_bytes;
+    int* flag = reinterpret_cast<int*>(b8 + b_bytes);
+    cudaError_t ce = cudaMemsetAsync(flag, 0, sizeof(int), cs);
+    if (ce != cudaSuccess) return cuda_fail(ce, "cudaMemsetAsync(bmm_i32 flag)");
+    i32_to_s8_kernel<<<grid_for(na / 4, 256, st->sms), 256, 0, cs>>>(A, a8, na, flag);
+    rc = check_launch("i32_to_s8_kernel launch");
+    if (rc) return rc;
+    i32_to_s8_kernel<<<grid_for(nb_ / 4, 256, st->sms), 256, 0, cs>>>(B, b8, nb_, flag);
+    rc = check_launch("i32_to_s8_kernel launch");
+    if (rc) return rc;
+    rc = bmm_s8_tcgen05(*st, a8, b8, C, batch, M, N, K, ta, tb, e, cs);
+    if (rc) return rc;
+    run_if = flag;
+  }
   for (int b0 = 0; b0 < batch; b0 += 65535) {
     const int nb = batch - b0 < 65535 ? batch - b0 : 65535;
     dim3 grid((N + 63) / 64, (M + 63) / 64, nb);
     if (grid.y > 65535) return fail(B200Q_ERR_UNSUPPORTED, "M too large for the CUDA-core bmm");
     bmm_simt_kernel<int32_t><<<grid, 256, 0, as_stream(stream)>>>(
         A + static_cast<size_t>(b0) * M * K, B + static_cast<size_t>(b0) * K * N,
-        C + static_cast<size_t>(b0) * M * N, M, N, K, trans_a != 0, trans_b != 0, e);
+        C + static_cast<size_t>(b0) * M * N, M, N, K, trans_a != 0, trans_b != 0, e, run_if);
     rc = check_launch("bmm_simt_kernel<int32> launch");
     if (rc) return rc;
   }
-  g_last_path = 6;
+  g_last_path = run_if ? 16 : 6;
   return B200Q_OK;
 }
 
@@ -1654,38 +1720,7 @@ int b200q_bmm_s8(const int8_t* A, const int8_t* B, const int32_t* d_bias, const 
                         (!d_col_scale || aligned16(d_col_scale));
   const bool tc_ok = g_policy.load() == 0 && K > 0 && vec_ptrs && (ta ? M % 16 == 0 : K % 16 == 0) &&
                      (tb ? K % 16 == 0 : N % 16 == 0);
-  if (tc_ok) {
-    TcArgs a{};
-    a.mode = 0;
-    a.BK = 128;
-    a.a_major = ta ? 1 : 0;
-    a.b_major = tb ? 0 : 1;  // B stored [K][N] (no transpose) is N-contiguous = MN-major
-    a.BN = pick_bn(N, a.b_major);
-    a.M = M;
-    a.N = N;
-    a.batch = batch;
-    a.b_batched = 1;
-    a.num_kb = (K + a.BK - 1) / a.BK;
-    a.epi = e;
-    a.out = C;
-    a.ldc = N;
-    a.batch_stride = static_cast<long long>(M) * N;
-    a.vec_ok = N % 16 == 0;
-    CUtensorMap ma, mb;
-    if (!ta)
-      rc = encode_tiled_3d(&ma, A, (uint64_t)K, (uint64_t)M, (uint64_t)batch, a.BK, kTcBM, 128);
-    else
-      rc = encode_tiled_3d(&ma, A, (uint64_t)M, (uint64_t)K, (uint64_t)batch, kTcBM, a.BK, 128);
-    if (rc) return rc;
-    a.pair = want_pair(st->sms, a);
-    if (tb)
-      rc = encode_tiled_3d(&mb, B, (uint64_t)K, (uint64_t)N, (uint64_t)batch, a.BK, a.pair ? a.BN / 2 : a.BN, 128);
-    else
-      rc = encode_tiled_3d(&mb, B, (uint64_t)N, (uint64_t)K, (uint64_t)batch, 128, a.BK, 128);
-    if (rc) return rc;
-    g_last_path = a.pair ? 8 : 2;
-    return launch_tc(*st, ma, mb, a, cs);
-  }
+  if (tc_ok) return bmm_s8_tcgen05(*st, A, B, C, batch, M, N, K, ta, tb, e, cs);
   for (int b0 = 0; b0 < batch; b0 += 65535) {
     const int nb = batch - b0 < 65535 ? batch - b0 : 65535;
     dim3 grid((N + 63) / 64, (M + 63) / 64, nb);
@@ -1693,7 +1728,7 @@ int b200q_bmm_s8(const int8_t* A, const int8_t* B, const int32_t* d_bias, const 
     const size_t osz = out_elem_size(e.out_kind);
     bmm_simt_kernel<int8_t><<<grid, 256, 0, cs>>>(A + static_cast<size_t>(b0) * M * K, B + static_cast<size_t>(b0) * K * N,
                                                   static_cast<char*>(C) + static_cast<size_t>(b0) * M * N * osz, M, N, K,
-                                                  ta, tb, e);
+                                                  ta, tb, e, nullptr);
     rc = check_launch("bmm_simt_kernel<int8> launch");
     if (rc) return rc;
   }

@@ -202,7 +202,10 @@ __global__ void __launch_bounds__(256) dw_conv_s8_kernel(const int8_t* __restric
 template <typename T>
 __global__ void __launch_bounds__(256) bmm_simt_kernel(const T* __restrict__ A, const T* __restrict__ B,
                                                        void* __restrict__ C, int M, int N, int K,
-                                                       int ta, int tb, Epilogue e) {
+                                                       int ta, int tb, Epilogue e, const int* run_if) {
+  // run_if: when given, the block does nothing unless *run_if != 0 (the int32 bmm's fallback
+  // after its tensor-core route found an operand outside the 8-bit range).
+  if (run_if && *reinterpret_cast<const volatile int*>(run_if) == 0) return;
   __shared__ int32_t As[16][64 + 1];
   __shared__ int32_t Bs[16][64 + 1];
   const int b = blockIdx.z;
@@ -252,6 +255,24 @@ __global__ void __launch_bounds__(256) bmm_simt_kernel(const T* __restrict__ A, 
                        static_cast<int32_t>(acc[i][j]), n);
     }
   }
+}
+
+// int32 operand -> int8 copy for the tensor-core route of the int32 bmm (bmm.cu:298-322 computes on
+// arbitrary int32 values).  n is a multiple of 4, src 16-byte and dst 4-byte aligned.  A value outside
+// [-128, 127] sets *flag; the CUDA-core kernel then recomputes C from the int32 operands, so the
+// result stays the reference's for every input without a host round trip.
+__global__ void __launch_bounds__(256) i32_to_s8_kernel(const int32_t* __restrict__ src, int8_t* __restrict__ dst,
+                                                        size_t n, int* __restrict__ flag) {
+  const size_t n4 = n / 4;
+  const size_t step = static_cast<size_t>(gridDim.x) * blockDim.x;
+  bool bad = false;
+  for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n4; i += step) {
+    const int4 v = __ldg(reinterpret_cast<const int4*>(src) + i);
+    bad |= static_cast<uint32_t>(v.x + 128) > 255u || static_cast<uint32_t>(v.y + 128) > 255u ||
+           static_cast<uint32_t>(v.z + 128) > 255u || static_cast<uint32_t>(v.w + 128) > 255u;
+    reinterpret_cast<uint32_t*>(dst)[i] = __byte_perm(__byte_perm(v.x, v.y, 0x0040), __byte_perm(v.z, v.w, 0x0040), 0x5410);
+  }
+  if (__syncthreads_or(bad) && threadIdx.x == 0) *reinterpret_cast<volatile int*>(flag) = 1;
 }
 
 // ------------------------------------------------------------------ generators

@@ -87,6 +87,47 @@ def test_bmm_matmul_i32_exact_wraparound(cuda_lib):
                 np.testing.assert_array_equal(C.cpu().numpy(), oracle.bmm_i32(A, B, batch, M, N, K, ta, tb))
 
 
+@pytest.mark.parametrize("ta,tb", [(0, 0), (0, 1), (1, 0), (1, 1)])
+def test_bmm_matmul_i32_tensor_core_route(cuda_lib, ta, tb):
+    """int32 operands whose values fit int8 take the tcgen05 route (path 16), bit-exact; one value
+    outside [-128, 127] anywhere in A or B makes the device-side fallback recompute C exactly."""
+    b2q = _b2q()
+    rng = np.random.default_rng(23 + 2 * ta + tb)
+    for batch, M, N, K in [(1, 16, 16, 16), (3, 144, 80, 96), (2, 208, 272, 400), (2, 256, 512, 1040)]:
+        A = rng.integers(-128, 128, size=(batch, K, M) if ta else (batch, M, K)).astype(np.int32)
+        B = rng.integers(-128, 128, size=(batch, N, K) if tb else (batch, K, N)).astype(np.int32)
+        want = oracle.bmm_i32(A, B, batch, M, N, K, ta, tb)
+        for poison in (None, "A", "B"):
+            Ap, Bp = A.copy(), B.copy()
+            if poison == "A":
+                Ap.reshape(-1)[Ap.size // 2 + 1] = 300
+            if poison == "B":
+                Bp.reshape(-1)[-1] = -129
+            exp = want if poison is None else oracle.bmm_i32(Ap, Bp, batch, M, N, K, ta, tb)
+            C = torch.full((batch, M, N), 7, dtype=torch.int32, device="cuda")
+            b2q.bmm_matmul_i32(torch.from_numpy(Ap).cuda(), torch.from_numpy(Bp).cuda(), C, batch, M, N, K, ta, tb)
+            torch.cuda.synchronize()
+            assert b2q.last_path() == "tcgen05-bmm-i32"
+            np.testing.assert_array_equal(C.cpu().numpy(), exp)
+
+
+def test_bmm_matmul_i32_config2_full_size_sampled(cuda_lib):
+    """BASELINE config 2 (64 x 1024^3) through the int32 drop-in with int8-range values: the tensor-core
+    route, two sampled batches checked against the oracle."""
+    b2q = _b2q()
+    batch, M, N, K = 64, 1024, 1024, 1024
+    g = torch.Generator(device="cuda").manual_seed(5)
+    A = torch.randint(-127, 128, (batch, M, K), dtype=torch.int32, device="cuda", generator=g)
+    B = torch.randint(-127, 128, (batch, K, N), dtype=torch.int32, device="cuda", generator=g)
+    C = torch.empty((batch, M, N), dtype=torch.int32, device="cuda")
+    b2q.bmm_matmul_i32(A, B, C, batch, M, N, K, 0, 0)
+    torch.cuda.synchronize()
+    assert b2q.last_path() == "tcgen05-bmm-i32"
+    for b in (0, 41):
+        want = oracle.bmm_i32(A[b:b + 1].cpu().numpy(), B[b:b + 1].cpu().numpy(), 1, M, N, K, 0, 0)
+        np.testing.assert_array_equal(C[b:b + 1].cpu().numpy(), want)
+
+
 # ------------------------------------------------------------------ int8 conv
 
 def _conv_case(n, h, w, c, r, s, k, p, seed, epi_kind="all", groups=1):
