@@ -1094,23 +1094,20 @@ int b200q_bmm_matmul_i32(const int32_t* A, const int32_t* B, int32_t* C, int bat
     int* flag = reinterpret_cast<int*>(b8 + b_bytes);
     cudaError_t ce = cudaMemsetAsync(flag, 0, sizeof(int), cs);
     if (ce != cudaSuccess) return cuda_fail(ce, "cudaMemsetAsync(bmm_i32 flag)");
-    i32_to_s8_kernel<<<grid_for(na / 4, 256, st->sms), 256, 0, cs>>>(A, a8, na, flag);
-    rc = check_launch("i32_to_s8_kernel launch");
-    if (rc) return rc;
-    i32_to_s8_kernel<<<grid_for(nb_ / 4, 256, st->sms), 256, 0, cs>>>(B, b8, nb_, flag);
+    i32_to_s8_kernel<<<grid_for((na + nb_) / 16, 256, st->sms), 256, 0, cs>>>(A, a8, na, B, b8, nb_, flag);
     rc = check_launch("i32_to_s8_kernel launch");
     if (rc) return rc;
     rc = bmm_s8_tcgen05(*st, a8, b8, C, batch, M, N, K, ta, tb, e, cs);
     if (rc) return rc;
     run_if = flag;
   }
-  for (int b0 = 0; b0 < batch; b0 += 65535) {
-    const int nb = batch - b0 < 65535 ? batch - b0 : 65535;
-    dim3 grid((N + 63) / 64, (M + 63) / 64, nb);
-    if (grid.y > 65535) return fail(B200Q_ERR_UNSUPPORTED, "M too large for the CUDA-core bmm");
-    bmm_simt_kernel<int32_t><<<grid, 256, 0, as_stream(stream)>>>(
-        A + static_cast<size_t>(b0) * M * K, B + static_cast<size_t>(b0) * K * N,
-        C + static_cast<size_t>(b0) * M * N, M, N, K, trans_a != 0, trans_b != 0, e, run_if);
+  {
+    // one block per 64 x 64 tile; the gated fallback after the tensor-core route launches one block
+    // per SM instead (the blocks walk the tiles), so it costs one small launch while its flag is clear
+    const long long tiles = static_cast<long long>((N + 63) / 64) * ((M + 63) / 64) * batch;
+    const long long cap = run_if ? st->sms : 0x7fffffffll;
+    const int blocks = static_cast<int>(tiles < cap ? tiles : cap);
+    bmm_simt_kernel<int32_t><<<blocks, 256, 0, cs>>>(A, B, C, M, N, K, ta, tb, e, run_if, batch);
     rc = check_launch("bmm_simt_kernel<int32> launch");
     if (rc) return rc;
   }
@@ -1721,14 +1718,10 @@ int b200q_bmm_s8(const int8_t* A, const int8_t* B, const int32_t* d_bias, const 
   const bool tc_ok = g_policy.load() == 0 && K > 0 && vec_ptrs && (ta ? M % 16 == 0 : K % 16 == 0) &&
                      (tb ? K % 16 == 0 : N % 16 == 0);
   if (tc_ok) return bmm_s8_tcgen05(*st, A, B, C, batch, M, N, K, ta, tb, e, cs);
-  for (int b0 = 0; b0 < batch; b0 += 65535) {
-    const int nb = batch - b0 < 65535 ? batch - b0 : 65535;
-    dim3 grid((N + 63) / 64, (M + 63) / 64, nb);
-    if (grid.y > 65535) return fail(B200Q_ERR_UNSUPPORTED, "M too large for the CUDA-core bmm");
-    const size_t osz = out_elem_size(e.out_kind);
-    bmm_simt_kernel<int8_t><<<grid, 256, 0, cs>>>(A + static_cast<size_t>(b0) * M * K, B + static_cast<size_t>(b0) * K * N,
-                                                  static_cast<char*>(C) + static_cast<size_t>(b0) * M * N * osz, M, N, K,
-                                                  ta, tb, e, nullptr);
+  {
+    const long long tiles = static_cast<long long>((N + 63) / 64) * ((M + 63) / 64) * batch;
+    const int blocks = static_cast<int>(tiles < 0x7fffffffll ? tiles : 0x7fffffffll);
+    bmm_simt_kernel<int8_t><<<blocks, 256, 0, cs>>>(A, B, C, M, N, K, ta, tb, e, nullptr, batch);
     rc = check_launch("bmm_simt_kernel<int8> launch");
     if (rc) return rc;
   }

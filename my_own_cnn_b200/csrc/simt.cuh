@@ -202,14 +202,19 @@ __global__ void __launch_bounds__(256) dw_conv_s8_kernel(const int8_t* __restric
 template <typename T>
 __global__ void __launch_bounds__(256) bmm_simt_kernel(const T* __restrict__ A, const T* __restrict__ B,
                                                        void* __restrict__ C, int M, int N, int K,
-                                                       int ta, int tb, Epilogue e, const int* run_if) {
+                                                       int ta, int tb, Epilogue e, const int* run_if, int batch) {
   // run_if: when given, the block does nothing unless *run_if != 0 (the int32 bmm's fallback
   // after its tensor-core route found an operand outside the 8-bit range).
+  // The block walks 64 x 64 output tiles t = blockIdx.x, blockIdx.x + gridDim.x, ... of all batches.
   if (run_if && *reinterpret_cast<const volatile int*>(run_if) == 0) return;
   __shared__ int32_t As[16][64 + 1];
   __shared__ int32_t Bs[16][64 + 1];
-  const int b = blockIdx.z;
-  const int m0 = blockIdx.y * 64, n0 = blockIdx.x * 64;
+  const int tn = (N + 63) / 64, tm = (M + 63) / 64;
+  const long long tiles = static_cast<long long>(tn) * tm * batch;
+  for (long long t = blockIdx.x; t < tiles; t += gridDim.x) {
+  const int b = static_cast<int>(t / (static_cast<long long>(tn) * tm));
+  const int rem = static_cast<int>(t - static_cast<long long>(b) * tn * tm);
+  const int m0 = (rem / tn) * 64, n0 = (rem % tn) * 64;
   const T* Ab = A + static_cast<size_t>(b) * M * K;
   const T* Bb = B + static_cast<size_t>(b) * K * N;
   const int tid = threadIdx.x;
@@ -255,22 +260,36 @@ __global__ void __launch_bounds__(256) bmm_simt_kernel(const T* __restrict__ A, 
                        static_cast<int32_t>(acc[i][j]), n);
     }
   }
+  }
 }
 
-// int32 operand -> int8 copy for the tensor-core route of the int32 bmm (bmm.cu:298-322 computes on
-// arbitrary int32 values).  n is a multiple of 4, src 16-byte and dst 4-byte aligned.  A value outside
+// int32 operands -> int8 copies for the tensor-core route of the int32 bmm (bmm.cu:298-322 computes
+// on arbitrary int32 values).  One launch converts both operands: unit u < na / 16 is 16 values of
+// A, the rest are 16 values of B (na, nb multiples of 16; sources 16-byte, destinations 16-byte
+// aligned); each thread has its four 16-byte loads in flight before it stores.  A value outside
 // [-128, 127] sets *flag; the CUDA-core kernel then recomputes C from the int32 operands, so the
 // result stays the reference's for every input without a host round trip.
-__global__ void __launch_bounds__(256) i32_to_s8_kernel(const int32_t* __restrict__ src, int8_t* __restrict__ dst,
-                                                        size_t n, int* __restrict__ flag) {
-  const size_t n4 = n / 4;
+__device__ __forceinline__ bool s8_out_of_range(const int4& v) {
+  return static_cast<uint32_t>(v.x + 128) > 255u || static_cast<uint32_t>(v.y + 128) > 255u ||
+         static_cast<uint32_t>(v.z + 128) > 255u || static_cast<uint32_t>(v.w + 128) > 255u;
+}
+__device__ __forceinline__ uint32_t pack4_s8_trunc(const int4& v) {
+  return __byte_perm(__byte_perm(v.x, v.y, 0x0040), __byte_perm(v.z, v.w, 0x0040), 0x5410);
+}
+__global__ void __launch_bounds__(256) i32_to_s8_kernel(const int32_t* __restrict__ a, int8_t* __restrict__ a8,
+                                                        size_t na, const int32_t* __restrict__ b,
+                                                        int8_t* __restrict__ b8, size_t nb, int* __restrict__ flag) {
+  const size_t ua = na / 16, units = ua + nb / 16;
   const size_t step = static_cast<size_t>(gridDim.x) * blockDim.x;
   bool bad = false;
-  for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n4; i += step) {
-    const int4 v = __ldg(reinterpret_cast<const int4*>(src) + i);
-    bad |= static_cast<uint32_t>(v.x + 128) > 255u || static_cast<uint32_t>(v.y + 128) > 255u ||
-           static_cast<uint32_t>(v.z + 128) > 255u || static_cast<uint32_t>(v.w + 128) > 255u;
-    reinterpret_cast<uint32_t*>(dst)[i] = __byte_perm(__byte_perm(v.x, v.y, 0x0040), __byte_perm(v.z, v.w, 0x0040), 0x5410);
+  for (size_t u = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; u < units; u += step) {
+    const bool in_a = u < ua;
+    const size_t k = in_a ? u : u - ua;
+    const int4* src = reinterpret_cast<const int4*>(in_a ? a : b) + 4 * k;
+    const int4 v0 = __ldg(src), v1 = __ldg(src + 1), v2 = __ldg(src + 2), v3 = __ldg(src + 3);
+    bad |= s8_out_of_range(v0) || s8_out_of_range(v1) || s8_out_of_range(v2) || s8_out_of_range(v3);
+    reinterpret_cast<uint4*>(in_a ? a8 : b8)[k] =
+        make_uint4(pack4_s8_trunc(v0), pack4_s8_trunc(v1), pack4_s8_trunc(v2), pack4_s8_trunc(v3));
   }
   if (__syncthreads_or(bad) && threadIdx.x == 0) *reinterpret_cast<volatile int*>(flag) = 1;
 }
