@@ -16,6 +16,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <atomic>
 #include <cstdarg>
 #include <cstdio>
@@ -590,12 +591,14 @@ int qi32_tensor_core(const DeviceState& st, int qtype, const float* x, const flo
   const size_t total = static_cast<size_t>(g.n) * g.ho * g.wo * g.k;
   const bool v4 = g.kg % 4 == 0 && aligned16(y) && aligned16(cbuf);
   const int fused = in_place ? 1 : 0;
+  // fused: the launch only serves the out-of-range fallback, so one block per SM (grid-stride loop)
+  // keeps it cheap while the flag is clear
+  const int gv4 = fused ? std::min(grid_for(total / 4, 256, st.sms), st.sms) : grid_for(total / 4, 256, st.sms);
+  const int gv1 = fused ? std::min(grid_for(total, 256, st.sms), st.sms) : grid_for(total, 256, st.sms);
   if (v4)
-    qi32_fixup_kernel<4><<<grid_for(total / 4, 256, st.sms), 256, 0, stream>>>(cbuf, y, rowterm, colsum, g, q, iq, fq,
-                                                                              flag, x, w, fused);
+    qi32_fixup_kernel<4><<<gv4, 256, 0, stream>>>(cbuf, y, rowterm, colsum, g, q, iq, fq, flag, x, w, fused);
   else
-    qi32_fixup_kernel<1><<<grid_for(total, 256, st.sms), 256, 0, stream>>>(cbuf, y, rowterm, colsum, g, q, iq, fq,
-                                                                          flag, x, w, fused);
+    qi32_fixup_kernel<1><<<gv1, 256, 0, stream>>>(cbuf, y, rowterm, colsum, g, q, iq, fq, flag, x, w, fused);
   rc = check_launch("qi32_fixup_kernel launch");
   if (rc) return rc;
   g_last_path = 11;

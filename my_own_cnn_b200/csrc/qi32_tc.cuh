@@ -94,6 +94,9 @@ __global__ void __launch_bounds__(256) qi32_pack_rows_kernel(const float* __rest
   const int words = q.kp >> 2;
   const int sc = g.s * g.cg;
   bool bad = false;
+  // Channels of a group in multiples of 4 with a 16-byte aligned x: every word is 4 consecutive
+  // channels of one tap, read with one 16-byte load (consecutive lanes, consecutive 16 bytes).
+  const bool v4 = (g.cg & 3) == 0 && (g.c & 3) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0;
   for (long long row = warp0; row < rows; row += nwarps) {
     const int gp = static_cast<int>(row / q.mb);
     int rem = static_cast<int>(row - static_cast<long long>(gp) * q.mb);
@@ -109,6 +112,44 @@ __global__ void __launch_bounds__(256) qi32_pack_rows_kernel(const float* __rest
     const float* xn = x + static_cast<size_t>(n) * g.h * g.w * g.c + static_cast<size_t>(grp) * g.cg;
     uint32_t* arow = a + static_cast<size_t>(row) * words;
     uint32_t sum = 0;
+    if (v4) {
+      // The lane's tap position (rr, ss, ci) of word wd advances by 128 taps per step (32 lanes x 4
+      // channels); divisions run only when ci leaves the group's channels (rarely for wide groups).
+      int j0 = lane * 4;
+      int rr = j0 / sc;
+      int ss = (j0 - rr * sc) / g.cg;
+      int ci = j0 - rr * sc - ss * g.cg;
+      for (int wd = lane; wd < words; wd += 32, j0 += 128) {
+        uint32_t word = 0;
+        if (j0 < q.T) {
+          const int hi = h0 + rr * g.dil_h, wi = w0 + ss * g.dil_w;
+          int v0 = zx, v1 = zx, v2 = zx, v3 = zx;
+          if (hi >= 0 && hi < g.h && wi >= 0 && wi < g.w) {
+            const float4 f = __ldg(reinterpret_cast<const float4*>(xn + (static_cast<size_t>(hi) * g.w + wi) * g.c + ci));
+            bool o0, o1, o2, o3;
+            v0 = qi32_code(f.x, q.qp_signed, o0);
+            v1 = qi32_code(f.y, q.qp_signed, o1);
+            v2 = qi32_code(f.z, q.qp_signed, o2);
+            v3 = qi32_code(f.w, q.qp_signed, o3);
+            bad |= !(o0 && o1 && o2 && o3);
+          }
+          sum += static_cast<uint32_t>(v0) + static_cast<uint32_t>(v1) + static_cast<uint32_t>(v2) +
+                 static_cast<uint32_t>(v3);
+          word = __byte_perm(__byte_perm(v0, v1, 0x0040), __byte_perm(v2, v3, 0x0040), 0x5410);
+          ci += 128;
+          if (ci >= g.cg) {
+            const int carry = ci / g.cg;
+            ci -= carry * g.cg;
+            ss += carry;
+            if (ss >= g.s) {
+              rr += ss / g.s;
+              ss %= g.s;
+            }
+          }
+        }
+        arow[wd] = word;
+      }
+    } else
     for (int wd = lane; wd < words; wd += 32) {
       uint32_t word = 0;
       const int j0 = wd * 4;
