@@ -97,11 +97,17 @@ __global__ void __launch_bounds__(256) qi32_pack_rows_kernel(const float* __rest
   // Channels of a group in multiples of 4 with a 16-byte aligned x: every word is 4 consecutive
   // channels of one tap, read with one 16-byte load (consecutive lanes, consecutive 16 bytes).
   const bool v4 = (g.cg & 3) == 0 && (g.c & 3) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0;
+  const bool one_gp = q.gcount == 1;  // a regular conv: row = pixel, no block / group decode
   for (long long row = warp0; row < rows; row += nwarps) {
-    const int gp = static_cast<int>(row / q.mb);
-    int rem = static_cast<int>(row - static_cast<long long>(gp) * q.mb);
-    const int grp = gp % g.groups, blk = gp / g.groups;
-    const int byi = blk / g.bx, bxi = blk - byi * g.bx;
+    int gp = 0, rem;
+    if (one_gp) {
+      rem = static_cast<int>(row);
+    } else {
+      gp = static_cast<int>(row / q.mb);
+      rem = static_cast<int>(row - static_cast<long long>(gp) * q.mb);
+    }
+    const int grp = one_gp ? 0 : gp % g.groups, blk = one_gp ? 0 : gp / g.groups;
+    const int byi = one_gp ? 0 : blk / g.bx, bxi = blk - byi * g.bx;
     const int owb = rem % g.bwo;
     rem /= g.bwo;
     const int ohb = rem % g.bho;
@@ -119,6 +125,7 @@ __global__ void __launch_bounds__(256) qi32_pack_rows_kernel(const float* __rest
       int rr = j0 / sc;
       int ss = (j0 - rr * sc) / g.cg;
       int ci = j0 - rr * sc - ss * g.cg;
+#pragma unroll 4
       for (int wd = lane; wd < words; wd += 32, j0 += 128) {
         uint32_t word = 0;
         if (j0 < q.T) {
