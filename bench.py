@@ -534,6 +534,21 @@ def _reference_gpu_f32(ref, dev, stream, flush) -> list[dict]:
                 "ours_ms": round(t_me, 4), "ours_path": path, "speedup": round(t_ref / t_me, 1),
                 "ours_tflops": round(2.0 * batch * M ** 3 / t_me / 1e9, 1),
                 "max_rel_diff": float((C_me - C_ref).abs().max() / C_ref.abs().max())})
+    # int32 bmm (bmm_matmul_i32) on config 2's shape with int8-range values held in int32
+    if hasattr(ref, "refgpu_bmm_i32"):
+        ref.refgpu_bmm_i32.argtypes = [ctypes.c_void_p] * 3 + [ctypes.c_int] * 6
+        del A, B, C_ref, C_me
+        Ai = torch.randint(-127, 128, (batch, M, M), dtype=torch.int32, device=dev, generator=g)
+        Bi = torch.randint(-127, 128, (batch, M, M), dtype=torch.int32, device=dev, generator=g)
+        Ci_ref, Ci_me = torch.empty_like(Ai), torch.empty_like(Ai)
+        run_ref = lambda: ref.refgpu_bmm_i32(Ai.data_ptr(), Bi.data_ptr(), Ci_ref.data_ptr(), batch, M, M, M, 0, 0)
+        run_me = lambda: b2q.bmm_matmul_i32(Ai, Bi, Ci_me, batch, M, M, M, 0, 0)
+        run_ref(); run_me(); path = b2q.last_path()
+        t_ref = statistics.median(_timed_ms(run_ref, 3, flush, stream))
+        t_me = statistics.median(_timed_ms(run_me, 10, flush, stream))
+        out.append({"impl": "reference-gpu", "case": "int32 bmm_matmul_i32 batch 64 x 1024^3 NN (int8-range values)",
+                    "reference_gpu_ms": round(t_ref, 4), "ours_ms": round(t_me, 4), "ours_path": path,
+                    "speedup": round(t_ref / t_me, 1), "identical": bool(torch.equal(Ci_me, Ci_ref))})
     return out
 
 

@@ -11,8 +11,9 @@
 //               CUDA-core direct kernel otherwise.
 //   bmm_s8    : tcgen05 tiled GEMM (K-major or MN-major operands) when the TMA stride rules hold,
 //               CUDA-core tiled GEMM otherwise.
-//   *_qi32 drop-ins and bmm_matmul_i32: exact CUDA-core kernels (float codes / arbitrary int32
-//               values do not fit the int8 tensor-core datapath).
+//   *_qi32 drop-ins and bmm_matmul_i32: float codes / int32 values copied to 8-bit operands for the
+//               tcgen05 GEMM, with a device flag that reruns exact CUDA-core kernels when a value
+//               does not fit the 8-bit operand type.
 #include <cuda.h>
 #include <cuda_runtime.h>
 

@@ -52,3 +52,11 @@ extern "C" int refgpu_bmm_f32(const float* A, const float* B, float* C, int batc
   bmm_matmul(A, B, C, batch, M, N, K, ta, tb);
   return 0;
 }
+
+// The reference's int32 batched GEMM (bmm.cu:298-322), for timing beside this library's
+// bmm_matmul_i32 drop-in.
+extern "C" int refgpu_bmm_i32(const int32_t* A, const int32_t* B, int32_t* C, int batch, int M, int N, int K, int ta,
+                              int tb) {
+  bmm_matmul_i32(A, B, C, batch, M, N, K, ta, tb);
+  return 0;
+}
