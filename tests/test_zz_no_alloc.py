@@ -5,7 +5,8 @@ owns and budgets all device memory, or latency-critical code where a cudaMalloc 
 Its scratch is one fixed device array of the library, shared by all calls on a device.  This file
 is collected last on purpose, so a run that stops at the first failure has run everything else.
 The test calls the entry point twice in a row through the C ABI (the second call reuses the
-scratch left by the first) and compares both results with b200q_conv2d_s8, bit for bit.
+scratch left by the first) and compares both results with b200q_conv2d_s8 and with the CPU oracle,
+bit for bit.
 """
 from __future__ import annotations
 
@@ -45,6 +46,21 @@ def _case(seed, shape, params, epi, out_dtype):
     return dict(x=x, w=w, bias=bias, scale=scale, shape=shape, params=params, epi=epi, y_new=mk(), y_ref=mk())
 
 
+def _oracle_out(cs):
+    """The CPU oracle's result for a case (int32: accumulators + bias, int8: the requantized codes)."""
+    from oracle import oracle
+
+    n, h, wd, c, r, s, k = cs["shape"]
+    pad_h, pad_w, sh, sw, dh, dw, groups = cs["params"]
+    a = oracle.conv_args(n, h, wd, c, r, s, k, pad_h, pad_w, sh, sw, dh, dw, groups)
+    acc = oracle.conv_s8(a, cs["x"].cpu().numpy(), cs["w"].cpu().numpy(), threads=4)
+    bias = cs["bias"].cpu().numpy()
+    kind, zp, lo, hi = cs["epi"]
+    if kind == _lib.OUT_S32:
+        return (acc.astype(np.int64) + bias).astype(np.uint32).astype(np.int32).reshape(cs["y_new"].shape)
+    return oracle.requant_s8(acc, bias, cs["scale"].cpu().numpy(), zp, lo, hi).reshape(cs["y_new"].shape)
+
+
 def test_noalloc_conv_matches_existing_entry_on_two_calls_in_a_row(cuda_lib):
     cases = [
         # MobileNetV2 stem (3x3/2, C = 3 -> 32), int8 requant with ReLU
@@ -66,6 +82,7 @@ def test_noalloc_conv_matches_existing_entry_on_two_calls_in_a_row(cuda_lib):
     assert _lib.lib().b200q_device_error() == 0
     for cs in cases:
         assert torch.equal(cs["y_new"], cs["y_ref"])
+        assert np.array_equal(cs["y_new"].cpu().numpy(), _oracle_out(cs))
 
 
 def test_noalloc_conv_rejects_requests_beyond_its_scratch(cuda_lib):
