@@ -551,14 +551,23 @@ int qi32_tensor_core(const DeviceState& st, int qtype, const float* x, const flo
   if (ce != cudaSuccess) return cuda_fail(ce, "cudaMemsetAsync(qi32 flag)");
   const uint8_t* iq = static_cast<const uint8_t*>(in_qp);
   const uint8_t* fq = static_cast<const uint8_t*>(f_qp);
-  qi32_pack_rows_kernel<<<grid_for(static_cast<size_t>(arows) * 32, 256, st.sms), 256, 0, stream>>>(
-      x, a_buf, rowterm, rowzx, g, q, iq, fq, flag);
-  rc = check_launch("qi32_pack_rows_kernel launch");
-  if (rc) return rc;
-  qi32_pack_filter_kernel<<<grid_for(static_cast<size_t>(brows) * 32, 256, st.sms), 256, 0, stream>>>(
-      w, b_buf, colsum, g, q, flag);
-  rc = check_launch("qi32_pack_filter_kernel launch");
-  if (rc) return rc;
+  const int row_blocks = grid_for(static_cast<size_t>(arows) * 32, 256, st.sms);
+  const int filter_blocks = grid_for(static_cast<size_t>(brows) * 32, 256, st.sms);
+  if (a_bytes + b_bytes <= (8u << 20)) {
+    // small problems are launch-latency-bound: both packs in one launch (config 1: 34.8 -> 28.7 us
+    // per call); large ones measured 3-7 % faster as two launches
+    qi32_pack_kernel<<<row_blocks + filter_blocks, 256, 0, stream>>>(x, a_buf, rowterm, rowzx, w, b_buf, colsum, g,
+                                                                     q, iq, fq, flag, row_blocks);
+    rc = check_launch("qi32_pack_kernel launch");
+    if (rc) return rc;
+  } else {
+    qi32_pack_rows_kernel<<<row_blocks, 256, 0, stream>>>(x, a_buf, rowterm, rowzx, g, q, iq, fq, flag);
+    rc = check_launch("qi32_pack_rows_kernel launch");
+    if (rc) return rc;
+    qi32_pack_filter_kernel<<<filter_blocks, 256, 0, stream>>>(w, b_buf, colsum, g, q, flag);
+    rc = check_launch("qi32_pack_filter_kernel launch");
+    if (rc) return rc;
+  }
   TcArgs a{};
   a.mode = 0;
   a.BK = q.kp % 128 == 0 ? 128 : (q.kp % 64 == 0 ? 64 : 32);

@@ -12,10 +12,12 @@
 // All four terms are taken modulo 2^32, so the result equals the reference's wrapping int32
 // accumulation bit for bit.
 //
-//   qi32_pack_rows_kernel    float NHWC codes -> 8-bit im2col rows [G'][Mb][Kp] (G' = blocks x
+//   qi32_pack_kernel         one launch running both packs below (small problems; large ones
+//                            launch qi32_pack_rows_kernel, then qi32_pack_filter_kernel):
+//   qi32_pack_rows           float NHWC codes -> 8-bit im2col rows [G'][Mb][Kp] (G' = blocks x
 //                            groups, Mb = pixels of one output block, Kp = T rounded up to 32) and
 //                            the row term  T*zx*zw - zw*sum a_j  (int32, one per row);
-//   qi32_pack_filter_kernel  float weights -> 8-bit rows [G'][Kg][Kp] and their sums  sum b_j;
+//   qi32_pack_filter         float weights -> 8-bit rows [G'][Kg][Kp] and their sums  sum b_j;
 //   tc_gemm_s8_kernel        C[G'][Mb][Kg] = A . B^T  (int32 out, unsigned or signed operands);
 //   qi32_fixup_kernel        y[n,ho,wo,k] = C + rowterm - zx * colsum, scattered to NHWC.
 // A regular conv (one block, one group) takes the correction in the GEMM's int32 epilogue instead
@@ -81,15 +83,16 @@ struct Qi32Pack {
 
 // One warp per packed row (gp, mb): gp = block * groups + group, mb = (image, row, column) inside
 // the output block.  Each lane builds 4-byte words of the row; the row sum is reduced over the warp.
-__global__ void __launch_bounds__(256) qi32_pack_rows_kernel(const float* __restrict__ x, uint32_t* __restrict__ a,
+__device__ __forceinline__ void qi32_pack_rows(const float* __restrict__ x, uint32_t* __restrict__ a,
                                                              int32_t* __restrict__ rowterm, int32_t* __restrict__ rowzx,
                                                              ConvGeom g, Qi32Pack q,
                                                              const uint8_t* __restrict__ in_qp,
-                                                             const uint8_t* __restrict__ f_qp, int* __restrict__ flag) {
+                                                             const uint8_t* __restrict__ f_qp, int* __restrict__ flag,
+                                               int bid, int nblk) {
   const int lane = threadIdx.x & 31;
   const long long rows = static_cast<long long>(q.gcount) * q.mb;
-  const long long warp0 = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
-  const long long nwarps = (static_cast<long long>(gridDim.x) * blockDim.x) >> 5;
+  const long long warp0 = (static_cast<long long>(bid) * blockDim.x + threadIdx.x) >> 5;
+  const long long nwarps = (static_cast<long long>(nblk) * blockDim.x) >> 5;
   const int zf = load_zp(f_qp, 0, q.qp_stride, q.qp_signed);
   const int words = q.kp >> 2;
   const int sc = g.s * g.cg;
@@ -204,13 +207,13 @@ __global__ void __launch_bounds__(256) qi32_pack_rows_kernel(const float* __rest
 
 // One warp per packed filter row (gp, kg): the weights of output channel grp * Kg + kg for output
 // block (byi, bxi), from [K][By][Bx][R][S][Cg] float codes.  colsum = sum of the row's codes.
-__global__ void __launch_bounds__(256) qi32_pack_filter_kernel(const float* __restrict__ w, uint32_t* __restrict__ b,
+__device__ __forceinline__ void qi32_pack_filter(const float* __restrict__ w, uint32_t* __restrict__ b,
                                                                int32_t* __restrict__ colsum, ConvGeom g, Qi32Pack q,
-                                                               int* __restrict__ flag) {
+                                                               int* __restrict__ flag, int bid, int nblk) {
   const int lane = threadIdx.x & 31;
   const long long rows = static_cast<long long>(q.gcount) * g.kg;
-  const long long warp0 = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
-  const long long nwarps = (static_cast<long long>(gridDim.x) * blockDim.x) >> 5;
+  const long long warp0 = (static_cast<long long>(bid) * blockDim.x + threadIdx.x) >> 5;
+  const long long nwarps = (static_cast<long long>(nblk) * blockDim.x) >> 5;
   const int words = q.kp >> 2;
   bool bad = false;
   for (long long row = warp0; row < rows; row += nwarps) {
@@ -242,6 +245,37 @@ __global__ void __launch_bounds__(256) qi32_pack_filter_kernel(const float* __re
     if (lane == 0) colsum[row] = static_cast<int32_t>(sum);
   }
   if (__any_sync(0xFFFFFFFFu, bad) && lane == 0) atomicOr(flag, 1);
+}
+
+// Both packs in one launch (a call of the drop-in is short and launch-latency-bound at small sizes):
+// blocks [0, row_blocks) pack the activation rows, the rest (if any) pack the filter rows.
+__global__ void __launch_bounds__(256) qi32_pack_kernel(const float* __restrict__ x, uint32_t* __restrict__ a,
+                                                        int32_t* __restrict__ rowterm, int32_t* __restrict__ rowzx,
+                                                        const float* __restrict__ w, uint32_t* __restrict__ b,
+                                                        int32_t* __restrict__ colsum, ConvGeom g, Qi32Pack q,
+                                                        const uint8_t* __restrict__ in_qp,
+                                                        const uint8_t* __restrict__ f_qp, int* __restrict__ flag,
+                                                        int row_blocks) {
+  const int bid = static_cast<int>(blockIdx.x);
+  if (bid < row_blocks)
+    qi32_pack_rows(x, a, rowterm, rowzx, g, q, in_qp, f_qp, flag, bid, row_blocks);
+  else
+    qi32_pack_filter(w, b, colsum, g, q, flag, bid - row_blocks, static_cast<int>(gridDim.x) - row_blocks);
+}
+
+// The two packs as separate kernels (large problems; each kernel keeps its own register budget).
+__global__ void __launch_bounds__(256) qi32_pack_rows_kernel(const float* __restrict__ x, uint32_t* __restrict__ a,
+                                                             int32_t* __restrict__ rowterm, int32_t* __restrict__ rowzx,
+                                                             ConvGeom g, Qi32Pack q, const uint8_t* __restrict__ in_qp,
+                                                             const uint8_t* __restrict__ f_qp, int* __restrict__ flag) {
+  qi32_pack_rows(x, a, rowterm, rowzx, g, q, in_qp, f_qp, flag, static_cast<int>(blockIdx.x),
+                 static_cast<int>(gridDim.x));
+}
+
+__global__ void __launch_bounds__(256) qi32_pack_filter_kernel(const float* __restrict__ w, uint32_t* __restrict__ b,
+                                                               int32_t* __restrict__ colsum, ConvGeom g, Qi32Pack q,
+                                                               int* __restrict__ flag) {
+  qi32_pack_filter(w, b, colsum, g, q, flag, static_cast<int>(blockIdx.x), static_cast<int>(gridDim.x));
 }
 
 // Output element (n, ho, wo, k) from the GEMM accumulators C[gp][mb][kg] (src may alias y when
