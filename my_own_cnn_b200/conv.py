@@ -23,6 +23,11 @@ from . import _lib
 from .quant import DataType, QPARAMS_TYPES, is_supported_quantized_input
 
 
+# ctypes structs handed to the C ABI by pointer (it only reads them), one per distinct value.
+_C_PARAMS: dict = {}
+_C_EPILOGUES: dict = {}
+
+
 @dataclass
 class Conv2DParams:
     pad_h: int = 1
@@ -34,8 +39,11 @@ class Conv2DParams:
     groups: int = 1
 
     def to_c(self) -> _lib.CConvParams:
-        return _lib.CConvParams(self.pad_h, self.pad_w, self.stride_h, self.stride_w,
-                                self.dilation_h, self.dilation_w, self.groups)
+        key = (self.pad_h, self.pad_w, self.stride_h, self.stride_w, self.dilation_h, self.dilation_w, self.groups)
+        c = _C_PARAMS.get(key)
+        if c is None:  # read-only use by the C ABI, so one struct per distinct value is shared
+            c = _C_PARAMS[key] = _lib.CConvParams(*key)
+        return c
 
 
 @dataclass
@@ -115,8 +123,14 @@ def _ptr(t) -> int:
     raise TypeError(f"expected a CUDA tensor or device address, got {type(t).__name__}")
 
 
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def _stream(stream) -> int:
+    """cudaStream_t of `stream`, or of the current device's current stream when None."""
     if stream is None:
+        if _raw_stream is not None:  # the same handle as current_stream().cuda_stream, without the object
+            return _raw_stream(torch.cuda.current_device())
         return torch.cuda.current_stream().cuda_stream
     return stream.cuda_stream if hasattr(stream, "cuda_stream") else int(stream)
 
@@ -182,7 +196,11 @@ class Epilogue:
         return Epilogue(_lib.OUT_S8, zp_out, lo, hi)
 
     def to_c(self) -> _lib.CEpilogue:
-        return _lib.CEpilogue(self.out_kind, self.zp_out, self.clamp_lo, self.clamp_hi)
+        key = (self.out_kind, self.zp_out, self.clamp_lo, self.clamp_hi)
+        c = _C_EPILOGUES.get(key)
+        if c is None:
+            c = _C_EPILOGUES[key] = _lib.CEpilogue(*key)
+        return c
 
     @property
     def torch_dtype(self):
