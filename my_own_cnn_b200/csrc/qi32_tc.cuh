@@ -100,6 +100,7 @@ __device__ __forceinline__ void qi32_pack_rows(const float* __restrict__ x, uint
   // Channels of a group in multiples of 4 with a 16-byte aligned x: every word is 4 consecutive
   // channels of one tap, read with one 16-byte load (consecutive lanes, consecutive 16 bytes).
   const bool v4 = (g.cg & 3) == 0 && (g.c & 3) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0;
+  const uint32_t bias8 = q.qp_signed ? 128u : 0u;
   const bool one_gp = q.gcount == 1;  // a regular conv: row = pixel, no block / group decode
   for (long long row = warp0; row < rows; row += nwarps) {
     int gp = 0, rem;
@@ -136,12 +137,15 @@ __device__ __forceinline__ void qi32_pack_rows(const float* __restrict__ x, uint
           int v0 = zx, v1 = zx, v2 = zx, v3 = zx;
           if (hi >= 0 && hi < g.h && wi >= 0 && wi < g.w) {
             const float4 f = __ldg(reinterpret_cast<const float4*>(xn + (static_cast<size_t>(hi) * g.w + wi) * g.c + ci));
-            bool o0, o1, o2, o3;
-            v0 = qi32_code(f.x, q.qp_signed, o0);
-            v1 = qi32_code(f.y, q.qp_signed, o1);
-            v2 = qi32_code(f.z, q.qp_signed, o2);
-            v3 = qi32_code(f.w, q.qp_signed, o3);
-            bad |= !(o0 && o1 && o2 && o3);
+            v0 = __float2int_rz(f.x);
+            v1 = __float2int_rz(f.y);
+            v2 = __float2int_rz(f.z);
+            v3 = __float2int_rz(f.w);
+            // a code fits iff (v + bias8) lies in [0, 255] (bias8 = 128 signed, 0 unsigned): one test
+            // of the OR of the four shifted codes against the bits above the low byte
+            const uint32_t any = (static_cast<uint32_t>(v0) + bias8) | (static_cast<uint32_t>(v1) + bias8) |
+                                 (static_cast<uint32_t>(v2) + bias8) | (static_cast<uint32_t>(v3) + bias8);
+            bad |= (any & ~0xFFu) != 0;
           }
           sum += static_cast<uint32_t>(v0) + static_cast<uint32_t>(v1) + static_cast<uint32_t>(v2) +
                  static_cast<uint32_t>(v3);
