@@ -42,6 +42,15 @@ thread_local char g_errmsg[512] = "";
 thread_local int g_last_path = 0;
 std::atomic<int> g_policy{0};
 std::atomic<long long> g_tc_launches{0};
+std::atomic<uint32_t> g_flag_gen{0};
+
+// Nonzero number of a drop-in call; its out-of-range flag is set to this value, so a flag left by an
+// earlier call (or uninitialised workspace) does not need a clearing copy before each call.
+int next_flag_gen() {
+  uint32_t v;
+  do v = (g_flag_gen.fetch_add(1) + 1) & 0x7fffffffu; while (v == 0);
+  return static_cast<int>(v);
+}
 
 __device__ int g_dev_err;
 
@@ -547,8 +556,7 @@ int qi32_tensor_core(const DeviceState& st, int qtype, const float* x, const flo
   int32_t* colsum = reinterpret_cast<int32_t*>(base + a_bytes + b_bytes + rt_bytes);
   int32_t* cbuf = in_place ? y : reinterpret_cast<int32_t*>(base + a_bytes + b_bytes + rt_bytes + cs_bytes);
   int* flag = reinterpret_cast<int*>(base + a_bytes + b_bytes + rt_bytes + cs_bytes + c_bytes);
-  cudaError_t ce = cudaMemsetAsync(flag, 0, sizeof(int), stream);
-  if (ce != cudaSuccess) return cuda_fail(ce, "cudaMemsetAsync(qi32 flag)");
+  q.gen = next_flag_gen();  // the flag is not cleared: the kernels compare it with this call's number
   const uint8_t* iq = static_cast<const uint8_t*>(in_qp);
   const uint8_t* fq = static_cast<const uint8_t*>(f_qp);
   const int row_blocks = grid_for(static_cast<size_t>(arows) * 32, 256, st.sms);
@@ -1094,6 +1102,7 @@ int b200q_bmm_matmul_i32(const int32_t* A, const int32_t* B, int32_t* C, int bat
   // are copied to int8 on the device; a value outside [-128, 127] sets a flag, and the CUDA-core
   // kernel below then runs (every block reads the flag and returns at once while it is clear).
   const int* run_if = nullptr;
+  int run_gen = 0;
   const bool ta = trans_a != 0, tb = trans_b != 0;
   if (g_policy.load() == 0 && K > 0 && K < (1 << 17) && aligned16(A) && aligned16(B) && aligned16(C) &&
       (ta ? M % 16 == 0 : K % 16 == 0) && (tb ? K % 16 == 0 : N % 16 == 0)) {
@@ -1105,9 +1114,8 @@ int b200q_bmm_matmul_i32(const int32_t* A, const int32_t* B, int32_t* C, int bat
     int8_t* a8 = static_cast<int8_t*>(ws);
     int8_t* b8 = a8 + a_bytes;
     int* flag = reinterpret_cast<int*>(b8 + b_bytes);
-    cudaError_t ce = cudaMemsetAsync(flag, 0, sizeof(int), cs);
-    if (ce != cudaSuccess) return cuda_fail(ce, "cudaMemsetAsync(bmm_i32 flag)");
-    i32_to_s8_kernel<<<grid_for((na + nb_) / 16, 256, st->sms), 256, 0, cs>>>(A, a8, na, B, b8, nb_, flag);
+    run_gen = next_flag_gen();  // the flag is not cleared: the kernels compare it with this number
+    i32_to_s8_kernel<<<grid_for((na + nb_) / 16, 256, st->sms), 256, 0, cs>>>(A, a8, na, B, b8, nb_, flag, run_gen);
     rc = check_launch("i32_to_s8_kernel launch");
     if (rc) return rc;
     rc = bmm_s8_tcgen05(*st, a8, b8, C, batch, M, N, K, ta, tb, e, cs);
@@ -1120,7 +1128,7 @@ int b200q_bmm_matmul_i32(const int32_t* A, const int32_t* B, int32_t* C, int bat
     const long long tiles = static_cast<long long>((N + 63) / 64) * ((M + 63) / 64) * batch;
     const long long cap = run_if ? st->sms : 0x7fffffffll;
     const int blocks = static_cast<int>(tiles < cap ? tiles : cap);
-    bmm_simt_kernel<int32_t><<<blocks, 256, 0, cs>>>(A, B, C, M, N, K, ta, tb, e, run_if, batch);
+    bmm_simt_kernel<int32_t><<<blocks, 256, 0, cs>>>(A, B, C, M, N, K, ta, tb, e, run_if, run_gen, batch);
     rc = check_launch("bmm_simt_kernel<int32> launch");
     if (rc) return rc;
   }
@@ -1734,7 +1742,7 @@ int b200q_bmm_s8(const int8_t* A, const int8_t* B, const int32_t* d_bias, const 
   {
     const long long tiles = static_cast<long long>((N + 63) / 64) * ((M + 63) / 64) * batch;
     const int blocks = static_cast<int>(tiles < 0x7fffffffll ? tiles : 0x7fffffffll);
-    bmm_simt_kernel<int8_t><<<blocks, 256, 0, cs>>>(A, B, C, M, N, K, ta, tb, e, nullptr, batch);
+    bmm_simt_kernel<int8_t><<<blocks, 256, 0, cs>>>(A, B, C, M, N, K, ta, tb, e, nullptr, 0, batch);
     rc = check_launch("bmm_simt_kernel<int8> launch");
     if (rc) return rc;
   }

@@ -24,7 +24,9 @@
 // (Epilogue::rowterm / rowzx, the column sums as its bias) and writes y directly; the fixup kernel
 // then only runs the out-of-range fallback, returning at once when the flag is clear.
 // Codes whose truncated value does not fit the 8-bit operand type (U8 outside [0, 255], S5
-// outside [-128, 127]) set a device flag in the pack kernels; the fixup kernel then computes every
+// outside [-128, 127]) set a device flag in the pack kernels (to the call's generation number, so
+// the flag needs no clearing between calls: a stale or uninitialised value at worst runs the exact
+// fallback); the fixup kernel then computes every
 // output directly on CUDA cores (qi32_direct), so out-of-range inputs still give the reference's
 // result, without a host round trip.
 #pragma once
@@ -79,6 +81,7 @@ struct Qi32Pack {
   int mb;      // rows per block item: N * bho * bwo
   int gcount;  // G' = by * bx * groups
   int qp_stride, qp_signed;
+  int gen;     // this call's generation number (nonzero): the out-of-range flag holds it when set
 };
 
 // One warp per packed row (gp, mb): gp = block * groups + group, mb = (image, row, column) inside
@@ -206,7 +209,7 @@ __device__ __forceinline__ void qi32_pack_rows(const float* __restrict__ x, uint
       rowzx[row] = zx;
     }
   }
-  if (__any_sync(0xFFFFFFFFu, bad) && lane == 0) atomicOr(flag, 1);
+  if (__any_sync(0xFFFFFFFFu, bad) && lane == 0) *reinterpret_cast<volatile int*>(flag) = q.gen;
 }
 
 // One warp per packed filter row (gp, kg): the weights of output channel grp * Kg + kg for output
@@ -248,7 +251,7 @@ __device__ __forceinline__ void qi32_pack_filter(const float* __restrict__ w, ui
     for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xFFFFFFFFu, sum, o);
     if (lane == 0) colsum[row] = static_cast<int32_t>(sum);
   }
-  if (__any_sync(0xFFFFFFFFu, bad) && lane == 0) atomicOr(flag, 1);
+  if (__any_sync(0xFFFFFFFFu, bad) && lane == 0) *reinterpret_cast<volatile int*>(flag) = q.gen;
 }
 
 // Both packs in one launch (a call of the drop-in is short and launch-latency-bound at small sizes):
@@ -296,7 +299,7 @@ __global__ void __launch_bounds__(256) qi32_fixup_kernel(const int32_t* src, int
                                                          int fused) {
   const size_t total = static_cast<size_t>(g.n) * g.ho * g.wo * g.k;
   const size_t items = total / V;
-  const bool direct = *flag != 0;
+  const bool direct = *reinterpret_cast<const volatile int*>(flag) == q.gen;
   // fused: the GEMM epilogue already applied the correction; only the out-of-range fallback is left
   if (fused && !direct) return;
   const int zf = load_zp(f_qp, 0, q.qp_stride, q.qp_signed);

@@ -202,11 +202,12 @@ __global__ void __launch_bounds__(256) dw_conv_s8_kernel(const int8_t* __restric
 template <typename T>
 __global__ void __launch_bounds__(256) bmm_simt_kernel(const T* __restrict__ A, const T* __restrict__ B,
                                                        void* __restrict__ C, int M, int N, int K,
-                                                       int ta, int tb, Epilogue e, const int* run_if, int batch) {
-  // run_if: when given, the block does nothing unless *run_if != 0 (the int32 bmm's fallback
-  // after its tensor-core route found an operand outside the 8-bit range).
+                                                       int ta, int tb, Epilogue e, const int* run_if, int run_gen,
+                                                       int batch) {
+  // run_if: when given, the block does nothing unless *run_if == run_gen (the int32 bmm's fallback
+  // after its tensor-core route found an operand outside the 8-bit range in call run_gen).
   // The block walks 64 x 64 output tiles t = blockIdx.x, blockIdx.x + gridDim.x, ... of all batches.
-  if (run_if && *reinterpret_cast<const volatile int*>(run_if) == 0) return;
+  if (run_if && *reinterpret_cast<const volatile int*>(run_if) != run_gen) return;
   __shared__ int32_t As[16][64 + 1];
   __shared__ int32_t Bs[16][64 + 1];
   const int tn = (N + 63) / 64, tm = (M + 63) / 64;
@@ -267,7 +268,8 @@ __global__ void __launch_bounds__(256) bmm_simt_kernel(const T* __restrict__ A, 
 // on arbitrary int32 values).  One launch converts both operands: unit u < na / 16 is 16 values of
 // A, the rest are 16 values of B (na, nb multiples of 16; sources 16-byte, destinations 16-byte
 // aligned); each thread has its four 16-byte loads in flight before it stores.  A value outside
-// [-128, 127] sets *flag; the CUDA-core kernel then recomputes C from the int32 operands, so the
+// [-128, 127] sets *flag to the call's generation number gen; the CUDA-core kernel then recomputes C
+// from the int32 operands, so the
 // result stays the reference's for every input without a host round trip.
 __device__ __forceinline__ bool s8_out_of_range(const int4& v) {
   return static_cast<uint32_t>(v.x + 128) > 255u || static_cast<uint32_t>(v.y + 128) > 255u ||
@@ -278,7 +280,8 @@ __device__ __forceinline__ uint32_t pack4_s8_trunc(const int4& v) {
 }
 __global__ void __launch_bounds__(256) i32_to_s8_kernel(const int32_t* __restrict__ a, int8_t* __restrict__ a8,
                                                         size_t na, const int32_t* __restrict__ b,
-                                                        int8_t* __restrict__ b8, size_t nb, int* __restrict__ flag) {
+                                                        int8_t* __restrict__ b8, size_t nb, int* __restrict__ flag,
+                                                        int gen) {
   const size_t ua = na / 16, units = ua + nb / 16;
   const size_t step = static_cast<size_t>(gridDim.x) * blockDim.x;
   bool bad = false;
@@ -291,7 +294,7 @@ __global__ void __launch_bounds__(256) i32_to_s8_kernel(const int32_t* __restric
     reinterpret_cast<uint4*>(in_a ? a8 : b8)[k] =
         make_uint4(pack4_s8_trunc(v0), pack4_s8_trunc(v1), pack4_s8_trunc(v2), pack4_s8_trunc(v3));
   }
-  if (__syncthreads_or(bad) && threadIdx.x == 0) *reinterpret_cast<volatile int*>(flag) = 1;
+  if (__syncthreads_or(bad) && threadIdx.x == 0) *reinterpret_cast<volatile int*>(flag) = gen;
 }
 
 // ------------------------------------------------------------------ generators
