@@ -162,7 +162,8 @@ def test_codes_outside_8_bits_fall_back_on_device(cuda_lib, kind):
     y, path = _run(kind, x, wt, n, h, w, c, r, s, k, prm)
     assert path == "tcgen05-qi32"
     np.testing.assert_array_equal(y, _ref(kind, x, wt, n, h, w, c, r, s, k, prm))
-    # the next in-range call takes the tensor-core result again (the flag is cleared per call)
+    # the next in-range call takes the tensor-core result again: the flag still holds the earlier
+    # call's generation number, which this call's number does not match
     x[1, 4, 5, 3] = 7.0
     wt[17] = 5.0
     y, _ = _run(kind, x, wt, n, h, w, c, r, s, k, prm)
